@@ -1,0 +1,152 @@
+/*
+ * ufp8 — C ABI of the B200 (sm_100a) FP8 dense-contraction library.
+ *
+ * This is the drop-in boundary for the FP8 mode of macrogpt-jax's `Einsum` layer and the
+ * layers built on it.  The reference computes that path with XLA; each entry point below
+ * replaces one piece of it (file:line relative to the reference repository):
+ *
+ *   ufp8_amax / ufp8_quantize / ufp8_amax_quant
+ *       replace the forward/backward fp8 casts of `custom_astype`
+ *       (ueaj/utils/gradutils.py:15-54, `lax.convert_element_type` at :34,:41,:49),
+ *       composed with per-tensor current scaling: amax = max|x|, s = FMAX/amax
+ *       (amax == 0 -> s = 1), q = RNE(f32(x) * s) with ml_dtypes 0.5.4 cast semantics,
+ *       inv_scale = 1/s (both divisions IEEE round-to-nearest).
+ *   ufp8_gemm (UFP8_EPI_STORE)
+ *       replaces the contraction `jnp.einsum(self.einsum_expr, x, self.w.value)`
+ *       (ueaj/model/einsum.py:243) and the two dot_generals JAX derives for its
+ *       backward pass; fp32 accumulation, output multiplied by inv_scale_a * inv_scale_b.
+ *   ufp8_gemm (UFP8_EPI_SWIGLU)
+ *       replaces GMLP's fused gate/up Einsum "bnd,idh->ibnh" plus its gating
+ *       `up * swish(gate)` (ueaj/model/mlp.py:78-86, 102-107).
+ *   ufp8_gemm (UFP8_EPI_DSWIGLU)
+ *       replaces the backward of the down-projection input together with the gating's
+ *       backward (JAX autodiff of ueaj/model/mlp.py:102-114).
+ *
+ * Conventions.  All pointers are device pointers owned by the caller; nothing here
+ * allocates device memory.  Every call is stream-ordered and asynchronous; nothing
+ * synchronises the device except ufp8_device_status.  Shapes and alignment are checked
+ * on the host before any launch: a call returns UFP8_OK (0) or a negative UFP8_ERR_*
+ * code, and ufp8_last_error() (per host thread) describes the last failure.  Device code
+ * never traps: every pipeline wait is bounded, and a wait that runs out sets a bit in
+ * the library's device status word, which ufp8_device_status reads.
+ */
+#ifndef UFP8_H_
+#define UFP8_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
+
+#define UFP8_ABI_VERSION 1
+
+/* return codes */
+#define UFP8_OK 0
+#define UFP8_ERR_INVALID (-1)     /* bad shape, null pointer, bad enum */
+#define UFP8_ERR_ALIGN (-2)       /* pointer / leading dimension breaks a 16-byte rule */
+#define UFP8_ERR_UNSUPPORTED (-3) /* valid request this build does not implement */
+#define UFP8_ERR_CUDA (-4)        /* a CUDA runtime / driver call failed */
+#define UFP8_ERR_DEVICE (-5)      /* device older than sm_100 */
+
+/* bits of the device status word */
+#define UFP8_STATUS_WAIT_TIMEOUT 1
+
+/* fp8 formats (values match the MMA instruction-descriptor encoding) */
+#define UFP8_E4M3 0 /* float8_e4m3fn: forward operands, max 448   */
+#define UFP8_E5M2 1 /* float8_e5m2:   gradients,        max 57344 */
+
+/* operand storage order */
+#define UFP8_K_MAJOR 0  /* stored [rows = M or N][K], K contiguous   */
+#define UFP8_MN_MAJOR 1 /* stored [K][cols = M or N], M/N contiguous */
+
+/* output element type */
+#define UFP8_OUT_BF16 0
+#define UFP8_OUT_F32 1
+
+/* GEMM epilogues */
+#define UFP8_EPI_STORE 0   /* D = acc * sa * sb                                          */
+#define UFP8_EPI_SWIGLU 1  /* D[0]=U, D[1]=G, H = U * silu(G), amax_out = max|H|          */
+#define UFP8_EPI_DSWIGLU 2 /* dH = acc*sa*sb; D[0]=dU, D[1]=dG from saved U,G; amax |dUG| */
+
+const char* ufp8_last_error(void);
+int ufp8_abi_version(void);
+
+/* amax = max |x| over n bf16 elements (NaN-propagating), written to *amax (device f32).
+ * Replaces the amax half of the per-tensor recipe feeding custom_astype
+ * (ueaj/utils/gradutils.py:15-54). */
+int ufp8_amax(const void* x_bf16, int64_t n, float* amax, ufp8_stream_t stream);
+
+/* q = fp8(x * s) with s = FMAX(fmt) / *amax, *inv_scale = 1/s.  `amax` is a device
+ * pointer produced by ufp8_amax or by a GEMM epilogue.  Replaces the forward cast
+ * `lax.convert_element_type(x, float8)` (ueaj/utils/gradutils.py:34,41) and, with
+ * fmt = UFP8_E5M2, the backward cast of the gradient (ueaj/utils/gradutils.py:49). */
+int ufp8_quantize(const void* x_bf16, int64_t n, int fmt, const float* amax, void* q, float* inv_scale,
+                  ufp8_stream_t stream);
+
+/* ufp8_amax followed by ufp8_quantize on the same stream. */
+int ufp8_amax_quant(const void* x_bf16, int64_t n, int fmt, void* q, float* amax, float* inv_scale,
+                    ufp8_stream_t stream);
+
+/* q = fp8(x) with a unit scale: the plain element-type conversion of custom_astype
+ * (ueaj/utils/gradutils.py:34,41,49 `lax.convert_element_type`) to float8_e4m3fn /
+ * float8_e5m2, round to nearest even with the ml_dtypes overflow rules. */
+int ufp8_cast(const void* x_bf16, int64_t n, int fmt, void* q, ufp8_stream_t stream);
+
+/* One fp8 operand of a GEMM.  Logical shape [rows, K] for A (rows = M) and for B
+ * (rows = N); `major` says which index is contiguous in memory.  `ld` is the pitch in
+ * elements between consecutive stored rows (K-major: >= K; MN-major: >= rows) and
+ * `batch_stride` the pitch between batch slices (elements). */
+typedef struct ufp8_operand {
+  const void* ptr;
+  int32_t fmt;   /* UFP8_E4M3 / UFP8_E5M2 */
+  int32_t major; /* UFP8_K_MAJOR / UFP8_MN_MAJOR */
+  int64_t ld;
+  int64_t batch_stride;
+  int32_t batch_count;    /* slices present in memory (1 = broadcast over the GEMM batch) */
+  int32_t reserved;
+  const float* inv_scale; /* device f32: 1/s of this operand */
+} ufp8_operand;
+
+/* D[g] = sum_{kb < k_batches} A[g or kb] * B[g or kb]^T for g < batch.
+ * k_batches > 1 concatenates K over operand slices (e.g. dx = sum_i dUG[i] W[i]^T).
+ * UFP8_EPI_SWIGLU reads B slice 0 as `up` and slice 1 as `gate` for the same N range;
+ * D then holds U (slice 0) and G (slice 1) and `h` receives U * silu(G).
+ * UFP8_EPI_DSWIGLU reads the saved U / G from `ug` (slice pitch ug_batch_stride) and
+ * writes dU / dG to D slices 0 / 1.  `amax_out` (device f32, may be null for STORE) is
+ * overwritten with max |H| (SWIGLU) or max |dU, dG| (DSWIGLU). */
+typedef struct ufp8_gemm_desc {
+  int64_t M, N, K;
+  int32_t batch;
+  int32_t k_batches;
+  ufp8_operand a;
+  ufp8_operand b;
+  void* d;
+  int32_t d_dtype; /* UFP8_OUT_BF16 / UFP8_OUT_F32 (F32 only with UFP8_EPI_STORE) */
+  int32_t epilogue;
+  int64_t ldd;
+  int64_t d_batch_stride;
+  void* h; /* SWIGLU: bf16 H [M, N] */
+  int64_t ldh;
+  const void* ug; /* DSWIGLU: bf16 U at ug, G at ug + ug_batch_stride */
+  int64_t ldug;
+  int64_t ug_batch_stride;
+  float* amax_out;
+} ufp8_gemm_desc;
+
+int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);
+
+/* Synchronises the current device, returns its status word in *status (0 = clean,
+ * UFP8_STATUS_* bits otherwise) and clears it when `clear` is non-zero. */
+int ufp8_device_status(int* status, int clear);
+
+/* Number of CTAs the persistent GEMM launches (0 = one per SM, the default). */
+int ufp8_set_gemm_ctas(int ctas);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UFP8_H_ */

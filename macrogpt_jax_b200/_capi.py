@@ -1,0 +1,137 @@
+"""ctypes binding of libufp8.so (the C ABI declared in include/ufp8.h).
+
+There is no fallback: if the library is missing or cannot be loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libufp8.so"
+
+# Constants mirrored from include/ufp8.h.
+OK = 0
+ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
+STATUS_WAIT_TIMEOUT = 1
+E4M3, E5M2 = 0, 1
+K_MAJOR, MN_MAJOR = 0, 1
+OUT_BF16, OUT_F32 = 0, 1
+EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU = 0, 1, 2
+
+EXPORTED_SYMBOLS = (
+    "ufp8_last_error",
+    "ufp8_abi_version",
+    "ufp8_amax",
+    "ufp8_quantize",
+    "ufp8_amax_quant",
+    "ufp8_cast",
+    "ufp8_gemm",
+    "ufp8_device_status",
+    "ufp8_set_gemm_ctas",
+)
+
+
+class Operand(ctypes.Structure):
+    _fields_ = [
+        ("ptr", ctypes.c_void_p),
+        ("fmt", ctypes.c_int32),
+        ("major", ctypes.c_int32),
+        ("ld", ctypes.c_int64),
+        ("batch_stride", ctypes.c_int64),
+        ("batch_count", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("inv_scale", ctypes.c_void_p),
+    ]
+
+
+class GemmDesc(ctypes.Structure):
+    _fields_ = [
+        ("M", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("batch", ctypes.c_int32),
+        ("k_batches", ctypes.c_int32),
+        ("a", Operand),
+        ("b", Operand),
+        ("d", ctypes.c_void_p),
+        ("d_dtype", ctypes.c_int32),
+        ("epilogue", ctypes.c_int32),
+        ("ldd", ctypes.c_int64),
+        ("d_batch_stride", ctypes.c_int64),
+        ("h", ctypes.c_void_p),
+        ("ldh", ctypes.c_int64),
+        ("ug", ctypes.c_void_p),
+        ("ldug", ctypes.c_int64),
+        ("ug_batch_stride", ctypes.c_int64),
+        ("amax_out", ctypes.c_void_p),
+    ]
+
+
+class UFP8Error(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ufp8 error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads libufp8.so once; raises if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(f"libufp8.so not built at {LIB_PATH}; run `python -m macrogpt_jax_b200.build`")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.ufp8_last_error.restype = ctypes.c_char_p
+    lib.ufp8_last_error.argtypes = []
+    lib.ufp8_abi_version.restype = i32
+    lib.ufp8_amax.argtypes = [vp, i64, vp, vp]
+    lib.ufp8_quantize.argtypes = [vp, i64, i32, vp, vp, vp, vp]
+    lib.ufp8_amax_quant.argtypes = [vp, i64, i32, vp, vp, vp, vp]
+    lib.ufp8_cast.argtypes = [vp, i64, i32, vp, vp]
+    lib.ufp8_gemm.argtypes = [ctypes.POINTER(GemmDesc), vp]
+    lib.ufp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_int), i32]
+    lib.ufp8_set_gemm_ctas.argtypes = [i32]
+    for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
+                 "ufp8_set_gemm_ctas"):
+        getattr(lib, name).restype = i32
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise UFP8Error(rc, load().ufp8_last_error().decode(errors="replace"))
+
+
+def amax(x_ptr: int, n: int, amax_ptr: int, stream: int) -> None:
+    check(load().ufp8_amax(x_ptr, n, amax_ptr, stream))
+
+
+def quantize(x_ptr: int, n: int, fmt: int, amax_ptr: int, q_ptr: int, inv_ptr: int, stream: int) -> None:
+    check(load().ufp8_quantize(x_ptr, n, fmt, amax_ptr, q_ptr, inv_ptr, stream))
+
+
+def amax_quant(x_ptr: int, n: int, fmt: int, q_ptr: int, amax_ptr: int, inv_ptr: int, stream: int) -> None:
+    check(load().ufp8_amax_quant(x_ptr, n, fmt, q_ptr, amax_ptr, inv_ptr, stream))
+
+
+def cast(x_ptr: int, n: int, fmt: int, q_ptr: int, stream: int) -> None:
+    check(load().ufp8_cast(x_ptr, n, fmt, q_ptr, stream))
+
+
+def gemm(desc: GemmDesc, stream: int) -> None:
+    check(load().ufp8_gemm(ctypes.byref(desc), stream))
+
+
+def device_status(clear: bool = True) -> int:
+    out = ctypes.c_int(0)
+    check(load().ufp8_device_status(ctypes.byref(out), 1 if clear else 0))
+    return out.value
+
+
+def set_gemm_ctas(ctas: int) -> None:
+    check(load().ufp8_set_gemm_ctas(ctas))

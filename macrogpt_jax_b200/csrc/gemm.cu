@@ -1,0 +1,587 @@
+// Persistent, warp-specialised FP8 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   D[g][m][n] = alpha * sum_k A[m][k] * B[n][k],  alpha = inv_scale_a * inv_scale_b
+//
+// One CTA per SM (192 threads, ~193 KB shared memory, all 512 TMEM columns):
+//   warp 0      TMA producer: 4-stage ring of {A 128x128, B 256x128} fp8 tiles in
+//               128-byte-swizzled shared memory (plain tiled loads, never multicast);
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma.cta_group::1.kind::f8f6f4
+//               (M=128, N=256, K=32) into a double-buffered fp32 TMEM accumulator
+//               (2 x 256 columns) and frees ring slots with tcgen05.commit;
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns), scale, bf16/f32 cast and the
+//               fused GMLP math, 16-byte global stores; overlaps the next tile's MMAs.
+// Operands may be K-major or MN-major (both legal for e4m3/e5m2 on tcgen05), so the
+// backward contractions over tokens read the row-major activations directly and no
+// transposed copy is ever made.  Every mbarrier wait is bounded (see ptx.cuh).
+#include <cuda_bf16.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace ufp8 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle atom row
+constexpr int kStages = 4;
+constexpr int kTileBytesA = kBM * kBK;                      // 16 KiB
+constexpr int kHalfBytesB = 128 * kBK;                      // 16 KiB: 128 rows of B
+constexpr int kStageBytes = kTileBytesA + 2 * kHalfBytesB;  // 48 KiB
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kBarrierBytes = 256;
+constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
+constexpr int kGroupM = 16;
+
+struct GemmArgs {
+  int M, N, K;
+  int batch, k_batches, mode;
+  int a_major, b_major, a_bcast, b_bcast;
+  int tiles_m, tiles_n, ksteps;
+  uint32_t idesc;
+  const float* inv_a;
+  const float* inv_b;
+  void* d;
+  int d_f32;
+  int vec_ok;
+  long long ldd, d_bstride;
+  __nv_bfloat16* h;
+  long long ldh;
+  const __nv_bfloat16* ug;
+  long long ldug, ug_bstride;
+  unsigned int* amax_bits;
+  int* status;
+};
+
+__device__ __forceinline__ void map_tile(int tile, const GemmArgs& a, int& g, int& mb, int& nb) {
+  const int tpb = a.tiles_m * a.tiles_n;
+  g = tile / tpb;
+  const int r = tile - g * tpb;
+  const int span = kGroupM * a.tiles_n;
+  const int grp = r / span;
+  const int first_m = grp * kGroupM;
+  const int gm = min(a.tiles_m - first_m, kGroupM);
+  const int rr = r - grp * span;
+  mb = first_m + rr % gm;
+  nb = rr / gm;
+}
+
+__device__ __forceinline__ uint32_t bf16_bits(float v) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+}
+__device__ __forceinline__ float bf16_round(float v) { return __uint_as_float(bf16_bits(v) << 16); }
+__device__ __forceinline__ float bf16_to_f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+__device__ __forceinline__ float sigmoidf_(float g) { return __frcp_rn(1.0f + __expf(-g)); }
+
+// Stores 32 consecutive bf16 values (bit patterns in the low halves of v[]) at p;
+// columns at or past `valid` are skipped.  Vector path when the whole run is in range.
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* p, const uint32_t (&v)[32], int valid, bool vec) {
+  if (vec && valid >= 32) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 o;
+      o.x = v[8 * i + 0] | (v[8 * i + 1] << 16);
+      o.y = v[8 * i + 2] | (v[8 * i + 3] << 16);
+      o.z = v[8 * i + 4] | (v[8 * i + 5] << 16);
+      o.w = v[8 * i + 6] | (v[8 * i + 7] << 16);
+      q[i] = o;
+    }
+  } else {
+    uint16_t* q = reinterpret_cast<uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) q[j] = static_cast<uint16_t>(v[j]);
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* p, uint32_t (&v)[32], int valid, bool vec) {
+  if (vec && valid >= 32) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 w = q[i];
+      v[8 * i + 0] = w.x & 0xFFFFu; v[8 * i + 1] = w.x >> 16;
+      v[8 * i + 2] = w.y & 0xFFFFu; v[8 * i + 3] = w.y >> 16;
+      v[8 * i + 4] = w.z & 0xFFFFu; v[8 * i + 5] = w.z >> 16;
+      v[8 * i + 6] = w.w & 0xFFFFu; v[8 * i + 7] = w.w >> 16;
+    }
+  } else {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = j < valid ? q[j] : 0u;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles_m * args.tiles_n * args.batch;
+  const int total_k = args.ksteps * args.k_batches;
+  const bool swiglu = args.mode == UFP8_EPI_SWIGLU;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_parity = 0;  // per-stage bookkeeping for the abort drain
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int g, mb, nb;
+        map_tile(tile, args, g, mb, nb);
+        for (int ks = 0; ks < total_k; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+          const int kb = ks / args.ksteps;
+          const int k0 = (ks - kb * args.ksteps) * kBK;
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + kTileBytesA;
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          armed |= 1u << stage;
+          armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          if (args.a_major == UFP8_K_MAJOR)
+            tma_load_3d(sa, &tmA, &full[stage], k0, mb * kBM, az);
+          else
+            tma_load_3d(sa, &tmA, &full[stage], mb * kBM, k0, az);
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            int n0, bz;
+            if (swiglu) {
+              n0 = nb * 128;
+              bz = half;
+            } else {
+              n0 = nb * kBN + half * 128;
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+            }
+            if (args.b_major == UFP8_K_MAJOR)
+              tma_load_3d(sb + half * kHalfBytesB, &tmB, &full[stage], k0, n0, bz);
+            else
+              tma_load_3d(sb + half * kHalfBytesB, &tmB, &full[stage], n0, k0, bz);
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let every load this thread issued land before the CTA can exit.
+        volatile int never = 0;
+        for (int s = 0; s < kStages; ++s)
+          if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tphase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
+        bool ok = true;
+        for (int ks = 0; ks < total_k; ++ks) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kTileBytesA;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            const uint64_t adesc = args.a_major == UFP8_K_MAJOR
+                                       ? make_sdesc_sw128(sa + kk * 32, 16, 1024)
+                                       : make_sdesc_sw128(sa + kk * 32 * 128, kHalfBytesB, 1024);
+            const uint64_t bdesc = args.b_major == UFP8_K_MAJOR
+                                       ? make_sdesc_sw128(sb + kk * 32, 16, 1024)
+                                       : make_sdesc_sw128(sb + kk * 32 * 128, kHalfBytesB, 1024);
+            umma_f8f6f4(d_tmem, adesc, bdesc, args.idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+      }
+      // All MMAs this thread issued must finish before TMEM is released.
+      umma_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
+    const int row_in_tile = quad * 32 + lane;
+    const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
+    const bool vec = args.vec_ok != 0;
+    uint32_t amax = 0;  // max |value| over bf16 bit patterns written by this thread
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      bool ok = mbar_wait(&tfull[buf], tphase, abort_flag);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      int g, mb, nb;
+      map_tile(tile, args, g, mb, nb);
+      const int row = mb * kBM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
+
+      if (args.mode == UFP8_EPI_STORE) {
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = nb * kBN + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            if (args.d_f32) {
+              float* p = static_cast<float*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
+              if (vec && valid >= 32) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  reinterpret_cast<float4*>(p)[i] =
+                      make_float4(__uint_as_float(r[4 * i]) * alpha, __uint_as_float(r[4 * i + 1]) * alpha,
+                                  __uint_as_float(r[4 * i + 2]) * alpha, __uint_as_float(r[4 * i + 3]) * alpha);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < valid) p[j] = __uint_as_float(r[j]) * alpha;
+              }
+            } else {
+              uint32_t o[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] = bf16_bits(__uint_as_float(r[j]) * alpha);
+              __nv_bfloat16* p = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
+              store_bf16x32(p, o, valid, vec);
+            }
+          }
+        }
+      } else if (args.mode == UFP8_EPI_SWIGLU) {
+        // TMEM columns [0,128) hold up, [128,256) hold gate for hidden units nb*128 + c.
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t ru[32], rg[32];
+          tmem_ld_32x32b_x32(tbase + c, ru);
+          tmem_ld_32x32b_x32(tbase + 128 + c, rg);
+          tmem_ld_wait();
+          const int col0 = nb * 128 + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            uint32_t oh[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const uint32_t ub = bf16_bits(__uint_as_float(ru[j]) * alpha);
+              const uint32_t gb = bf16_bits(__uint_as_float(rg[j]) * alpha);
+              const float u = bf16_to_f(ub), gt = bf16_to_f(gb);
+              const float hv = u * (gt * sigmoidf_(gt));
+              const uint32_t hb = bf16_bits(hv);
+              ru[j] = ub;
+              rg[j] = gb;
+              oh[j] = hb;
+              if (j < valid) amax = max(amax, hb & 0x7FFFu);
+            }
+            __nv_bfloat16* pu = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
+            store_bf16x32(pu, ru, valid, vec);
+            store_bf16x32(pu + args.d_bstride, rg, valid, vec);
+            store_bf16x32(args.h + row * args.ldh + col0, oh, valid, vec);
+          }
+        }
+      } else {  // UFP8_EPI_DSWIGLU
+#pragma unroll 1
+        for (int c = 0; c < kBN; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = nb * kBN + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            uint32_t u16[32], g16[32];
+            const __nv_bfloat16* pu = args.ug + row * args.ldug + col0;
+            load_bf16x32(pu, u16, valid, vec);
+            load_bf16x32(pu + args.ug_bstride, g16, valid, vec);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float dh = bf16_round(__uint_as_float(r[j]) * alpha);
+              const float u = bf16_to_f(u16[j]), gt = bf16_to_f(g16[j]);
+              const float sg = sigmoidf_(gt);
+              const float du = dh * (gt * sg);
+              const float dg = (dh * u) * (sg * (1.0f + gt * (1.0f - sg)));
+              u16[j] = bf16_bits(du);
+              g16[j] = bf16_bits(dg);
+              if (j < valid) amax = max(amax, max(u16[j] & 0x7FFFu, g16[j] & 0x7FFFu));
+            }
+            __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
+            store_bf16x32(pd, u16, valid, vec);
+            store_bf16x32(pd + args.d_bstride, g16, valid, vec);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+    if (args.amax_bits != nullptr) {
+      amax = __reduce_max_sync(0xFFFFFFFFu, amax);
+      if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(args.status, UFP8_STATUS_WAIT_TIMEOUT);
+}
+
+// Writes zeros to every output of an empty-K contraction (K == 0).
+__global__ void zero_outputs_kernel(GemmArgs a) {
+  const long long total = static_cast<long long>(a.batch) * a.M * a.N;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long g = i / (static_cast<long long>(a.M) * a.N);
+    const long long r = i - g * a.M * a.N;
+    const long long m = r / a.N, n = r - m * a.N;
+    const int slices = a.mode == UFP8_EPI_STORE ? 1 : 2;
+    for (int s = 0; s < slices; ++s) {
+      const long long off = (g + s) * a.d_bstride + m * a.ldd + n;
+      if (a.d_f32)
+        static_cast<float*>(a.d)[off] = 0.0f;
+      else
+        static_cast<__nv_bfloat16*>(a.d)[off] = __float2bfloat16_rn(0.0f);
+    }
+    if (a.mode == UFP8_EPI_SWIGLU) a.h[m * a.ldh + n] = __float2bfloat16_rn(0.0f);
+  }
+}
+
+// ----------------------------------------------------------------------------- host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 3-D map over one fp8 operand: x = contiguous index, y = the other matrix index,
+// z = batch slice.  Box = 128 x 128 x 1 bytes with 128-byte swizzle.
+int encode_operand(CUtensorMap* map, const ufp8_operand& op, int64_t rows, int64_t K, const char* name) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(UFP8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const int64_t inner = op.major == UFP8_K_MAJOR ? K : rows;
+  const int64_t outer = op.major == UFP8_K_MAJOR ? rows : K;
+  const int64_t slices = op.batch_count < 1 ? 1 : op.batch_count;
+  const int64_t bstride = slices > 1 ? op.batch_stride : op.ld * outer;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(slices)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld), static_cast<cuuint64_t>(bstride)};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(op.ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(UFP8_ERR_INVALID, "cuTensorMapEncodeTiled failed for operand %s (CUresult %d)", name,
+                     static_cast<int>(r));
+  return UFP8_OK;
+}
+
+int check_operand(const ufp8_operand& op, int64_t rows, int64_t K, int need_slices, const char* name) {
+  if (!op.ptr) return set_error(UFP8_ERR_INVALID, "operand %s: null pointer", name);
+  if (!op.inv_scale) return set_error(UFP8_ERR_INVALID, "operand %s: null inv_scale", name);
+  if (op.fmt != UFP8_E4M3 && op.fmt != UFP8_E5M2)
+    return set_error(UFP8_ERR_INVALID, "operand %s: fmt %d is not UFP8_E4M3/UFP8_E5M2", name, op.fmt);
+  if (op.major != UFP8_K_MAJOR && op.major != UFP8_MN_MAJOR)
+    return set_error(UFP8_ERR_INVALID, "operand %s: major %d is not K/MN", name, op.major);
+  const int64_t inner = op.major == UFP8_K_MAJOR ? K : rows;
+  if (op.ld < inner) return set_error(UFP8_ERR_INVALID, "operand %s: ld %lld < contiguous extent %lld", name,
+                                      static_cast<long long>(op.ld), static_cast<long long>(inner));
+  if (reinterpret_cast<uintptr_t>(op.ptr) & 15u)
+    return set_error(UFP8_ERR_ALIGN, "operand %s: base pointer is not 16-byte aligned", name);
+  if (op.ld % 16 != 0)
+    return set_error(UFP8_ERR_ALIGN, "operand %s: ld %lld is not a multiple of 16 bytes", name,
+                     static_cast<long long>(op.ld));
+  if (op.batch_count > 1 && op.batch_stride % 16 != 0)
+    return set_error(UFP8_ERR_ALIGN, "operand %s: batch_stride is not a multiple of 16 bytes", name);
+  if (need_slices > 1 && op.batch_count < need_slices)
+    return set_error(UFP8_ERR_INVALID, "operand %s: needs %d batch slices, has %d", name, need_slices,
+                     op.batch_count);
+  if (inner >= (int64_t(1) << 31) || (op.major == UFP8_K_MAJOR ? rows : K) >= (int64_t(1) << 31))
+    return set_error(UFP8_ERR_INVALID, "operand %s: extent exceeds 2^31", name);
+  return UFP8_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& dev, int ctas_override) {
+  if (d.M < 0 || d.N < 0 || d.K < 0) return set_error(UFP8_ERR_INVALID, "negative GEMM extent");
+  if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
+  if (d.batch > 1 && d.k_batches > 1)
+    return set_error(UFP8_ERR_UNSUPPORTED, "batch > 1 together with k_batches > 1 is not supported");
+  if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU)
+    return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
+  if (d.d_dtype != UFP8_OUT_BF16 && d.d_dtype != UFP8_OUT_F32)
+    return set_error(UFP8_ERR_INVALID, "unknown output dtype %d", d.d_dtype);
+  if (d.epilogue != UFP8_EPI_STORE && (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1 || d.k_batches != 1))
+    return set_error(UFP8_ERR_INVALID, "SWIGLU/DSWIGLU epilogues need bf16 output, batch 1, k_batches 1");
+  if (!d.d) return set_error(UFP8_ERR_INVALID, "null output pointer");
+  if (d.ldd < d.N) return set_error(UFP8_ERR_INVALID, "ldd < N");
+  if (d.epilogue == UFP8_EPI_SWIGLU && (!d.h || d.ldh < d.N))
+    return set_error(UFP8_ERR_INVALID, "SWIGLU needs h with ldh >= N");
+  if (d.epilogue == UFP8_EPI_DSWIGLU && (!d.ug || d.ldug < d.N))
+    return set_error(UFP8_ERR_INVALID, "DSWIGLU needs ug with ldug >= N");
+  if (d.epilogue != UFP8_EPI_STORE && !d.amax_out)
+    return set_error(UFP8_ERR_INVALID, "SWIGLU/DSWIGLU need amax_out");
+  if (d.M >= (int64_t(1) << 31) || d.N >= (int64_t(1) << 31) || d.K >= (int64_t(1) << 31))
+    return set_error(UFP8_ERR_INVALID, "extent exceeds 2^31");
+
+  cudaError_t e;
+  if (d.amax_out) {
+    e = cudaMemsetAsync(d.amax_out, 0, sizeof(float), stream);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(amax_out)");
+  }
+  if (d.M == 0 || d.N == 0) return UFP8_OK;
+
+  GemmArgs a{};
+  a.M = static_cast<int>(d.M);
+  a.N = static_cast<int>(d.N);
+  a.K = static_cast<int>(d.K);
+  a.batch = d.batch;
+  a.k_batches = d.k_batches;
+  a.mode = d.epilogue;
+  a.d = d.d;
+  a.d_f32 = d.d_dtype == UFP8_OUT_F32;
+  a.ldd = d.ldd;
+  a.d_bstride = d.d_batch_stride;
+  a.h = static_cast<__nv_bfloat16*>(d.h);
+  a.ldh = d.ldh;
+  a.ug = static_cast<const __nv_bfloat16*>(d.ug);
+  a.ldug = d.ldug;
+  a.ug_bstride = d.ug_batch_stride;
+  a.amax_bits = reinterpret_cast<unsigned int*>(d.amax_out);
+  a.status = dev.status_word;
+
+  if (d.K == 0) {
+    zero_outputs_kernel<<<dev.sm_count * 4, 256, 0, stream>>>(a);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? UFP8_OK : cuda_error(e, "zero-fill launch");
+  }
+
+  const bool swiglu = d.epilogue == UFP8_EPI_SWIGLU;
+  int rc = check_operand(d.a, d.M, d.K, d.k_batches > 1 ? d.k_batches : (d.a.batch_count > 1 ? d.batch : 1), "A");
+  if (rc) return rc;
+  rc = check_operand(d.b, d.N, d.K, swiglu ? 2 : (d.k_batches > 1 ? d.k_batches : (d.b.batch_count > 1 ? d.batch : 1)),
+                     "B");
+  if (rc) return rc;
+
+  a.a_major = d.a.major;
+  a.b_major = d.b.major;
+  a.a_bcast = d.a.batch_count <= 1 && d.k_batches == 1;
+  a.b_bcast = !swiglu && d.b.batch_count <= 1 && d.k_batches == 1;
+  a.inv_a = d.a.inv_scale;
+  a.inv_b = d.b.inv_scale;
+  a.tiles_m = static_cast<int>((d.M + kBM - 1) / kBM);
+  const int bn = swiglu ? 128 : kBN;
+  a.tiles_n = static_cast<int>((d.N + bn - 1) / bn);
+  a.ksteps = static_cast<int>((d.K + kBK - 1) / kBK);
+  a.idesc = (1u << 4)                                       // f32 accumulator
+            | (static_cast<uint32_t>(d.a.fmt) << 7)         // A format
+            | (static_cast<uint32_t>(d.b.fmt) << 10)        // B format
+            | (static_cast<uint32_t>(d.a.major) << 15)      // A major
+            | (static_cast<uint32_t>(d.b.major) << 16)      // B major
+            | (static_cast<uint32_t>(kBN >> 3) << 17)       // N = 256
+            | (static_cast<uint32_t>(kBM >> 4) << 24);      // M = 128
+
+  const int esz = a.d_f32 ? 4 : 2;
+  bool vec = aligned16(d.d) && (d.ldd * esz) % 16 == 0 && (d.d_batch_stride * esz) % 16 == 0;
+  if (swiglu) vec = vec && aligned16(d.h) && (d.ldh * 2) % 16 == 0;
+  if (d.epilogue == UFP8_EPI_DSWIGLU) vec = vec && aligned16(d.ug) && (d.ldug * 2) % 16 == 0 && (d.ug_batch_stride * 2) % 16 == 0;
+  a.vec_ok = vec ? 1 : 0;
+
+  CUtensorMap tmA, tmB;
+  rc = encode_operand(&tmA, d.a, d.M, d.K, "A");
+  if (rc) return rc;
+  rc = encode_operand(&tmB, d.b, d.N, d.K, "B");
+  if (rc) return rc;
+
+  static thread_local int attr_device = -1;
+  if (attr_device != dev.device) {
+    e = cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
+    attr_device = dev.device;
+  }
+  const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
+  if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
+  int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
+  if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
+  gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "gemm kernel launch");
+}
+
+}  // namespace ufp8

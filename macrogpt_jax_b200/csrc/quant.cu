@@ -1,0 +1,217 @@
+// Per-tensor amax and fp8 quantisation (bf16 -> float8_e4m3fn / float8_e5m2).
+//
+// Semantics (the per-tensor current-scaling recipe around the reference's casts,
+// ueaj/utils/gradutils.py:15-54):
+//   amax      = max |x|, taken as an unsigned max over the sign-cleared bf16 bit patterns,
+//               so it is exact and NaN-propagating (a NaN pattern is above +inf);
+//   s         = FMAX / amax in IEEE fp32 (FMAX = 448 for e4m3fn, 57344 for e5m2), s = 1
+//               when amax == 0;
+//   q         = cast(f32(x) * s) with round-to-nearest-even and the ml_dtypes 0.5.4
+//               overflow rules (e4m3fn: |p| > 464 or inf -> NaN 0x7F|sign;
+//               e5m2: |p| >= 61440 or inf -> inf 0x7C|sign); a NaN product becomes the
+//               positive NaN pattern (0x7F e4m3fn, 0x7E e5m2);
+//   inv_scale = 1 / s in IEEE fp32.
+// The hardware conversion (cvt.rn.satfinite) rounds to nearest even like the cast; it
+// only saturates where the cast overflows, so those products (and NaN) are re-encoded.
+// With s derived from the tensor's own amax, |x*s| <= 448.0001 (resp. 57344.004) and the
+// re-encoding is reached only by non-finite products; a caller-supplied amax below the
+// true maximum reaches the overflow rules.
+//
+// Both kernels are HBM-bound streaming passes: 16-byte vector loads, a grid of a few
+// CTAs per SM with grid-stride loops, and (amax) a packed 2x16-bit unsigned max
+// followed by a warp shuffle reduction and one atomicMax per CTA.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include "internal.h"
+
+namespace ufp8 {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kCtasPerSm = 8;
+
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) {
+  return __vmaxu2(acc, w & 0x7FFF7FFFu);
+}
+
+__device__ __forceinline__ void block_amax_commit(uint32_t m2, unsigned int* amax_bits) {
+  uint32_t m = max(m2 & 0xFFFFu, m2 >> 16);
+  m = __reduce_max_sync(0xFFFFFFFFu, m);
+  __shared__ uint32_t warp_max[kThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) warp_max[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t v = lane < (kThreads / 32) ? warp_max[lane] : 0u;
+    v = __reduce_max_sync(0xFFFFFFFFu, v);
+    if (lane == 0 && v != 0u) atomicMax(amax_bits, v << 16);
+  }
+}
+
+// Vector body: x is 16-byte aligned; n_vec groups of 8 bf16, then n_tail (< 8) scalars.
+__global__ void __launch_bounds__(kThreads) amax_vec_kernel(const uint4* __restrict__ x, int64_t n_vec,
+                                                            const uint16_t* __restrict__ tail, int n_tail,
+                                                            unsigned int* amax_bits) {
+  uint32_t m2 = 0;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  // Two independent 16-byte loads in flight per thread per iteration.
+  for (; i + stride < n_vec; i += 2 * stride) {
+    const uint4 a = ld_stream(x + i);
+    const uint4 b = ld_stream(x + i + stride);
+    m2 = absmax2(m2, a.x); m2 = absmax2(m2, a.y); m2 = absmax2(m2, a.z); m2 = absmax2(m2, a.w);
+    m2 = absmax2(m2, b.x); m2 = absmax2(m2, b.y); m2 = absmax2(m2, b.z); m2 = absmax2(m2, b.w);
+  }
+  if (i < n_vec) {
+    const uint4 a = ld_stream(x + i);
+    m2 = absmax2(m2, a.x); m2 = absmax2(m2, a.y); m2 = absmax2(m2, a.z); m2 = absmax2(m2, a.w);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n_tail) m2 = __vmaxu2(m2, static_cast<uint32_t>(tail[threadIdx.x] & 0x7FFFu));
+  block_amax_commit(m2, amax_bits);
+}
+
+// Any alignment: one element per thread per step.
+__global__ void __launch_bounds__(kThreads) amax_scalar_kernel(const uint16_t* __restrict__ x, int64_t n,
+                                                               unsigned int* amax_bits) {
+  uint32_t m2 = 0;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kThreads)
+    m2 = max(m2, static_cast<uint32_t>(x[i] & 0x7FFFu));
+  block_amax_commit(m2, amax_bits);
+}
+
+__device__ __forceinline__ float fp8_fmax(int fmt) { return fmt == UFP8_E4M3 ? 448.0f : 57344.0f; }
+
+__device__ __forceinline__ float scale_from_amax(float amax, int fmt) {
+  return amax == 0.0f ? 1.0f : __fdiv_rn(fp8_fmax(fmt), amax);
+}
+
+// True where the satfinite hardware conversion differs from the non-saturating cast:
+// NaN, and magnitudes that round past the largest finite value (e4m3fn: above 464,
+// e5m2: 61440 and above, infinities included).
+__device__ __forceinline__ bool is_special(float p, int fmt) {
+  const float a = fabsf(p);
+  return fmt == UFP8_E4M3 ? !(a <= 464.0f) : !(a < 61440.0f);
+}
+
+// ml_dtypes encoding of a special product: NaN -> positive NaN pattern, overflow ->
+// NaN (e4m3fn, which has no infinity) or inf (e5m2), keeping the sign.
+__device__ __forceinline__ uint32_t special_code(float p, int fmt) {
+  const uint32_t sign = (__float_as_uint(p) >> 24) & 0x80u;
+  if (isnan(p)) return fmt == UFP8_E4M3 ? 0x7Fu : 0x7Eu;
+  return (fmt == UFP8_E4M3 ? 0x7Fu : 0x7Cu) | sign;
+}
+
+// Converts two products to packed fp8 (first -> low byte).
+__device__ __forceinline__ uint32_t cvt2(float p0, float p1, int fmt) {
+  const __nv_fp8_interpretation_t kind = fmt == UFP8_E4M3 ? __NV_E4M3 : __NV_E5M2;
+  uint32_t v = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(p0, p1), __NV_SATFINITE, kind));
+  if (is_special(p0, fmt)) v = (v & 0xFF00u) | special_code(p0, fmt);
+  if (is_special(p1, fmt)) v = (v & 0x00FFu) | (special_code(p1, fmt) << 8);
+  return v;
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// 2 bf16 (one 32-bit word) -> 2 fp8 bytes.
+__device__ __forceinline__ uint32_t quant_word(uint32_t w, float s, int fmt) {
+  return cvt2(__fmul_rn(bf16lo(w), s), __fmul_rn(bf16hi(w), s), fmt);
+}
+
+__device__ __forceinline__ uint32_t quant_4bytes(uint32_t w0, uint32_t w1, float s, int fmt) {
+  return quant_word(w0, s, fmt) | (quant_word(w1, s, fmt) << 16);
+}
+
+// Vector body: 16 bf16 (two 16-byte loads) -> 16 fp8 (one 16-byte store) per step.
+// A null `amax` means a unit scale (plain cast); a null `inv_scale` is not written.
+__global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __restrict__ x, int64_t n_vec16,
+                                                             const uint16_t* __restrict__ x_tail,
+                                                             uint8_t* __restrict__ q_tail, int n_tail,
+                                                             int fmt, const float* __restrict__ amax,
+                                                             uint4* __restrict__ q, float* __restrict__ inv_scale) {
+  const float s = amax ? scale_from_amax(*amax, fmt) : 1.0f;
+  if (inv_scale && blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = __fdiv_rn(1.0f, s);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n_vec16; i += stride) {
+    const uint4 a = ld_stream(x + 2 * i);
+    const uint4 b = ld_stream(x + 2 * i + 1);
+    uint4 o;
+    o.x = quant_4bytes(a.x, a.y, s, fmt);
+    o.y = quant_4bytes(a.z, a.w, s, fmt);
+    o.z = quant_4bytes(b.x, b.y, s, fmt);
+    o.w = quant_4bytes(b.z, b.w, s, fmt);
+    q[i] = o;
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n_tail) {
+    const float p = __fmul_rn(__uint_as_float(static_cast<uint32_t>(x_tail[threadIdx.x]) << 16), s);
+    q_tail[threadIdx.x] = static_cast<uint8_t>(cvt2(p, 0.0f, fmt) & 0xFFu);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) quant_scalar_kernel(const uint16_t* __restrict__ x, int64_t n, int fmt,
+                                                                const float* __restrict__ amax,
+                                                                uint8_t* __restrict__ q,
+                                                                float* __restrict__ inv_scale) {
+  const float s = amax ? scale_from_amax(*amax, fmt) : 1.0f;
+  if (inv_scale && blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = __fdiv_rn(1.0f, s);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const float p = __fmul_rn(__uint_as_float(static_cast<uint32_t>(x[i]) << 16), s);
+    q[i] = static_cast<uint8_t>(cvt2(p, 0.0f, fmt) & 0xFFu);
+  }
+}
+
+int grid_for(int64_t work_items, const DeviceInfo& dev) {
+  const int64_t want = (work_items + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(dev.sm_count) * kCtasPerSm;
+  return static_cast<int>(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+}  // namespace
+
+int launch_amax(const void* x, int64_t n, float* amax, cudaStream_t s, const DeviceInfo& dev) {
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(float), s);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemsetAsync(amax)");
+  if (n == 0) return UFP8_OK;
+  unsigned int* bits = reinterpret_cast<unsigned int*>(amax);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const int64_t n_vec = n / 8;
+    const int n_tail = static_cast<int>(n - n_vec * 8);
+    const uint16_t* tail = static_cast<const uint16_t*>(x) + n_vec * 8;
+    amax_vec_kernel<<<grid_for((n_vec + 1) / 2, dev), kThreads, 0, s>>>(static_cast<const uint4*>(x), n_vec, tail,
+                                                                       n_tail, bits);
+  } else {
+    amax_scalar_kernel<<<grid_for(n, dev), kThreads, 0, s>>>(static_cast<const uint16_t*>(x), n, bits);
+  }
+  e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "amax kernel launch");
+}
+
+int launch_quantize(const void* x, int64_t n, int fmt, const float* amax, void* q, float* inv_scale,
+                    cudaStream_t s, const DeviceInfo& dev) {
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(q)) & 15u) == 0;
+  if (aligned) {
+    const int64_t n_vec16 = n / 16;
+    const int n_tail = static_cast<int>(n - n_vec16 * 16);
+    quant_vec_kernel<<<grid_for(n_vec16, dev), kThreads, 0, s>>>(
+        static_cast<const uint4*>(x), n_vec16, static_cast<const uint16_t*>(x) + n_vec16 * 16,
+        static_cast<uint8_t*>(q) + n_vec16 * 16, n_tail, fmt, amax, static_cast<uint4*>(q), inv_scale);
+  } else {
+    quant_scalar_kernel<<<grid_for(n, dev), kThreads, 0, s>>>(static_cast<const uint16_t*>(x), n, fmt, amax,
+                                                              static_cast<uint8_t*>(q), inv_scale);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "quantize kernel launch");
+}
+
+}  // namespace ufp8

@@ -1,0 +1,195 @@
+"""Device ops of the FP8 contraction path, each a direct call into libufp8 (include/ufp8.h).
+
+torch is used only for device memory, the current stream and autograd plumbing; every
+amax, quantisation and contraction below runs in this package's sm_100a kernels.  There is
+no CPU path: inputs must be CUDA tensors and a missing library raises.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _capi as C
+
+FP8_DTYPE = {C.E4M3: torch.float8_e4m3fn, C.E5M2: torch.float8_e5m2}
+FMT_OF_DTYPE = {torch.float8_e4m3fn: C.E4M3, torch.float8_e5m2: C.E5M2}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _check_bf16_cuda(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_cuda:
+        raise ValueError(f"{name}: expected a CUDA tensor (this library has no CPU path)")
+    if t.dtype != torch.bfloat16:
+        raise TypeError(f"{name}: expected bfloat16, got {t.dtype}")
+    return t.contiguous()
+
+
+@dataclass
+class Fp8Tensor:
+    """fp8 payload with its per-tensor factors (device f32 scalars)."""
+    q: torch.Tensor
+    inv_scale: torch.Tensor
+    amax: torch.Tensor
+
+    @property
+    def fmt(self) -> int:
+        return FMT_OF_DTYPE[self.q.dtype]
+
+
+def amax(x: torch.Tensor) -> torch.Tensor:
+    x = _check_bf16_cuda(x, "amax")
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    C.amax(x.data_ptr(), x.numel(), out.data_ptr(), _stream())
+    return out
+
+
+def quantize(x: torch.Tensor, fmt: int, amax_t: torch.Tensor | None = None) -> Fp8Tensor:
+    """Per-tensor current scaling: amax (unless given) -> s = FMAX/amax -> fp8(x*s)."""
+    x = _check_bf16_cuda(x, "quantize")
+    q = torch.empty(x.shape, dtype=FP8_DTYPE[fmt], device=x.device)
+    inv = torch.empty(1, dtype=torch.float32, device=x.device)
+    if amax_t is None:
+        amax_t = torch.empty(1, dtype=torch.float32, device=x.device)
+        C.amax_quant(x.data_ptr(), x.numel(), fmt, q.data_ptr(), amax_t.data_ptr(), inv.data_ptr(), _stream())
+    else:
+        C.quantize(x.data_ptr(), x.numel(), fmt, amax_t.data_ptr(), q.data_ptr(), inv.data_ptr(), _stream())
+    return Fp8Tensor(q, inv, amax_t)
+
+
+def operand(t: Fp8Tensor, major: int, ld: int, batch_stride: int = 0, batch_count: int = 1,
+            inv_scale: torch.Tensor | None = None) -> C.Operand:
+    inv = t.inv_scale if inv_scale is None else inv_scale
+    return C.Operand(t.q.data_ptr(), t.fmt, major, ld, batch_stride, batch_count, 0, inv.data_ptr())
+
+
+def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ldd: int,
+         d_batch_stride: int = 0, batch: int = 1, k_batches: int = 1, epilogue: int = C.EPI_STORE,
+         h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
+         ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None) -> None:
+    desc = C.GemmDesc()
+    desc.M, desc.N, desc.K = M, N, K
+    desc.batch, desc.k_batches = batch, k_batches
+    desc.a, desc.b = a, b
+    desc.d = d.data_ptr()
+    desc.d_dtype = C.OUT_F32 if d.dtype == torch.float32 else C.OUT_BF16
+    desc.epilogue = epilogue
+    desc.ldd, desc.d_batch_stride = ldd, d_batch_stride
+    desc.h = h.data_ptr() if h is not None else None
+    desc.ldh = ldh
+    desc.ug = ug.data_ptr() if ug is not None else None
+    desc.ldug, desc.ug_batch_stride = ldug, ug_batch_stride
+    desc.amax_out = amax_out.data_ptr() if amax_out is not None else None
+    C.gemm(desc, _stream())
+
+
+# ----------------------------------------------------------------------------- Einsum
+@dataclass(frozen=True)
+class EinsumPlan:
+    """GEMM view of a canonical Einsum: out[g] = X[M,K] @ W[g][K,N]."""
+    G: int
+    M_shape: tuple
+    K: int
+    N: int
+    out_shape: tuple
+
+
+def einsum_forward(plan: EinsumPlan, x: torch.Tensor, w: torch.Tensor, fwd_fmt: int,
+                   alpha: float | None = None):
+    """Forward of ueaj.model.Einsum (ueaj/model/einsum.py:233-251) in FP8."""
+    G, K, N = plan.G, plan.K, plan.N
+    M = 1
+    for s in plan.M_shape:
+        M *= s
+    qx = quantize(x.reshape(M, K), fwd_fmt)
+    qw = quantize(w.reshape(G, K, N), fwd_fmt)
+    out = torch.empty((G, M, N), dtype=torch.bfloat16, device=x.device)
+    inv_b = qw.inv_scale if alpha is None else qw.inv_scale * alpha
+    gemm(operand(qx, C.K_MAJOR, K), operand(qw, C.MN_MAJOR, N, K * N, G, inv_scale=inv_b),
+         M, N, K, out, N, M * N, batch=G)
+    return out.reshape(plan.out_shape), (qx, qw)
+
+
+def einsum_backward(plan: EinsumPlan, dout: torch.Tensor, saved, bwd_fmt: int, need_dx: bool, need_dw: bool,
+                    alpha: float | None = None):
+    """dX = dOut W^T (summed over weight batch slices) and dW = X^T dOut."""
+    qx, qw = saved
+    G, K, N = plan.G, plan.K, plan.N
+    M = qx.q.shape[0]
+    qd = quantize(dout.reshape(G * M, N), bwd_fmt)
+    dx = dw = None
+    if need_dx:
+        dx = torch.empty((M, K), dtype=torch.bfloat16, device=dout.device)
+        inv_b = qw.inv_scale if alpha is None else qw.inv_scale * alpha
+        gemm(operand(qd, C.K_MAJOR, N, M * N, G), operand(qw, C.K_MAJOR, N, K * N, G, inv_scale=inv_b),
+             M, K, N, dx, K, k_batches=G)
+    if need_dw:
+        dw = torch.empty((G, K, N), dtype=torch.bfloat16, device=dout.device)
+        gemm(operand(qx, C.MN_MAJOR, K), operand(qd, C.MN_MAJOR, N, M * N, G),
+             K, N, M, dw, N, K * N, batch=G)
+    return dx, dw
+
+
+# ----------------------------------------------------------------------------- GMLP
+def gmlp_forward(x: torch.Tensor, wf: torch.Tensor, wd: torch.Tensor):
+    """FP8 GMLP forward, GMLP.__call__ (ueaj/model/mlp.py:100-115) with the fused gate/up
+    Einsum "bnd,idh->ibnh" and its gating fused into one GEMM epilogue.
+
+    x [T, d] bf16, wf [2, d, h] bf16 (index 0 = up, 1 = gate), wd [h, d] bf16.
+    Returns y [T, d] bf16 and the tensors the backward needs.
+    """
+    x = _check_bf16_cuda(x, "x")
+    wf = _check_bf16_cuda(wf, "wf")
+    wd = _check_bf16_cuda(wd, "wd")
+    T, d = x.shape
+    h = wf.shape[2]
+    dev = x.device
+    qx = quantize(x, C.E4M3)
+    qwf = quantize(wf, C.E4M3)
+    ug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
+    hid = torch.empty((T, h), dtype=torch.bfloat16, device=dev)
+    amax_h = torch.empty(1, dtype=torch.float32, device=dev)
+    gemm(operand(qx, C.K_MAJOR, d), operand(qwf, C.MN_MAJOR, h, d * h, 2), T, h, d, ug, h, T * h,
+         epilogue=C.EPI_SWIGLU, h=hid, ldh=h, amax_out=amax_h)
+    qh = quantize(hid, C.E4M3, amax_h)
+    qwd = quantize(wd, C.E4M3)
+    y = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+    gemm(operand(qh, C.K_MAJOR, h), operand(qwd, C.MN_MAJOR, d), T, d, h, y, d)
+    return y, (qx, qwf, ug, qh, qwd)
+
+
+def gmlp_backward(dy: torch.Tensor, saved, need_dx: bool = True, need_dw: bool = True):
+    """Backward of gmlp_forward: the four contractions JAX derives for the two Einsums plus
+    the gating backward, with e5m2 gradients and e4m3 saved operands."""
+    qx, qwf, ug, qh, qwd = saved
+    dy = _check_bf16_cuda(dy, "dy")
+    T, d = dy.shape
+    h = ug.shape[2]
+    dev = dy.device
+    qdy = quantize(dy, C.E5M2)
+    dug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
+    amax_dug = torch.empty(1, dtype=torch.float32, device=dev)
+    # dH = dY Wd^T fused with the gating backward -> [dU, dG]
+    gemm(operand(qdy, C.K_MAJOR, d), operand(qwd, C.K_MAJOR, d), T, h, d, dug, h, T * h,
+         epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug)
+    dwd = dwf = dx = None
+    if need_dw:  # dWd = H^T dY
+        dwd = torch.empty((h, d), dtype=torch.bfloat16, device=dev)
+        gemm(operand(qh, C.MN_MAJOR, h), operand(qdy, C.MN_MAJOR, d), h, d, T, dwd, d)
+    qdug = quantize(dug, C.E5M2, amax_dug)
+    if need_dx:  # dx = sum_i dUG[i] Wf[i]^T
+        dx = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
+        gemm(operand(qdug, C.K_MAJOR, h, T * h, 2), operand(qwf, C.K_MAJOR, h, d * h, 2), T, d, h, dx, d,
+             k_batches=2)
+    if need_dw:  # dWf[i] = x^T dUG[i]
+        dwf = torch.empty((2, d, h), dtype=torch.bfloat16, device=dev)
+        gemm(operand(qx, C.MN_MAJOR, d), operand(qdug, C.MN_MAJOR, h, T * h, 2), d, h, T, dwf, h, d * h,
+             batch=2)
+    return dx, dwf, dwd
+
+
+def device_status(clear: bool = True) -> int:
+    return C.device_status(clear)
