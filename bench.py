@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""FP8 GMLP forward + backward benchmark (one JSON line on rank 0).
+
+Workload: the tensor-parallel GMLP block of macrogpt-jax at d_model 4096, hidden 14336,
+16384 tokens (B 4 x S 4096) per step, FP8 (e4m3 forward operands, e5m2 gradients, fp32
+accumulate, bf16 outputs), seeded synthetic inputs: x ~ N(0, 1), dY ~ N(0, 1e-3),
+weights ~ N(0, 1/fan_in).  A step is one forward and one backward pass of the block
+through the public module API (GMLP(...)(x).backward(dY)); at N GPUs the same 16384-token
+step runs tensor-parallel over N ranks (strong scaling).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the CPU oracle of the same path (the reference's own program is
+JAX, which cannot be installed on these machines) on the host cores, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP8 GMLP fwd+bwd TFLOP/s/GPU (% of FP8 peak), tokens/s at 1/2/4/8 B200"
+CONFIGS = {
+    # C4 (the headline, TP GMLP) and C2 (small single-GPU GMLP)
+    "gmlp_d4096": dict(d=4096, h=14336, B=4, S=4096),
+    "gmlp_d768": dict(d=768, h=3072, B=8, S=1024),
+}
+FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def flops_per_step(T, d, h):
+    """Algorithmic GMLP fwd+bwd FLOPs: 18 T d h (F1 4Tdh, F2 2Tdh, backward twice that)."""
+    return 18.0 * T * d * h
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured (MEASURED_PEAKS.json)"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback (earlier measurement on this pool)"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(", ") for r in Path(self.path).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.path)
+        rows = [r for r in rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_oracle_step(d, h, T, seed=0):
+    """Seconds the oracle takes for one GMLP fwd+bwd step of T tokens on the host: per-tensor
+    quantisation (and dequantisation) of the weights, both contractions forward, the four
+    backward, gating and the activation/gradient quantisations."""
+    import numpy as np
+    from oracle import path as op
+    op.FAST_CAST = True
+    rng = np.random.default_rng(seed)
+    wf = op.bf16_normal(rng, (2, d, h), d ** -0.5)
+    wd = op.bf16_normal(rng, (h, d), h ** -0.5)
+    x = op.bf16_normal(rng, (T, d))
+    dy = op.bf16_normal(rng, (T, d), 1e-3)
+    t0 = time.perf_counter()
+    _, saved = op.gmlp_forward(x, wf, wd, acc=np.float32)
+    op.gmlp_backward(dy, saved, acc=np.float32)
+    return time.perf_counter() - t0
+
+
+def extrapolate(samples, T_full, h_scale):
+    """Least-squares fit t(T) = a + b T over (T, seconds) samples taken at a hidden slice,
+    evaluated at T_full and scaled by h_scale = hidden / slice (every cost of the block, the
+    weights included, is linear in the hidden width)."""
+    import numpy as np
+    Ts = np.array([s[0] for s in samples], dtype=np.float64)
+    ts = np.array([s[1] for s in samples], dtype=np.float64)
+    b, a = np.polyfit(Ts, ts, 1) if len(set(Ts)) > 1 else (ts.mean() / Ts.mean(), 0.0)
+    return float((max(a, 0.0) + max(b, 0.0) * T_full) * h_scale)
+
+
+def cpu_plan(T, h, ref_tokens, ref_hidden):
+    T_lo = max(16, min(T, ref_tokens))
+    T_hi = min(T, 3 * T_lo)
+    h_s = max(128, min(h, ref_hidden))
+    return T_lo, T_hi, h_s
+
+
+def cpu_sample_desc(T_lo, T_hi, h_s, T_full, h):
+    return (f"oracle GMLP fwd+bwd steps of {T_lo} and {T_hi} tokens at d_model full and hidden {h_s} of {h} "
+            f"(weights quantised each step), fitted as a + b*T, evaluated at {T_full} tokens and scaled by "
+            f"{h}/{h_s} (all costs are linear in hidden); numpy fp32 BLAS matmuls on all host threads, "
+            "ml_dtypes casts, single-threaded elementwise")
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------- arms
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return None
+    d, h, T = cfg["d"], cfg["h"], cfg["B"] * cfg["S"]
+    T_lo, T_hi, h_s = cpu_plan(T, h, args.ref_tokens, args.ref_hidden)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        Ti = T_lo if i % 2 == 0 else T_hi
+        t = cpu_oracle_step(d, h_s, Ti, seed=i)
+        if i >= args.warmup:
+            samples.append((Ti, t))
+    step_s = extrapolate(samples, T, h / h_s)
+    step_times = [step_s] * args.steps
+    sample = cpu_sample_desc(T_lo, T_hi, h_s, T, h)
+    total = sum(step_times)
+    value = T * args.steps / total
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8",
+        "data": "synthetic (seeded)",
+        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h},
+        "tflops_per_gpu": flops_per_step(T, d, h) * value / T / 1e12,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    return out
+
+
+def run_ours(args, cfg, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from macrogpt_jax_b200 import _capi, ops
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.mlp import GMLP
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
+    T = B * S
+    if world > 1:
+        from macrogpt_jax_b200.tp import TPGMLP
+        mlp = TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
+                     fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5))
+        parallelism = f"tp{world}"
+    else:
+        mlp = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(d ** -0.5)),
+                            down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
+            model_d=d, hidden_d=h, rngs=Rngs(0))
+        assert mlp.fused()
+        parallelism = "tp1"
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)  # identical activations on every rank (TP replicates x and dY)
+    x_full = torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    dy_full = (torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32) * 1e-3).to(torch.bfloat16)
+    x_in, dy_in = (mlp.shard_tokens(x_full), mlp.shard_tokens(dy_full)) if world > 1 else (x_full, dy_full)
+    params = list(mlp.parameters())
+
+    def step(xb, dyb):
+        xl = xb.detach().requires_grad_(True)
+        y = mlp(xl)
+        y.backward(dyb)
+        for p in params:
+            p.grad = None
+        return y
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step(x_in, dy_in)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- headline: device-resident inputs, per-launch events on the launching stream
+    timer = ops.KernelTimer()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = _capi.launches
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.set_timer(timer)
+    ev0.record()
+    for _ in range(args.steps):
+        step(x_in, dy_in)
+    ev1.record()
+    ops.set_timer(None)
+    torch.cuda.synchronize()
+    barrier()
+    launches = _capi.launches - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    summ = timer.summary()
+
+    # ---- end to end: host (pinned) inputs copied in and y read back inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        x_host = x_in.cpu().pin_memory()
+        dy_host = dy_in.cpu().pin_memory()
+        x_dev = torch.empty_like(x_in)
+        dy_dev = torch.empty_like(dy_in)
+        y_host = torch.empty(x_in.shape, dtype=torch.bfloat16).pin_memory()
+        for _ in range(2):
+            x_dev.copy_(x_host, non_blocking=True)
+            dy_dev.copy_(dy_host, non_blocking=True)
+            y_host.copy_(step(x_dev, dy_dev).detach(), non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            dy_dev.copy_(dy_host, non_blocking=True)
+            y_host.copy_(step(x_dev, dy_dev).detach(), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ems_t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(ems_t, op=dist.ReduceOp.MAX)
+        ems = float(ems_t.item())
+        nb = x_in.numel() * 2
+        e2e = {"value": T * args.steps / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems / args.steps,
+               "h2d_bytes_per_step": 2 * nb * world, "d2h_bytes_per_step": nb * world,
+               "path": "GMLP module forward+backward with x, dY copied from pinned host memory and y "
+                       "copied back every step"}
+
+    if rank != 0:
+        return None
+    peaks, peak_src = load_peaks()
+    fl = flops_per_step(T, d, h)
+    tokens_s = T * args.steps / (ms / 1000.0)
+    tflops_gpu = fl * args.steps / (ms / 1000.0) / world / 1e12
+    g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
+    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
+    q_n, q_ms, q_b = summ.get("quantize", (0, 0.0, 0.0))
+    a_n, a_ms, a_b = summ.get("amax", (0, 0.0, 0.0))
+    out = {
+        "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
+        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h,
+                   "parallelism": parallelism, "l2": "inputs larger than L2 (working set > 4 GB/step)"},
+        "tflops_per_gpu": tflops_gpu,
+        "frac_of_fp8_peak": {"nominal_4500": tflops_gpu / FP8_NOMINAL_TFLOPS,
+                             "measured_2x_bf16_sustained": tflops_gpu / peak_fp8},
+        "roofline": {"kernel": "gemm_fp8_kernel", "bound": "tensor", "achieved": achieved,
+                     "peak": peak_fp8, "unit": "TFLOP/s", "frac": (achieved / peak_fp8) if achieved else None,
+                     "frac_of_nominal_fp8": (achieved / FP8_NOMINAL_TFLOPS) if achieved else None,
+                     "peak_source": f"2 x bf16_tflops_sustained, {peak_src}; tcgen05 runs fp8 at twice "
+                                    "its bf16 rate",
+                     "launches": g_n, "time_share": g_ms / ms if ms else None,
+                     "traffic": args.gemm_traffic},
+        "roofline_quantize": {"bound": "hbm", "unit": "GB/s",
+                              "achieved": (q_b / (q_ms / 1000.0) / 1e9) if q_n else None,
+                              "peak": peaks["hbm_gbs"],
+                              "frac": (q_b / (q_ms / 1000.0) / 1e9 / peaks["hbm_gbs"]) if q_n else None,
+                              "launches": q_n, "time_share": q_ms / ms if ms else None,
+                              "amax_achieved_gbs": (a_b / (a_ms / 1000.0) / 1e9) if a_n else None,
+                              "amax_time_share": a_ms / ms if ms else None},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    if world == 1 and not args.no_cpu_baseline:
+        T_lo, T_hi, h_s = cpu_plan(T, h, args.ref_tokens, args.ref_hidden)
+        samples = [(Ti, cpu_oracle_step(d, h_s, Ti, seed=k)) for k, Ti in enumerate((T_lo, T_hi, T_lo, T_hi))]
+        step_s = extrapolate(samples, T, h / h_s)
+        out["cpu_baseline"] = {"value": T / step_s, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                               "sample": cpu_sample_desc(T_lo, T_hi, h_s, T, h), "est_ms_per_step": step_s * 1000.0,
+                               "tflops": flops_per_step(T, d, h) / step_s / 1e12}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="gmlp_d4096")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-tokens", type=int, default=256)
+    ap.add_argument("--ref-hidden", type=int, default=1792)
+    ap.add_argument("--gemm-traffic", type=float, default=None)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    args.config_desc = (f"GMLP fwd+bwd, {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
+                        f"d_model {cfg['d']}, hidden {cfg['h']}, FP8 e4m3/e5m2")
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+
+    if args.impl == "reference":
+        out = run_reference(args, cfg, rank, world)
+    else:
+        if world > 1:
+            import datetime
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local_rank))
+        try:
+            out = run_ours(args, cfg, rank, world, local_rank)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

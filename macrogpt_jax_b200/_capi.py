@@ -75,6 +75,9 @@ class UFP8Error(RuntimeError):
 
 _lib = None
 
+# Number of kernels this library has launched from this process (host-side count).
+launches = 0
+
 
 def load() -> ctypes.CDLL:
     """Loads libufp8.so once; raises if it is absent (no fallback path exists)."""
@@ -107,24 +110,34 @@ def check(rc: int) -> None:
         raise UFP8Error(rc, load().ufp8_last_error().decode(errors="replace"))
 
 
+def _count(k: int) -> None:
+    global launches
+    launches += k
+
+
 def amax(x_ptr: int, n: int, amax_ptr: int, stream: int) -> None:
     check(load().ufp8_amax(x_ptr, n, amax_ptr, stream))
+    _count(1 if n > 0 else 0)
 
 
 def quantize(x_ptr: int, n: int, fmt: int, amax_ptr: int, q_ptr: int, inv_ptr: int, stream: int) -> None:
     check(load().ufp8_quantize(x_ptr, n, fmt, amax_ptr, q_ptr, inv_ptr, stream))
+    _count(1)
 
 
 def amax_quant(x_ptr: int, n: int, fmt: int, q_ptr: int, amax_ptr: int, inv_ptr: int, stream: int) -> None:
     check(load().ufp8_amax_quant(x_ptr, n, fmt, q_ptr, amax_ptr, inv_ptr, stream))
+    _count(2 if n > 0 else 1)
 
 
 def cast(x_ptr: int, n: int, fmt: int, q_ptr: int, stream: int) -> None:
     check(load().ufp8_cast(x_ptr, n, fmt, q_ptr, stream))
+    _count(1 if n > 0 else 0)
 
 
 def gemm(desc: GemmDesc, stream: int) -> None:
     check(load().ufp8_gemm(ctypes.byref(desc), stream))
+    _count(1 if desc.M > 0 and desc.N > 0 else 0)
 
 
 def device_status(clear: bool = True) -> int:

@@ -20,6 +20,45 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+class KernelTimer:
+    """Optional per-launch CUDA-event timing of this module's kernels, recorded on the
+    stream each kernel is launched on.  Install with set_timer(); read after a sync."""
+
+    def __init__(self):
+        self.records = []  # (kind, start_event, end_event, work) ; work = FLOPs or bytes
+
+    def wrap(self, kind: str, work: float, fn):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        self.records.append((kind, s, e, work))
+
+    def summary(self):
+        """{kind: (launches, total_ms, total_work)}"""
+        out = {}
+        for kind, s, e, work in self.records:
+            n, ms, w = out.get(kind, (0, 0.0, 0.0))
+            out[kind] = (n + 1, ms + s.elapsed_time(e), w + work)
+        return out
+
+
+_timer: KernelTimer | None = None
+
+
+def set_timer(t: KernelTimer | None) -> None:
+    global _timer
+    _timer = t
+
+
+def _launch(kind: str, work: float, fn) -> None:
+    if _timer is None:
+        fn()
+    else:
+        _timer.wrap(kind, work, fn)
+
+
 def _check_bf16_cuda(t: torch.Tensor, name: str) -> torch.Tensor:
     if not t.is_cuda:
         raise ValueError(f"{name}: expected a CUDA tensor (this library has no CPU path)")
@@ -43,7 +82,7 @@ class Fp8Tensor:
 def amax(x: torch.Tensor) -> torch.Tensor:
     x = _check_bf16_cuda(x, "amax")
     out = torch.empty(1, dtype=torch.float32, device=x.device)
-    C.amax(x.data_ptr(), x.numel(), out.data_ptr(), _stream())
+    _launch("amax", 2.0 * x.numel(), lambda: C.amax(x.data_ptr(), x.numel(), out.data_ptr(), _stream()))
     return out
 
 
@@ -52,11 +91,13 @@ def quantize(x: torch.Tensor, fmt: int, amax_t: torch.Tensor | None = None) -> F
     x = _check_bf16_cuda(x, "quantize")
     q = torch.empty(x.shape, dtype=FP8_DTYPE[fmt], device=x.device)
     inv = torch.empty(1, dtype=torch.float32, device=x.device)
+    n = x.numel()
     if amax_t is None:
         amax_t = torch.empty(1, dtype=torch.float32, device=x.device)
-        C.amax_quant(x.data_ptr(), x.numel(), fmt, q.data_ptr(), amax_t.data_ptr(), inv.data_ptr(), _stream())
-    else:
-        C.quantize(x.data_ptr(), x.numel(), fmt, amax_t.data_ptr(), q.data_ptr(), inv.data_ptr(), _stream())
+        _launch("amax", 2.0 * n, lambda: C.amax(x.data_ptr(), n, amax_t.data_ptr(), _stream()))
+    # algorithmic bytes of the quantize pass: 2 B read + 1 B written per element
+    _launch("quantize", 3.0 * n,
+            lambda: C.quantize(x.data_ptr(), n, fmt, amax_t.data_ptr(), q.data_ptr(), inv.data_ptr(), _stream()))
     return Fp8Tensor(q, inv, amax_t)
 
 
@@ -83,7 +124,9 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
     desc.ug = ug.data_ptr() if ug is not None else None
     desc.ldug, desc.ug_batch_stride = ldug, ug_batch_stride
     desc.amax_out = amax_out.data_ptr() if amax_out is not None else None
-    C.gemm(desc, _stream())
+    n_eff = 2 * N if epilogue == C.EPI_SWIGLU else N
+    flops = 2.0 * M * n_eff * K * batch * k_batches
+    _launch("gemm", flops, lambda: C.gemm(desc, _stream()))
 
 
 # ----------------------------------------------------------------------------- Einsum

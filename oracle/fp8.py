@@ -75,17 +75,42 @@ def f32_to_fp8(x: np.ndarray, fmt: int) -> np.ndarray:
     return codes.astype(np.uint8)
 
 
+def f32_to_fp8_fast(x: np.ndarray, fmt: int) -> np.ndarray:
+    """Same codes as f32_to_fp8, computed by ml_dtypes 0.5.4's C++ cast (the reference's
+    pinned cast library) with NaN mapped to the positive pattern.  Used where the oracle is
+    timed as the CPU baseline; tests check it equals f32_to_fp8."""
+    import ml_dtypes
+
+    x = np.asarray(x, dtype=np.float32)
+    dt = ml_dtypes.float8_e4m3fn if fmt == E4M3 else ml_dtypes.float8_e5m2
+    with np.errstate(invalid="ignore", over="ignore"):
+        codes = x.astype(dt).view(np.uint8)
+    nan = np.isnan(x)
+    if nan.any():
+        codes = np.where(nan, np.uint8(0x7F if fmt == E4M3 else 0x7E), codes)
+    return codes
+
+
 # ----------------------------------------------------------------------------- bf16
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
-    """Round-to-nearest-even f32 -> bf16 (NaN stays NaN)."""
-    b = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    rounded = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
-    nan = np.isnan(np.asarray(x, dtype=np.float32))
-    return np.where(nan, ((b >> 16) | 0x40).astype(np.uint16), rounded).astype(np.uint16)
+    """Round-to-nearest-even f32 -> bf16 (NaN stays NaN, quieted).
+
+    For every non-NaN pattern b (at most 0xFF800000), b + 0x7FFF + 1 stays below 2**32,
+    so the rounding add is done in uint32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = x.view(np.uint32)
+    r = (b >> 16) & np.uint32(1)
+    r += b
+    r += np.uint32(0x7FFF)
+    out = (r >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    if nan.any():
+        out[nan] = ((b[nan] >> 16) | np.uint32(0x40)).astype(np.uint16)
+    return out
 
 
 def round_bf16(x: np.ndarray) -> np.ndarray:
@@ -110,7 +135,7 @@ def scale_from_amax(amax: np.float32, fmt: int) -> np.float32:
         return np.float32(FMAX[fmt]) / np.float32(amax)
 
 
-def quantize_bits(x_bits: np.ndarray, fmt: int, amax: np.float32 | None = None):
+def quantize_bits(x_bits: np.ndarray, fmt: int, amax: np.float32 | None = None, fast: bool = False):
     """Per-tensor current scaling of a bf16 tensor given as bit patterns.
 
     Returns (codes uint8, amax f32, inv_scale f32)."""
@@ -120,4 +145,5 @@ def quantize_bits(x_bits: np.ndarray, fmt: int, amax: np.float32 | None = None):
     with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
         p = bf16_bits_to_f32(x_bits) * s  # float32 * float32, IEEE round to nearest
         inv = np.float32(1.0) / s
-    return f32_to_fp8(p, fmt), np.float32(amax), np.float32(inv)
+    cast = f32_to_fp8_fast if fast else f32_to_fp8
+    return cast(p, fmt), np.float32(amax), np.float32(inv)

@@ -25,11 +25,21 @@ class Q:
     inv: np.float32
 
     def deq(self, dtype=np.float64) -> np.ndarray:
-        return fp8_to_f64(self.codes, self.fmt).astype(dtype, copy=False)
+        """Exact values of the codes (memoised per dtype: weights are reused in a step)."""
+        cache = self.__dict__.setdefault("_deq", {})
+        key = np.dtype(dtype).str
+        if key not in cache:
+            cache[key] = fp8_to_f64(self.codes, self.fmt).astype(dtype, copy=False)
+        return cache[key]
+
+
+# Module-wide switch: True makes every quantisation use the ml_dtypes-backed cast (same
+# codes, verified by the tests) so that the oracle can be timed as the CPU baseline.
+FAST_CAST = False
 
 
 def quant(x_bits: np.ndarray, fmt: int, amax: np.float32 | None = None) -> Q:
-    codes, a, inv = quantize_bits(x_bits, fmt, amax)
+    codes, a, inv = quantize_bits(x_bits, fmt, amax, fast=FAST_CAST)
     return Q(codes, fmt, a, inv)
 
 
@@ -96,17 +106,18 @@ def dswiglu(dh: np.ndarray, u_bits: np.ndarray, g_bits: np.ndarray):
     return f32_to_bf16_bits(du), f32_to_bf16_bits(dg)
 
 
-def gmlp_forward(x_bits: np.ndarray, wf_bits: np.ndarray, wd_bits: np.ndarray, acc=np.float64):
+def gmlp_forward(x_bits: np.ndarray, wf_bits, wd_bits, acc=np.float64):
     """GMLP.__call__ (ueaj/model/mlp.py:100-115) with both Einsums in FP8.
 
-    x [T, d], wf [2, d, h] (index 0 = up, 1 = gate), wd [h, d]; all bf16 bit patterns."""
+    x [T, d], wf [2, d, h] (index 0 = up, 1 = gate), wd [h, d]; all bf16 bit patterns.
+    wf / wd may also be given already quantised (Q), as one training step reuses them."""
     qx = quant(x_bits, E4M3)
-    qwf = quant(wf_bits, E4M3)
+    qwf = wf_bits if isinstance(wf_bits, Q) else quant(wf_bits, E4M3)
     acc_ug = np.einsum("td,idh->ith", qx.deq(acc), qwf.deq(acc), optimize=True)
     ug = f32_to_bf16_bits(_scale_out(acc_ug, alpha_of(qx, qwf)))
     hid = swiglu(ug[0], ug[1])
     qh = quant(hid, E4M3, amax_bits(hid))
-    qwd = quant(wd_bits, E4M3)
+    qwd = wd_bits if isinstance(wd_bits, Q) else quant(wd_bits, E4M3)
     y = gemm(qh, qwd, "th", "hd", "td", acc)
     return y, dict(qx=qx, qwf=qwf, ug=ug, h=hid, qh=qh, qwd=qwd)
 
