@@ -145,6 +145,14 @@ int ufp8_device_status(int* status, int clear);
 /* Number of CTAs the persistent GEMM launches (0 = one per SM, the default). */
 int ufp8_set_gemm_ctas(int ctas);
 
+/* GEMM kernel variant for this process: UFP8_GEMM_AUTO (default: the CTA-pair kernel),
+ * UFP8_GEMM_SINGLE_CTA (128 x 256 tiles, one CTA each) or UFP8_GEMM_CTA_PAIR (256 x 256
+ * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2). */
+#define UFP8_GEMM_AUTO 0
+#define UFP8_GEMM_SINGLE_CTA 1
+#define UFP8_GEMM_CTA_PAIR 2
+int ufp8_set_gemm_variant(int variant);
+
 #ifdef __cplusplus
 }
 #endif

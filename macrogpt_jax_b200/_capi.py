@@ -17,6 +17,7 @@ E4M3, E5M2 = 0, 1
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU = 0, 1, 2
+GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR = 0, 1, 2
 
 EXPORTED_SYMBOLS = (
     "ufp8_last_error",
@@ -28,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "ufp8_gemm",
     "ufp8_device_status",
     "ufp8_set_gemm_ctas",
+    "ufp8_set_gemm_variant",
 )
 
 
@@ -98,8 +100,9 @@ def load() -> ctypes.CDLL:
     lib.ufp8_gemm.argtypes = [ctypes.POINTER(GemmDesc), vp]
     lib.ufp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_int), i32]
     lib.ufp8_set_gemm_ctas.argtypes = [i32]
+    lib.ufp8_set_gemm_variant.argtypes = [i32]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
-                 "ufp8_set_gemm_ctas"):
+                 "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -148,3 +151,7 @@ def device_status(clear: bool = True) -> int:
 
 def set_gemm_ctas(ctas: int) -> None:
     check(load().ufp8_set_gemm_ctas(ctas))
+
+
+def set_gemm_variant(variant: int) -> None:
+    check(load().ufp8_set_gemm_variant(variant))

@@ -60,6 +60,7 @@ int device_info(DeviceInfo** out) {
 
 namespace {
 int g_gemm_ctas = 0;
+int g_gemm_variant = UFP8_GEMM_AUTO;
 
 bool is_fmt(int fmt) { return fmt == UFP8_E4M3 || fmt == UFP8_E5M2; }
 }  // namespace
@@ -121,7 +122,7 @@ int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream) {
   if (!desc) return set_error(UFP8_ERR_INVALID, "ufp8_gemm: null descriptor");
   DeviceInfo* dev;
   if (int rc = device_info(&dev)) return rc;
-  return launch_gemm(*desc, reinterpret_cast<cudaStream_t>(stream), *dev, g_gemm_ctas);
+  return launch_gemm(*desc, reinterpret_cast<cudaStream_t>(stream), *dev, g_gemm_ctas, g_gemm_variant);
 }
 
 int ufp8_device_status(int* status, int clear) {
@@ -134,6 +135,13 @@ int ufp8_device_status(int* status, int clear) {
     return cuda_error(e, "read status word");
   if (clear && (e = cudaMemset(dev->status_word, 0, sizeof(int))) != cudaSuccess)
     return cuda_error(e, "clear status word");
+  return UFP8_OK;
+}
+
+int ufp8_set_gemm_variant(int variant) {
+  if (variant != UFP8_GEMM_AUTO && variant != UFP8_GEMM_SINGLE_CTA && variant != UFP8_GEMM_CTA_PAIR)
+    return set_error(UFP8_ERR_INVALID, "ufp8_set_gemm_variant: unknown variant %d", variant);
+  g_gemm_variant = variant;
   return UFP8_OK;
 }
 

@@ -389,6 +389,397 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicOr(args.status, UFP8_STATUS_WAIT_TIMEOUT);
 }
 
+// ============================================================================= CTA-pair kernel
+// Same contraction with 2-CTA MMAs: a cluster of two CTAs computes a 256 x 256 tile, each CTA
+// holding 128 rows of A and 128 rows (N) of B per stage, so a CTA streams 32 KiB per 128-deep
+// k-step instead of 48 KiB and six stages fit in shared memory.  The even CTA's MMA thread
+// issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) and multicasts its commits to
+// both CTAs' barriers; both CTAs' loads complete on the even CTA's "full" barrier.  Eight
+// epilogue warps per CTA (two per TMEM lane quadrant, splitting the columns).
+constexpr int kPStages = 7;
+constexpr int kPHalfBytes = 128 * kBK;            // 16 KiB: 128 rows x 128 B
+constexpr int kPStageBytes = 2 * kPHalfBytes;     // A half + B half
+constexpr int kPEpiWarps = 8;
+constexpr int kPThreads = 64 + 32 * kPEpiWarps;   // 320
+constexpr int kPSmemBytes = kPStages * kPStageBytes + kBarrierBytes + 1024;
+
+// Stores 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]).
+__device__ __forceinline__ void store_bf16x32_packed(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
+                                                     bool vec) {
+  if (vec && valid >= 32) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  } else {
+    uint16_t* q = reinterpret_cast<uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) q[j] = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu));
+  }
+}
+
+// Stores 16 consecutive bf16 values packed two per word.
+__device__ __forceinline__ void store_bf16x16_packed(__nv_bfloat16* p, const uint32_t (&w)[8], int valid,
+                                                     bool vec) {
+  if (vec && valid >= 16) {
+    uint4* q = reinterpret_cast<uint4*>(p);
+    q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  } else {
+    uint16_t* q = reinterpret_cast<uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (j < valid) q[j] = static_cast<uint16_t>((j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu));
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  return bf16_bits(lo) | (bf16_bits(hi) << 16);
+}
+
+// Loads 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]);
+// elements at or past `valid` read as zero.
+__device__ __forceinline__ void load_bf16x32_packed(const __nv_bfloat16* p, uint32_t (&w)[16], int valid,
+                                                    bool vec) {
+  if (vec && valid >= 32) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 t = q[i];
+      w[4 * i] = t.x;
+      w[4 * i + 1] = t.y;
+      w[4 * i + 2] = t.z;
+      w[4 * i + 3] = t.w;
+    }
+  } else {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = (2 * j < valid) ? q[2 * j] : 0u;
+      const uint32_t hi = (2 * j + 1 < valid) ? q[2 * j + 1] : 0u;
+      w[j] = lo | (hi << 16);
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[16], int j) {
+  return (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPStages * kPStageBytes);
+  uint64_t* empty = full + kPStages;
+  uint64_t* tfull = empty + kPStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kPEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = args.tiles_m * args.tiles_n * args.batch;
+  const int total_k = args.ksteps * args.k_batches;
+  const bool swiglu = args.mode == UFP8_EPI_SWIGLU;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_parity = 0;
+      for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters) {
+        int g, mb, nb;
+        map_tile(tile, args, g, mb, nb);
+        const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        for (int ks = 0; ks < total_k; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+          const int kb = ks / args.ksteps;
+          const int k0 = (ks - kb * args.ksteps) * kBK;
+          uint8_t* sa = smem + stage * kPStageBytes;
+          uint8_t* sb = sa + kPHalfBytes;
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage], 2 * kPStageBytes);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          if (args.a_major == UFP8_K_MAJOR)
+            tma_load_3d_pair(sa, &tmA, bar, k0, row0, az);
+          else
+            tma_load_3d_pair(sa, &tmA, bar, row0, k0, az);
+          int n0, bz;
+          if (swiglu) {
+            n0 = nb * 128;
+            bz = static_cast<int>(rank);
+          } else {
+            n0 = nb * kBN + static_cast<int>(rank) * 128;
+            bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          }
+          if (args.b_major == UFP8_K_MAJOR)
+            tma_load_3d_pair(sb, &tmB, bar, k0, n0, bz);
+          else
+            tma_load_3d_pair(sb, &tmB, bar, n0, k0, bz);
+          if (++stage == kPStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag && leader) {
+        // Both CTAs' loads for a stage complete on the leader's barrier: wait for every
+        // armed stage so that no load is still in flight when the cluster exits.
+        volatile int never = 0;
+        for (int s = 0; s < kPStages; ++s)
+          if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters, ++local) {
+        const int buf = local & 1;
+        const uint32_t tphase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tphase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
+        bool ok = true;
+        for (int ks = 0; ks < total_k; ++ks) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kPStageBytes);
+          const uint32_t sb = sa + kPHalfBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            const uint64_t adesc = args.a_major == UFP8_K_MAJOR ? make_sdesc_sw128(sa + kk * 32, 16, 1024)
+                                                                : make_sdesc_sw128(sa + kk * 32 * 128, kPHalfBytes, 1024);
+            const uint64_t bdesc = args.b_major == UFP8_K_MAJOR ? make_sdesc_sw128(sb + kk * 32, 16, 1024)
+                                                                : make_sdesc_sw128(sb + kk * 32 * 128, kPHalfBytes, 1024);
+            umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kPStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[buf], 0x3);
+      }
+      umma_commit_pair(drain, 0x1);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int e = warp - 2;
+    const int quad = warp & 3;   // TMEM lanes this warp may read: [32*quad, 32*quad+32)
+    const int chalf = e >> 2;    // which half of the tile's columns this warp handles
+    const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
+    const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
+    const bool vec = args.vec_ok != 0;
+    const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    uint32_t amax = 0;
+    int local = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
+      const int buf = local & 1;
+      const uint32_t tphase = (local >> 1) & 1;
+      bool ok = mbar_wait(&tfull[buf], tphase, abort_flag);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      int g, mb, nb;
+      map_tile(tile, args, g, mb, nb);
+      const int row = mb * 2 * kBM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
+
+      if (args.mode == UFP8_EPI_STORE) {
+#pragma unroll 1
+        for (int c = chalf * 128; c < chalf * 128 + 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = nb * kBN + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            if (args.d_f32) {
+              float* p = static_cast<float*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
+              if (vec && valid >= 32) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  reinterpret_cast<float4*>(p)[i] =
+                      make_float4(__uint_as_float(r[4 * i]) * alpha, __uint_as_float(r[4 * i + 1]) * alpha,
+                                  __uint_as_float(r[4 * i + 2]) * alpha, __uint_as_float(r[4 * i + 3]) * alpha);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < valid) p[j] = __uint_as_float(r[j]) * alpha;
+              }
+            } else {
+              uint32_t o[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
+              __nv_bfloat16* p = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
+              store_bf16x32_packed(p, o, valid, vec);
+            }
+          }
+        }
+      } else if (args.mode == UFP8_EPI_SWIGLU) {
+        // TMEM columns [0,128) hold up, [128,256) hold gate for hidden units nb*128 + c.
+#pragma unroll 1
+        for (int c = chalf * 64; c < chalf * 64 + 64; c += 16) {
+          uint32_t ru[16], rg[16];
+          tmem_ld_32x32b_x16(tbase + c, ru);
+          tmem_ld_32x32b_x16(tbase + 128 + c, rg);
+          tmem_ld_wait();
+          const int col0 = nb * 128 + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            uint32_t ou[8], og[8], oh[8];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const uint32_t ub = bf16_bits(__uint_as_float(ru[j]) * alpha);
+              const uint32_t gb = bf16_bits(__uint_as_float(rg[j]) * alpha);
+              const float u = bf16_to_f(ub), gt = bf16_to_f(gb);
+              const uint32_t hb = bf16_bits(u * (gt * sigmoidf_(gt)));
+              if (j & 1) {
+                ou[j >> 1] |= ub << 16;
+                og[j >> 1] |= gb << 16;
+                oh[j >> 1] |= hb << 16;
+              } else {
+                ou[j >> 1] = ub;
+                og[j >> 1] = gb;
+                oh[j >> 1] = hb;
+              }
+              if (j < valid) amax = max(amax, hb & 0x7FFFu);
+            }
+            __nv_bfloat16* pu = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
+            store_bf16x16_packed(pu, ou, valid, vec);
+            store_bf16x16_packed(pu + args.d_bstride, og, valid, vec);
+            store_bf16x16_packed(args.h + row * args.ldh + col0, oh, valid, vec);
+          }
+        }
+      } else {  // UFP8_EPI_DSWIGLU: U / G of the next 32 columns are loaded while this chunk computes
+        const int c_begin = chalf * 128, c_end = c_begin + 128;
+        const __nv_bfloat16* ug_row = args.ug + row * args.ldug;
+        uint32_t cu[16], cg[16];
+        {
+          const int col0 = nb * kBN + c_begin;
+          const int valid = row_ok ? args.N - col0 : 0;
+          if (valid > 0) {
+            load_bf16x32_packed(ug_row + col0, cu, valid, vec);
+            load_bf16x32_packed(ug_row + args.ug_bstride + col0, cg, valid, vec);
+          }
+        }
+#pragma unroll 1
+        for (int c = c_begin; c < c_end; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c, r);
+          uint32_t nu[16], ng[16];
+          const int ncol0 = nb * kBN + c + 32;
+          const int nvalid = (row_ok && c + 32 < c_end) ? args.N - ncol0 : 0;
+          if (nvalid > 0) {
+            load_bf16x32_packed(ug_row + ncol0, nu, nvalid, vec);
+            load_bf16x32_packed(ug_row + args.ug_bstride + ncol0, ng, nvalid, vec);
+          }
+          tmem_ld_wait();
+          const int col0 = nb * kBN + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            uint32_t odu[16], odg[16];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float dh = bf16_round(__uint_as_float(r[j]) * alpha);
+              const float u = bf16_to_f(half_of(cu, j)), gt = bf16_to_f(half_of(cg, j));
+              const float sg = sigmoidf_(gt);
+              const uint32_t dub = bf16_bits(dh * (gt * sg));
+              const uint32_t dgb = bf16_bits((dh * u) * (sg * (1.0f + gt * (1.0f - sg))));
+              if (j & 1) {
+                odu[j >> 1] |= dub << 16;
+                odg[j >> 1] |= dgb << 16;
+              } else {
+                odu[j >> 1] = dub;
+                odg[j >> 1] = dgb;
+              }
+              if (j < valid) amax = max(amax, max(dub & 0x7FFFu, dgb & 0x7FFFu));
+            }
+            __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
+            store_bf16x32_packed(pd, odu, valid, vec);
+            store_bf16x32_packed(pd + args.d_bstride, odg, valid, vec);
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            cu[i] = nu[i];
+            cg[i] = ng[i];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader0 + static_cast<uint32_t>(buf * sizeof(uint64_t)));
+    }
+    if (args.amax_bits != nullptr) {
+      amax = __reduce_max_sync(0xFFFFFFFFu, amax);
+      if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(args.status, UFP8_STATUS_WAIT_TIMEOUT);
+}
+
 // Writes zeros to every output of an empty-K contraction (K == 0).
 __global__ void zero_outputs_kernel(GemmArgs a) {
   const long long total = static_cast<long long>(a.batch) * a.M * a.N;
@@ -478,7 +869,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& dev, int ctas_override) {
+int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& dev, int ctas_override,
+                int variant) {
   if (d.M < 0 || d.N < 0 || d.K < 0) return set_error(UFP8_ERR_INVALID, "negative GEMM extent");
   if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
   if (d.batch > 1 && d.k_batches > 1)
@@ -545,7 +937,9 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.b_bcast = !swiglu && d.b.batch_count <= 1 && d.k_batches == 1;
   a.inv_a = d.a.inv_scale;
   a.inv_b = d.b.inv_scale;
-  a.tiles_m = static_cast<int>((d.M + kBM - 1) / kBM);
+  const bool pair = variant != UFP8_GEMM_SINGLE_CTA;
+  const int bm = pair ? 2 * kBM : kBM;
+  a.tiles_m = static_cast<int>((d.M + bm - 1) / bm);
   const int bn = swiglu ? 128 : kBN;
   a.tiles_n = static_cast<int>((d.N + bn - 1) / bn);
   a.ksteps = static_cast<int>((d.K + kBK - 1) / kBK);
@@ -555,7 +949,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
             | (static_cast<uint32_t>(d.a.major) << 15)      // A major
             | (static_cast<uint32_t>(d.b.major) << 16)      // B major
             | (static_cast<uint32_t>(kBN >> 3) << 17)       // N = 256
-            | (static_cast<uint32_t>(kBM >> 4) << 24);      // M = 128
+            | (static_cast<uint32_t>(bm >> 4) << 24);       // M = 128 (one CTA) or 256 (CTA pair)
 
   const int esz = a.d_f32 ? 4 : 2;
   bool vec = aligned16(d.d) && (d.ldd * esz) % 16 == 0 && (d.d_batch_stride * esz) % 16 == 0;
@@ -572,14 +966,38 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   static thread_local int attr_device = -1;
   if (attr_device != dev.device) {
     e = cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
-  if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
-  gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);
+  if (pair) {
+    static thread_local int occ_device = -1, max_clusters = 0;
+    if (occ_device != dev.device) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(kPThreads, 1, 1);
+      cfg.dynamicSmemBytes = kPSmemBytes;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, gemm_fp8_pair_kernel, &cfg);
+      if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
+      if (n < 1) return set_error(UFP8_ERR_DEVICE, "no CTA pair of the GEMM kernel fits on this device");
+      max_clusters = n;
+      occ_device = dev.device;
+    }
+    // Persistent grid: no more clusters than can be resident at once.
+    if (ctas_override <= 0 || ctas > 2 * max_clusters) ctas = 2 * max_clusters;
+    long long clusters = ctas / 2;
+    if (clusters < 1) clusters = 1;
+    if (num_tiles < clusters) clusters = num_tiles;
+    gemm_fp8_pair_kernel<<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytes, stream>>>(tmA, tmB, a);
+  } else {
+    if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
+    gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);
+  }
   e = cudaGetLastError();
   return e == cudaSuccess ? UFP8_OK : cuda_error(e, "gemm kernel launch");
 }

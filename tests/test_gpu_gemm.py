@@ -14,6 +14,15 @@ from helpers import bf16_bits_to_f64, compare, torch_bf16_to_bits, bits_to_torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=[1, 2], ids=["single_cta", "cta_pair"], autouse=True)
+def variant(request, cuda):
+    """Runs every test with the one-CTA kernel and with the CTA-pair kernel."""
+    from macrogpt_jax_b200 import _capi
+    _capi.set_gemm_variant(request.param)
+    yield request.param
+    _capi.set_gemm_variant(0)
+
+
 def _upload(q: op.Q, cuda, transpose=False):
     import torch
     from macrogpt_jax_b200 import ops
@@ -48,7 +57,8 @@ def test_gemm_layouts(cuda, a_major, b_major, fmts):
     compare(bf16_bits_to_f64(torch_bf16_to_bits(d)), bf16_bits_to_f64(ref))
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 16, 16), (130, 300, 48), (257, 129, 144), (128, 256, 128), (1000, 40, 1040)])
+@pytest.mark.parametrize("M,N,K", [(1, 16, 16), (130, 300, 48), (257, 129, 144), (128, 256, 128), (1000, 40, 1040),
+                                   (384, 512, 256), (600, 700, 96)])
 def test_gemm_ragged(cuda, M, N, K):
     """Tails in M, N and K (K-major operands; pitches padded to 16 bytes as TMA needs)."""
     import torch
@@ -108,7 +118,7 @@ def test_gemm_k_zero(cuda):
     assert (d == 0).all()
 
 
-@pytest.mark.parametrize("T,d,h", [(256, 128, 256), (200, 256, 384), (512, 384, 640)])
+@pytest.mark.parametrize("T,d,h", [(256, 128, 256), (200, 256, 384), (512, 384, 640), (300, 128, 208)])
 def test_swiglu_epilogue(cuda, T, d, h):
     import torch
     from macrogpt_jax_b200 import ops
@@ -133,7 +143,7 @@ def test_swiglu_epilogue(cuda, T, d, h):
     assert amax.item() == float(ofp8.amax_bits(got_h))
 
 
-@pytest.mark.parametrize("T,d,h", [(256, 128, 256), (200, 256, 384)])
+@pytest.mark.parametrize("T,d,h", [(256, 128, 256), (200, 256, 384), (520, 256, 464)])
 def test_dswiglu_epilogue(cuda, T, d, h):
     import torch
     from macrogpt_jax_b200 import ops
@@ -153,6 +163,21 @@ def test_dswiglu_epilogue(cuda, T, d, h):
     compare(bf16_bits_to_f64(got[0]), bf16_bits_to_f64(du))
     compare(bf16_bits_to_f64(got[1]), bf16_bits_to_f64(dg))
     assert amax.item() == float(ofp8.amax_bits(got))
+
+
+def test_many_tiles(cuda):
+    """More tiles than resident CTAs / clusters (several persistent passes, both TMEM buffers)."""
+    import torch
+    from macrogpt_jax_b200 import ops
+    rng = np.random.default_rng(9)
+    M, N, K = 4096, 2560, 256
+    qa = _rand_q(rng, (M, K), 0)
+    qb = _rand_q(rng, (N, K), 0)
+    ta, tb = _upload(qa, cuda), _upload(qb, cuda)
+    d = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+    ops.gemm(ops.operand(ta, 0, K), ops.operand(tb, 0, K), M, N, K, d, N)
+    ref = op.gemm(qa, qb, "mk", "nk", "mn")
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(d)), bf16_bits_to_f64(ref))
 
 
 def test_device_status_clean(cuda):
