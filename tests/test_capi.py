@@ -1,0 +1,78 @@
+"""libufp8.so on a machine without a GPU: it loads, exports every entry point include/ufp8.h
+declares, and rejects bad requests on the host with an error code and message (no call
+here reaches a kernel)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from macrogpt_jax_b200 import _capi as C
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ufp8.h"
+
+
+def _declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(ufp8_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_header_symbols():
+    lib = C.load()
+    declared = _declared()
+    assert declared, "no declarations parsed from include/ufp8.h"
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in ufp8.h but not exported"
+    assert sorted(C.EXPORTED_SYMBOLS) == declared
+
+
+def test_header_constants_match_binding():
+    text = HEADER.read_text()
+    consts = dict(re.findall(r"#define (UFP8_[A-Z0-9_]+) \(?(-?\d+)\)?", text))
+    assert int(consts["UFP8_OK"]) == C.OK
+    assert int(consts["UFP8_ERR_INVALID"]) == C.ERR_INVALID
+    assert int(consts["UFP8_ERR_ALIGN"]) == C.ERR_ALIGN
+    assert (int(consts["UFP8_E4M3"]), int(consts["UFP8_E5M2"])) == (C.E4M3, C.E5M2)
+    assert (int(consts["UFP8_K_MAJOR"]), int(consts["UFP8_MN_MAJOR"])) == (C.K_MAJOR, C.MN_MAJOR)
+    assert (int(consts["UFP8_EPI_STORE"]), int(consts["UFP8_EPI_SWIGLU"]), int(consts["UFP8_EPI_DSWIGLU"])) == \
+        (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU)
+    assert int(consts["UFP8_ABI_VERSION"]) == C.load().ufp8_abi_version()
+
+
+def test_struct_layout_matches_header():
+    """Sizes and offsets as gcc lays out ufp8_operand / ufp8_gemm_desc on x86-64."""
+    assert ctypes.sizeof(C.Operand) == 48
+    assert ctypes.sizeof(C.GemmDesc) == 208
+    assert (C.GemmDesc.a.offset, C.GemmDesc.b.offset, C.GemmDesc.d.offset, C.GemmDesc.amax_out.offset) == \
+        (32, 80, 128, 200)
+
+
+@pytest.mark.parametrize("call,code,msg", [
+    (lambda L: L.ufp8_gemm(None, None), C.ERR_INVALID, "null descriptor"),
+    (lambda L: L.ufp8_amax(None, -1, None, None), C.ERR_INVALID, "n < 0"),
+    (lambda L: L.ufp8_quantize(None, 4, 7, None, None, None, None), C.ERR_INVALID, "fmt 7"),
+    (lambda L: L.ufp8_amax_quant(None, 4, 3, None, None, None, None), C.ERR_INVALID, "fmt 3"),
+    (lambda L: L.ufp8_cast(None, -5, 0, None, None), C.ERR_INVALID, "n < 0"),
+    (lambda L: L.ufp8_set_gemm_variant(9), C.ERR_INVALID, "unknown variant"),
+    (lambda L: L.ufp8_set_gemm_ctas(-2), C.ERR_INVALID, "ctas < 0"),
+    (lambda L: L.ufp8_device_status(None, 0), C.ERR_INVALID, "null pointer"),
+])
+def test_host_validation_errors(call, code, msg):
+    lib = C.load()
+    assert call(lib) == code
+    assert msg in lib.ufp8_last_error().decode()
+
+
+def test_python_wrapper_raises():
+    with pytest.raises(C.UFP8Error) as e:
+        C.set_gemm_variant(5)
+    assert e.value.code == C.ERR_INVALID
+    C.set_gemm_variant(0)
+
+
+def test_ops_refuse_cpu_tensors():
+    """There is no CPU path: the ops raise instead of computing on the host."""
+    import torch
+    from macrogpt_jax_b200 import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.quantize(torch.zeros(4, dtype=torch.bfloat16), C.E4M3)
