@@ -4,7 +4,7 @@
 //
 // One CTA per SM (192 threads, ~193 KB shared memory, all 512 TMEM columns):
 //   warp 0      TMA producer: 4-stage ring of {A 128x128, B 256x128} fp8 tiles in
-//               128-byte-swizzled shared memory (plain tiled loads, never multicast);
+//               128-byte-swizzled shared memory (plain per-CTA tiled loads);
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma.cta_group::1.kind::f8f6f4
 //               (M=128, N=256, K=32) into a double-buffered fp32 TMEM accumulator
 //               (2 x 256 columns) and frees ring slots with tcgen05.commit;
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Same contraction with 2-CTA MMAs: a cluster of two CTAs computes a 256 x 256 tile, each CTA
 // holding 128 rows of A and 128 rows (N) of B per stage, so a CTA streams 32 KiB per 128-deep
 // k-step instead of 48 KiB and six stages fit in shared memory.  The even CTA's MMA thread
-// issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) and multicasts its commits to
+// issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) and signals its commits to
 // both CTAs' barriers; both CTAs' loads complete on the even CTA's "full" barrier.  Eight
 // epilogue warps per CTA (two per TMEM lane quadrant, splitting the columns).
 constexpr int kPStages = 7;

@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the FP8 contraction kernels use:
-// mbarriers, TMA tensor loads (no multicast anywhere), tcgen05 MMA / TMEM, and a
+// mbarriers, plain per-CTA TMA tensor loads, tcgen05 MMA / TMEM, and a
 // %globaltimer-bounded wait so that no kernel in this library can spin forever.
 #pragma once
 #include <cstdint>
@@ -187,7 +187,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 }
 
 // 3-D tiled load into this CTA's shared memory whose completion is signalled on an mbarrier
-// of either CTA of the pair (`bar_cluster` is a shared::cluster address).  No multicast.
+// of either CTA of the pair (`bar_cluster` is a shared::cluster address).
 __device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster,
                                                  int x, int y, int z) {
   asm volatile(

@@ -36,24 +36,13 @@ def build(T, d, h, dev):
     qdy = _fp8((T, d), C.E5M2, dev, gen, 1e-3)
     qdug = _fp8((2, T, h), C.E5M2, dev, gen, 1e-3)
     ug = torch.randn((2, T, h), generator=gen, device=dev).to(torch.bfloat16)
-    bf = lambda *s: torch.empty(s, dtype=torch.bfloat16, device=dev)  # noqa: E731
-    ug_out, hid, dug = bf(2, T, h), bf(T, h), bf(2, T, h)
-    y, dx, dwd, dwf = bf(T, d), bf(T, d), bf(h, d), bf(2, d, h)
-    amax = torch.empty(1, dtype=torch.float32, device=dev)
-    op = ops.operand
     g = {
-        "F1": (4.0 * T * d * h, lambda: ops.gemm(op(qx, C.K_MAJOR, d), op(qwf, C.MN_MAJOR, h, d * h, 2), T, h, d,
-                                                 ug_out, h, T * h, epilogue=C.EPI_SWIGLU, h=hid, ldh=h,
-                                                 amax_out=amax)),
-        "F2": (2.0 * T * d * h, lambda: ops.gemm(op(qh, C.K_MAJOR, h), op(qwd, C.MN_MAJOR, d), T, d, h, y, d)),
-        "B2": (2.0 * T * d * h, lambda: ops.gemm(op(qdy, C.K_MAJOR, d), op(qwd, C.K_MAJOR, d), T, h, d, dug, h,
-                                                 T * h, epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h,
-                                                 ug_batch_stride=T * h, amax_out=amax)),
-        "B1": (2.0 * T * d * h, lambda: ops.gemm(op(qh, C.MN_MAJOR, h), op(qdy, C.MN_MAJOR, d), h, d, T, dwd, d)),
-        "B4": (4.0 * T * d * h, lambda: ops.gemm(op(qdug, C.K_MAJOR, h, T * h, 2), op(qwf, C.K_MAJOR, h, d * h, 2),
-                                                 T, d, h, dx, d, k_batches=2)),
-        "B3": (4.0 * T * d * h, lambda: ops.gemm(op(qx, C.MN_MAJOR, d), op(qdug, C.MN_MAJOR, h, T * h, 2), d, h, T,
-                                                 dwf, h, d * h, batch=2)),
+        "F1": (4.0 * T * d * h, lambda: ops.gmlp_f1(qx, qwf)),
+        "F2": (2.0 * T * d * h, lambda: ops.gmlp_f2(qh, qwd)),
+        "B2": (2.0 * T * d * h, lambda: ops.gmlp_b2(qdy, qwd, ug)),
+        "B1": (2.0 * T * d * h, lambda: ops.gmlp_b1(qh, qdy)),
+        "B4": (4.0 * T * d * h, lambda: ops.gmlp_b4(qdug, qwf)),
+        "B3": (4.0 * T * d * h, lambda: ops.gmlp_b3(qx, qdug)),
     }
     return g
 

@@ -177,6 +177,69 @@ def einsum_backward(plan: EinsumPlan, dout: torch.Tensor, saved, bwd_fmt: int, n
 
 
 # ----------------------------------------------------------------------------- GMLP
+# The six contractions of one GMLP step (ueaj/model/mlp.py:100-115 and the backward JAX
+# derives for it).  Shapes: x [T, d], Wf [2, d, h] (index 0 = up, 1 = gate), Wd [h, d].
+def gmlp_f1(qx: Fp8Tensor, qwf: Fp8Tensor):
+    """[U, G] = x Wf with H = U * swish(G) and max|H| from the epilogue."""
+    T, d = qx.q.shape
+    h = qwf.q.shape[2]
+    dev = qx.q.device
+    ug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
+    hid = torch.empty((T, h), dtype=torch.bfloat16, device=dev)
+    amax_h = torch.empty(1, dtype=torch.float32, device=dev)
+    gemm(operand(qx, C.K_MAJOR, d), operand(qwf, C.MN_MAJOR, h, d * h, 2), T, h, d, ug, h, T * h,
+         epilogue=C.EPI_SWIGLU, h=hid, ldh=h, amax_out=amax_h)
+    return ug, hid, amax_h
+
+
+def gmlp_f2(qh: Fp8Tensor, qwd: Fp8Tensor) -> torch.Tensor:
+    """y = H Wd."""
+    T, h = qh.q.shape
+    d = qwd.q.shape[1]
+    y = torch.empty((T, d), dtype=torch.bfloat16, device=qh.q.device)
+    gemm(operand(qh, C.K_MAJOR, h), operand(qwd, C.MN_MAJOR, d), T, d, h, y, d)
+    return y
+
+
+def gmlp_b2(qdy: Fp8Tensor, qwd: Fp8Tensor, ug: torch.Tensor):
+    """dH = dY Wd^T fused with the gating backward -> [dU, dG] and max|dU, dG|."""
+    T, d = qdy.q.shape
+    h = qwd.q.shape[0]
+    dev = qdy.q.device
+    dug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
+    amax_dug = torch.empty(1, dtype=torch.float32, device=dev)
+    gemm(operand(qdy, C.K_MAJOR, d), operand(qwd, C.K_MAJOR, d), T, h, d, dug, h, T * h,
+         epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug)
+    return dug, amax_dug
+
+
+def gmlp_b1(qh: Fp8Tensor, qdy: Fp8Tensor) -> torch.Tensor:
+    """dWd = H^T dY (contraction over tokens; MN-major operands, no transposed copies)."""
+    T, h = qh.q.shape
+    d = qdy.q.shape[1]
+    dwd = torch.empty((h, d), dtype=torch.bfloat16, device=qh.q.device)
+    gemm(operand(qh, C.MN_MAJOR, h), operand(qdy, C.MN_MAJOR, d), h, d, T, dwd, d)
+    return dwd
+
+
+def gmlp_b4(qdug: Fp8Tensor, qwf: Fp8Tensor) -> torch.Tensor:
+    """dx = sum_i dUG[i] Wf[i]^T (K concatenated over [up, gate])."""
+    _, T, h = qdug.q.shape
+    d = qwf.q.shape[1]
+    dx = torch.empty((T, d), dtype=torch.bfloat16, device=qdug.q.device)
+    gemm(operand(qdug, C.K_MAJOR, h, T * h, 2), operand(qwf, C.K_MAJOR, h, d * h, 2), T, d, h, dx, d, k_batches=2)
+    return dx
+
+
+def gmlp_b3(qx: Fp8Tensor, qdug: Fp8Tensor) -> torch.Tensor:
+    """dWf[i] = x^T dUG[i]."""
+    T, d = qx.q.shape
+    h = qdug.q.shape[2]
+    dwf = torch.empty((2, d, h), dtype=torch.bfloat16, device=qx.q.device)
+    gemm(operand(qx, C.MN_MAJOR, d), operand(qdug, C.MN_MAJOR, h, T * h, 2), d, h, T, dwf, h, d * h, batch=2)
+    return dwf
+
+
 def gmlp_forward(x: torch.Tensor, wf: torch.Tensor, wd: torch.Tensor):
     """FP8 GMLP forward, GMLP.__call__ (ueaj/model/mlp.py:100-115) with the fused gate/up
     Einsum "bnd,idh->ibnh" and its gating fused into one GEMM epilogue.
@@ -187,20 +250,12 @@ def gmlp_forward(x: torch.Tensor, wf: torch.Tensor, wd: torch.Tensor):
     x = _check_bf16_cuda(x, "x")
     wf = _check_bf16_cuda(wf, "wf")
     wd = _check_bf16_cuda(wd, "wd")
-    T, d = x.shape
-    h = wf.shape[2]
-    dev = x.device
     qx = quantize(x, C.E4M3)
     qwf = quantize(wf, C.E4M3)
-    ug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
-    hid = torch.empty((T, h), dtype=torch.bfloat16, device=dev)
-    amax_h = torch.empty(1, dtype=torch.float32, device=dev)
-    gemm(operand(qx, C.K_MAJOR, d), operand(qwf, C.MN_MAJOR, h, d * h, 2), T, h, d, ug, h, T * h,
-         epilogue=C.EPI_SWIGLU, h=hid, ldh=h, amax_out=amax_h)
+    ug, hid, amax_h = gmlp_f1(qx, qwf)
     qh = quantize(hid, C.E4M3, amax_h)
     qwd = quantize(wd, C.E4M3)
-    y = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
-    gemm(operand(qh, C.K_MAJOR, h), operand(qwd, C.MN_MAJOR, d), T, d, h, y, d)
+    y = gmlp_f2(qh, qwd)
     return y, (qx, qwf, ug, qh, qwd)
 
 
@@ -209,28 +264,12 @@ def gmlp_backward(dy: torch.Tensor, saved, need_dx: bool = True, need_dw: bool =
     the gating backward, with e5m2 gradients and e4m3 saved operands."""
     qx, qwf, ug, qh, qwd = saved
     dy = _check_bf16_cuda(dy, "dy")
-    T, d = dy.shape
-    h = ug.shape[2]
-    dev = dy.device
     qdy = quantize(dy, C.E5M2)
-    dug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
-    amax_dug = torch.empty(1, dtype=torch.float32, device=dev)
-    # dH = dY Wd^T fused with the gating backward -> [dU, dG]
-    gemm(operand(qdy, C.K_MAJOR, d), operand(qwd, C.K_MAJOR, d), T, h, d, dug, h, T * h,
-         epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug)
-    dwd = dwf = dx = None
-    if need_dw:  # dWd = H^T dY
-        dwd = torch.empty((h, d), dtype=torch.bfloat16, device=dev)
-        gemm(operand(qh, C.MN_MAJOR, h), operand(qdy, C.MN_MAJOR, d), h, d, T, dwd, d)
+    dug, amax_dug = gmlp_b2(qdy, qwd, ug)
+    dwd = gmlp_b1(qh, qdy) if need_dw else None
     qdug = quantize(dug, C.E5M2, amax_dug)
-    if need_dx:  # dx = sum_i dUG[i] Wf[i]^T
-        dx = torch.empty((T, d), dtype=torch.bfloat16, device=dev)
-        gemm(operand(qdug, C.K_MAJOR, h, T * h, 2), operand(qwf, C.K_MAJOR, h, d * h, 2), T, d, h, dx, d,
-             k_batches=2)
-    if need_dw:  # dWf[i] = x^T dUG[i]
-        dwf = torch.empty((2, d, h), dtype=torch.bfloat16, device=dev)
-        gemm(operand(qx, C.MN_MAJOR, d), operand(qdug, C.MN_MAJOR, h, T * h, 2), d, h, T, dwf, h, d * h,
-             batch=2)
+    dx = gmlp_b4(qdug, qwf) if need_dx else None
+    dwf = gmlp_b3(qx, qdug) if need_dw else None
     return dx, dwf, dwd
 
 

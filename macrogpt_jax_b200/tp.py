@@ -1,0 +1,159 @@
+"""Tensor-parallel FP8 GMLP across the GPUs of one box (one process per GPU).
+
+The reference declares this split but never builds a mesh (ueaj/model/mlp.py:85,96 put
+'tensor' on the hidden axis of both weights; ueaj/model/layer.py:9,57 shard activations over
+tokens).  Here it runs for real:
+
+  * gate/up weight column-split over hidden: rank r holds Wf[:, :, r*h/k:(r+1)*h/k], so
+    swish(gate) * up stays local; down weight row-split: Wd[r*h/k:(r+1)*h/k, :];
+  * activations are token-sharded [T/k, d] between blocks;
+  * forward: all-gather fp8 x -> local [U, G, H] GEMM -> local partial y = H Wd over this
+    rank's hidden slice -> reduce-scatter of the partials over tokens;
+  * backward mirrors it: all-gather fp8 dY -> local dH/gating and dWd -> local partial dx
+    -> reduce-scatter; dWf and dWd stay local (no data-parallel all-reduce in this block).
+
+Every per-tensor scale is the scale of the WHOLE logical tensor (a MAX all-reduce of the
+local amax values), so each rank quantises exactly as the single-GPU path does; the only
+numerical difference from one GPU is the order of the final bf16 sums.
+
+Collectives go through torch.distributed (NCCL on GPUs).  The compute backend defaults to
+this package's CUDA ops; tests substitute a CPU backend to exercise the host logic over
+gloo.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _capi as C
+from . import ops as cuda_ops
+from .configurator import config
+from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
+
+
+class TPContext:
+    """Process group, rank layout and compute backend of one tensor-parallel block."""
+
+    def __init__(self, group=None, backend=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.be = backend if backend is not None else cuda_ops
+
+    def global_amax(self, t: torch.Tensor) -> torch.Tensor:
+        a = self.be.amax(t)
+        dist.all_reduce(a, op=dist.ReduceOp.MAX, group=self.group)
+        return a
+
+    def quant_global(self, t: torch.Tensor, fmt: int):
+        return self.be.quantize(t, fmt, self.global_amax(t))
+
+    def all_gather_tokens(self, q):
+        """Concatenates every rank's fp8 token shard [T/k, d] into [T, d] (rank order)."""
+        local = q.q
+        full = torch.empty((local.shape[0] * self.world,) + tuple(local.shape[1:]), dtype=local.dtype,
+                           device=local.device)
+        dist.all_gather_into_tensor(full.view(torch.uint8), local.contiguous().view(torch.uint8), group=self.group)
+        return self.be.Fp8Tensor(full, q.inv_scale, q.amax)
+
+    def reduce_scatter_tokens(self, partial: torch.Tensor) -> torch.Tensor:
+        """Sums the ranks' [T, d] partials and leaves rank r its token block [T/k, d]."""
+        out = torch.empty((partial.shape[0] // self.world,) + tuple(partial.shape[1:]), dtype=partial.dtype,
+                          device=partial.device)
+        dist.reduce_scatter_tensor(out, partial.contiguous(), op=dist.ReduceOp.SUM, group=self.group)
+        return out
+
+
+class _TPGMLPFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, wf, wd, tp: TPContext):
+        be = tp.be
+        qx = tp.all_gather_tokens(tp.quant_global(x, C.E4M3))
+        qwf = tp.quant_global(wf, C.E4M3)
+        ug, hid, amax_h = be.gmlp_f1(qx, qwf)
+        dist.all_reduce(amax_h, op=dist.ReduceOp.MAX, group=tp.group)
+        qh = be.quantize(hid, C.E4M3, amax_h)
+        qwd = tp.quant_global(wd, C.E4M3)
+        y = tp.reduce_scatter_tokens(be.gmlp_f2(qh, qwd))
+        ctx.tp = tp
+        ctx.saved = (qx, qwf, ug, qh, qwd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        tp = ctx.tp
+        be = tp.be
+        qx, qwf, ug, qh, qwd = ctx.saved
+        ctx.saved = None
+        qdy = tp.all_gather_tokens(tp.quant_global(dy.to(torch.bfloat16).contiguous(), C.E5M2))
+        dug, amax_dug = be.gmlp_b2(qdy, qwd, ug)
+        dist.all_reduce(amax_dug, op=dist.ReduceOp.MAX, group=tp.group)
+        dwd = be.gmlp_b1(qh, qdy)
+        qdug = be.quantize(dug, C.E5M2, amax_dug)
+        dx = tp.reduce_scatter_tokens(be.gmlp_b4(qdug, qwf))
+        dwf = be.gmlp_b3(qx, qdug)
+        return dx, dwf, dwd, None
+
+
+@config
+class TPGMLP(torch.nn.Module):
+    """GMLP (ueaj/model/mlp.py:59-115) split over a process group.
+
+    Same constructor as GMLP plus `group` (the tensor-parallel process group; `mesh` is
+    accepted as an alias), `device`, and `fused_init` / `down_init` for the two weights.
+    Every rank builds the full weights from `rngs` exactly as GMLP does and keeps its slice,
+    so a TPGMLP and a GMLP built from the same seed hold the same logical weights.
+    `forward` takes this rank's token shard [..., T/k, d] and returns its shard of y.
+    """
+
+    def __init__(self, model_d: int, hidden_d: Optional[int] = None, activation_fn: Callable = None,
+                 param_dtype: torch.dtype = torch.bfloat16, *, rngs: Rngs, mesh=None, group=None, device=None,
+                 fused_init=lecun_normal_init, down_init=zeros_init, backend=None):
+        super().__init__()
+        hidden_d = 4 * model_d if hidden_d is None else hidden_d
+        group = group if group is not None else mesh
+        self.tp = TPContext(group, backend)
+        k, r = self.tp.world, self.tp.rank
+        if hidden_d % k:
+            raise ValueError(f"hidden {hidden_d} is not divisible by the tensor-parallel size {k}")
+        if activation_fn is not None:
+            from .mlp import swish
+            if activation_fn is not swish:
+                raise NotImplementedError("the tensor-parallel GMLP fuses swish gating only")
+        hl = hidden_d // k
+        self.model_d, self.hidden_d, self.hidden_local = model_d, hidden_d, hl
+        cpu = torch.device("cpu")
+        full_f = Einsum("bnd,idh->ibnh", initializer=fused_init, size_dict={"d": model_d, "h": hidden_d, "i": 2},
+                        batch_dims="i", rngs=rngs, dtype=param_dtype, sharding=(None, None, "tensor"), device=cpu)
+        full_d = Einsum("bnh,hd->bnd", initializer=down_init, size_dict={"d": model_d, "h": hidden_d}, rngs=rngs,
+                        dtype=param_dtype, sharding=("tensor", None), device=cpu)
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else cpu
+        # Local shards as Einsum layers over the local hidden width, so optimisers that read
+        # Einsum metadata see the shard's canonical layout.
+        self.fused_proj = Einsum("bnd,idh->ibnh", initializer=zeros_init, size_dict={"d": model_d, "h": hl, "i": 2},
+                                 batch_dims="i", rngs=Rngs(0), dtype=param_dtype, sharding=(None, None, "tensor"),
+                                 device=device)
+        self.down_proj = Einsum("bnh,hd->bnd", initializer=zeros_init, size_dict={"d": model_d, "h": hl},
+                                rngs=Rngs(0), dtype=param_dtype, sharding=("tensor", None), device=device)
+        with torch.no_grad():
+            self.fused_proj.w.copy_(full_f.w[:, :, r * hl:(r + 1) * hl])
+            self.down_proj.w.copy_(full_d.w[r * hl:(r + 1) * hl, :])
+
+    def shard_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's contiguous token block of a full [..., d] activation, as [T/k, d]."""
+        flat = x.reshape(-1, x.shape[-1])
+        n = flat.shape[0]
+        if n % self.tp.world:
+            raise ValueError(f"{n} tokens are not divisible by the tensor-parallel size {self.tp.world}")
+        b = n // self.tp.world
+        return flat[self.tp.rank * b:(self.tp.rank + 1) * b].contiguous()
+
+    def forward(self, x_local: torch.Tensor) -> torch.Tensor:
+        lead = x_local.shape[:-1]
+        x2d = x_local.to(torch.bfloat16).reshape(-1, self.model_d).contiguous()
+        wf = self.fused_proj.w if self.fused_proj.w.dtype == torch.bfloat16 else self.fused_proj.w.to(torch.bfloat16)
+        wd = self.down_proj.w if self.down_proj.w.dtype == torch.bfloat16 else self.down_proj.w.to(torch.bfloat16)
+        return _TPGMLPFn.apply(x2d, wf, wd, self.tp).reshape(*lead, self.model_d)

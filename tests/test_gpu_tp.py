@@ -1,0 +1,79 @@
+"""Tensor-parallel FP8 GMLP on 2 GPUs (NCCL, one process per GPU) against the oracle.
+Skips when fewer than two GPUs are visible."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+T, D, H = 512, 256, 1024
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, outdir):
+    import sys
+    import torch.distributed as dist
+    sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from macrogpt_jax_b200.einsum import Rngs, scaled_normal_init
+        from macrogpt_jax_b200.tp import TPGMLP
+        from oracle import path as op
+        dev = torch.device("cuda", rank)
+        m = TPGMLP(D, H, rngs=Rngs(7), device=dev, fused_init=scaled_normal_init(D ** -0.5),
+                   down_init=scaled_normal_init(H ** -0.5))
+        rng = np.random.default_rng(0)
+        xb = op.bf16_normal(rng, (T, D))
+        dyb = op.bf16_normal(rng, (T, D), 1e-3)
+        to_t = lambda b: torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
+        x = m.shard_tokens(to_t(xb)).requires_grad_(True)
+        y = m(x)
+        y.backward(m.shard_tokens(to_t(dyb)))
+        torch.cuda.synchronize()
+        bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=bits(y), dx=bits(x.grad),
+                 dwf=bits(m.fused_proj.w.grad), dwd=bits(m.down_proj.w.grad))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_gpu_matches_oracle(cuda, tmp_path):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from helpers import bf16_bits_to_f64, compare
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.mlp import GMLP
+    from oracle import path as op
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    r = [np.load(tmp_path / f"rank{i}.npz") for i in range(2)]
+    cpu = torch.device("cpu")
+    full = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5), device=cpu),
+                         down_proj=Einsum.override(initializer=scaled_normal_init(H ** -0.5), device=cpu))(
+        D, H, rngs=Rngs(7))
+    bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    rng = np.random.default_rng(0)
+    xb = op.bf16_normal(rng, (T, D))
+    dyb = op.bf16_normal(rng, (T, D), 1e-3)
+    y, saved = op.gmlp_forward(xb, bits(full.fused_proj.w), bits(full.down_proj.w))
+    g = op.gmlp_backward(dyb, saved)
+    f = bf16_bits_to_f64
+    compare(f(np.concatenate([r[0]["y"], r[1]["y"]])), f(y))
+    compare(f(np.concatenate([r[0]["dx"], r[1]["dx"]])), f(g["dx"]))
+    compare(f(np.concatenate([r[0]["dwf"], r[1]["dwf"]], axis=2)), f(g["dwf"]))
+    compare(f(np.concatenate([r[0]["dwd"], r[1]["dwd"]], axis=0)), f(g["dwd"]))
