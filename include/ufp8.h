@@ -153,6 +153,10 @@ int ufp8_set_gemm_ctas(int ctas);
 #define UFP8_GEMM_CTA_PAIR 2
 int ufp8_set_gemm_variant(int variant);
 
+/* Tile raster of the persistent GEMM: how many M tiles form a group that is swept along N
+ * before the next group starts (0 = default 16).  Tuning knob for L2 reuse. */
+int ufp8_set_gemm_raster(int group_m);
+
 #ifdef __cplusplus
 }
 #endif

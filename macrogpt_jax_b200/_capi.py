@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "ufp8_device_status",
     "ufp8_set_gemm_ctas",
     "ufp8_set_gemm_variant",
+    "ufp8_set_gemm_raster",
 )
 
 
@@ -101,8 +102,9 @@ def load() -> ctypes.CDLL:
     lib.ufp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_int), i32]
     lib.ufp8_set_gemm_ctas.argtypes = [i32]
     lib.ufp8_set_gemm_variant.argtypes = [i32]
+    lib.ufp8_set_gemm_raster.argtypes = [i32]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
-                 "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant"):
+                 "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -155,3 +157,7 @@ def set_gemm_ctas(ctas: int) -> None:
 
 def set_gemm_variant(variant: int) -> None:
     check(load().ufp8_set_gemm_variant(variant))
+
+
+def set_gemm_raster(group_m: int) -> None:
+    check(load().ufp8_set_gemm_raster(group_m))

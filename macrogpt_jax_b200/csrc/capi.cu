@@ -61,6 +61,7 @@ int device_info(DeviceInfo** out) {
 namespace {
 int g_gemm_ctas = 0;
 int g_gemm_variant = UFP8_GEMM_AUTO;
+int g_gemm_group_m = 0;
 
 bool is_fmt(int fmt) { return fmt == UFP8_E4M3 || fmt == UFP8_E5M2; }
 }  // namespace
@@ -122,7 +123,7 @@ int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream) {
   if (!desc) return set_error(UFP8_ERR_INVALID, "ufp8_gemm: null descriptor");
   DeviceInfo* dev;
   if (int rc = device_info(&dev)) return rc;
-  return launch_gemm(*desc, reinterpret_cast<cudaStream_t>(stream), *dev, g_gemm_ctas, g_gemm_variant);
+  return launch_gemm(*desc, reinterpret_cast<cudaStream_t>(stream), *dev, g_gemm_ctas, g_gemm_variant, g_gemm_group_m);
 }
 
 int ufp8_device_status(int* status, int clear) {
@@ -142,6 +143,12 @@ int ufp8_set_gemm_variant(int variant) {
   if (variant != UFP8_GEMM_AUTO && variant != UFP8_GEMM_SINGLE_CTA && variant != UFP8_GEMM_CTA_PAIR)
     return set_error(UFP8_ERR_INVALID, "ufp8_set_gemm_variant: unknown variant %d", variant);
   g_gemm_variant = variant;
+  return UFP8_OK;
+}
+
+int ufp8_set_gemm_raster(int group_m) {
+  if (group_m < 0 || group_m > 4096) return set_error(UFP8_ERR_INVALID, "ufp8_set_gemm_raster: group_m %d", group_m);
+  g_gemm_group_m = group_m;
   return UFP8_OK;
 }
 

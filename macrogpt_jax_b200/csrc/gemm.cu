@@ -32,7 +32,6 @@ constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kBarrierBytes = 256;
 constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + alignment slack
-constexpr int kGroupM = 16;
 
 struct GemmArgs {
   int M, N, K;
@@ -52,16 +51,17 @@ struct GemmArgs {
   long long ldug, ug_bstride;
   unsigned int* amax_bits;
   int* status;
+  int group_m;  // tile raster: M tiles per group swept before moving along N
 };
 
 __device__ __forceinline__ void map_tile(int tile, const GemmArgs& a, int& g, int& mb, int& nb) {
   const int tpb = a.tiles_m * a.tiles_n;
   g = tile / tpb;
   const int r = tile - g * tpb;
-  const int span = kGroupM * a.tiles_n;
+  const int span = a.group_m * a.tiles_n;
   const int grp = r / span;
-  const int first_m = grp * kGroupM;
-  const int gm = min(a.tiles_m - first_m, kGroupM);
+  const int first_m = grp * a.group_m;
+  const int gm = min(a.tiles_m - first_m, a.group_m);
   const int rr = r - grp * span;
   mb = first_m + rr % gm;
   nb = rr / gm;
@@ -73,7 +73,9 @@ __device__ __forceinline__ uint32_t bf16_bits(float v) {
 __device__ __forceinline__ float bf16_round(float v) { return __uint_as_float(bf16_bits(v) << 16); }
 __device__ __forceinline__ float bf16_to_f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
 
-__device__ __forceinline__ float sigmoidf_(float g) { return __frcp_rn(1.0f + __expf(-g)); }
+// Logistic function for the gating epilogues: MUFU exp2 and approximate reciprocal (a few
+// ulp, far below bf16 resolution).  g << 0 gives 1 + inf -> 0, g >> 0 gives 1.
+__device__ __forceinline__ float sigmoidf_(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
 
 // Stores 32 consecutive bf16 values (bit patterns in the low halves of v[]) at p;
 // columns at or past `valid` are skipped.  Vector path when the whole run is in range.
@@ -433,9 +435,33 @@ __device__ __forceinline__ void store_bf16x16_packed(__nv_bfloat16* p, const uin
   }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return bf16_bits(lo) | (bf16_bits(hi) << 16);
+__device__ __forceinline__ void store_bf16x16_packed_h(__nv_bfloat16* p, const uint32_t (&w)[8], int valid,
+                                                       bool vec, uint64_t pol) {
+  if (vec && valid >= 16) {
+    st_global_v4_hint(p, make_uint4(w[0], w[1], w[2], w[3]), pol);
+    st_global_v4_hint(p + 8, make_uint4(w[4], w[5], w[6], w[7]), pol);
+  } else {
+    store_bf16x16_packed(p, w, valid, vec);
+  }
 }
+
+__device__ __forceinline__ void store_bf16x32_packed_h(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
+                                                       bool vec, uint64_t pol) {
+  if (vec && valid >= 32) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st_global_v4_hint(p + 8 * i, make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]), pol);
+  } else {
+    store_bf16x32_packed(p, w, valid, vec);
+  }
+}
+
+// Two floats -> packed bf16x2 (lo in the low half) with one cvt.rn.bf16x2.f32.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+__device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // Loads 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]);
 // elements at or past `valid` read as zero.
@@ -455,6 +481,25 @@ __device__ __forceinline__ void load_bf16x32_packed(const __nv_bfloat16* p, uint
     const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = (2 * j < valid) ? q[2 * j] : 0u;
+      const uint32_t hi = (2 * j + 1 < valid) ? q[2 * j + 1] : 0u;
+      w[j] = lo | (hi << 16);
+    }
+  }
+}
+
+// Loads 16 consecutive bf16 values packed two per word; elements at or past `valid` read 0.
+__device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint32_t (&w)[8], int valid,
+                                                    bool vec) {
+  if (vec && valid >= 16) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+    const uint4 t0 = q[0], t1 = q[1];
+    w[0] = t0.x; w[1] = t0.y; w[2] = t0.z; w[3] = t0.w;
+    w[4] = t1.x; w[5] = t1.y; w[6] = t1.z; w[7] = t1.w;
+  } else {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
       const uint32_t lo = (2 * j < valid) ? q[2 * j] : 0u;
       const uint32_t hi = (2 * j + 1 < valid) ? q[2 * j + 1] : 0u;
       w[j] = lo | (hi << 16);
@@ -623,6 +668,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
     const bool vec = args.vec_ok != 0;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint64_t stream = l2_policy_evict_first();  // outputs are not re-read by this kernel
     uint32_t amax = 0;
     int local = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
@@ -666,7 +712,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               for (int j = 0; j < 16; ++j)
                 o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
               __nv_bfloat16* p = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
-              store_bf16x32_packed(p, o, valid, vec);
+              store_bf16x32_packed_h(p, o, valid, vec, stream);
             }
           }
         }
@@ -682,81 +728,77 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           if (row_ok && col0 < args.N) {
             const int valid = args.N - col0;
             uint32_t ou[8], og[8], oh[8];
+            uint32_t m2 = 0;  // packed 2 x 16-bit max of |H|
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const uint32_t ub = bf16_bits(__uint_as_float(ru[j]) * alpha);
-              const uint32_t gb = bf16_bits(__uint_as_float(rg[j]) * alpha);
-              const float u = bf16_to_f(ub), gt = bf16_to_f(gb);
-              const uint32_t hb = bf16_bits(u * (gt * sigmoidf_(gt)));
-              if (j & 1) {
-                ou[j >> 1] |= ub << 16;
-                og[j >> 1] |= gb << 16;
-                oh[j >> 1] |= hb << 16;
-              } else {
-                ou[j >> 1] = ub;
-                og[j >> 1] = gb;
-                oh[j >> 1] = hb;
-              }
-              if (j < valid) amax = max(amax, hb & 0x7FFFu);
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t uw = pack_bf16x2(__uint_as_float(ru[2 * j]) * alpha, __uint_as_float(ru[2 * j + 1]) * alpha);
+              const uint32_t gw = pack_bf16x2(__uint_as_float(rg[2 * j]) * alpha, __uint_as_float(rg[2 * j + 1]) * alpha);
+              const float g0 = lo_f(gw), g1 = hi_f(gw);
+              const uint32_t hw = pack_bf16x2(lo_f(uw) * (g0 * sigmoidf_(g0)), hi_f(uw) * (g1 * sigmoidf_(g1)));
+              ou[j] = uw;
+              og[j] = gw;
+              oh[j] = hw;
+              const uint32_t keep = (2 * j + 1 < valid) ? 0x7FFF7FFFu : (2 * j < valid ? 0x00007FFFu : 0u);
+              m2 = __vmaxu2(m2, hw & keep);
             }
+            amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
             __nv_bfloat16* pu = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
-            store_bf16x16_packed(pu, ou, valid, vec);
-            store_bf16x16_packed(pu + args.d_bstride, og, valid, vec);
-            store_bf16x16_packed(args.h + row * args.ldh + col0, oh, valid, vec);
+            store_bf16x16_packed_h(pu, ou, valid, vec, stream);
+            store_bf16x16_packed_h(pu + args.d_bstride, og, valid, vec, stream);
+            store_bf16x16_packed_h(args.h + row * args.ldh + col0, oh, valid, vec, stream);
           }
         }
-      } else {  // UFP8_EPI_DSWIGLU: U / G of the next 32 columns are loaded while this chunk computes
-        const int c_begin = chalf * 128, c_end = c_begin + 128;
+      } else {  // UFP8_EPI_DSWIGLU: 16-column chunks; U / G loads run two chunks ahead
+        const int c_begin = chalf * 128;
         const __nv_bfloat16* ug_row = args.ug + row * args.ldug;
-        uint32_t cu[16], cg[16];
-        {
-          const int col0 = nb * kBN + c_begin;
+        uint32_t bu[3][8], bg[3][8];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int col0 = nb * kBN + c_begin + 16 * p;
           const int valid = row_ok ? args.N - col0 : 0;
           if (valid > 0) {
-            load_bf16x32_packed(ug_row + col0, cu, valid, vec);
-            load_bf16x32_packed(ug_row + args.ug_bstride + col0, cg, valid, vec);
+            load_bf16x16_packed(ug_row + col0, bu[p], valid, vec);
+            load_bf16x16_packed(ug_row + args.ug_bstride + col0, bg[p], valid, vec);
           }
         }
-#pragma unroll 1
-        for (int c = c_begin; c < c_end; c += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c, r);
-          uint32_t nu[16], ng[16];
-          const int ncol0 = nb * kBN + c + 32;
-          const int nvalid = (row_ok && c + 32 < c_end) ? args.N - ncol0 : 0;
-          if (nvalid > 0) {
-            load_bf16x32_packed(ug_row + ncol0, nu, nvalid, vec);
-            load_bf16x32_packed(ug_row + args.ug_bstride + ncol0, ng, nvalid, vec);
+#pragma unroll
+        for (int ci = 0; ci < 8; ++ci) {
+          const int c = c_begin + 16 * ci;
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + c, r);
+          if (ci + 2 < 8) {
+            const int ncol0 = nb * kBN + c + 32;
+            const int nvalid = row_ok ? args.N - ncol0 : 0;
+            if (nvalid > 0) {
+              load_bf16x16_packed(ug_row + ncol0, bu[(ci + 2) % 3], nvalid, vec);
+              load_bf16x16_packed(ug_row + args.ug_bstride + ncol0, bg[(ci + 2) % 3], nvalid, vec);
+            }
           }
           tmem_ld_wait();
           const int col0 = nb * kBN + c;
           if (row_ok && col0 < args.N) {
             const int valid = args.N - col0;
-            uint32_t odu[16], odg[16];
+            const uint32_t(&cu)[8] = bu[ci % 3];
+            const uint32_t(&cg)[8] = bg[ci % 3];
+            uint32_t odu[8], odg[8];
+            uint32_t m2 = 0;  // packed 2 x 16-bit max of |dU|, |dG|
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float dh = bf16_round(__uint_as_float(r[j]) * alpha);
-              const float u = bf16_to_f(half_of(cu, j)), gt = bf16_to_f(half_of(cg, j));
-              const float sg = sigmoidf_(gt);
-              const uint32_t dub = bf16_bits(dh * (gt * sg));
-              const uint32_t dgb = bf16_bits((dh * u) * (sg * (1.0f + gt * (1.0f - sg))));
-              if (j & 1) {
-                odu[j >> 1] |= dub << 16;
-                odg[j >> 1] |= dgb << 16;
-              } else {
-                odu[j >> 1] = dub;
-                odg[j >> 1] = dgb;
-              }
-              if (j < valid) amax = max(amax, max(dub & 0x7FFFu, dgb & 0x7FFFu));
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t dhw = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
+              const float dh0 = lo_f(dhw), dh1 = hi_f(dhw);
+              const float u0 = lo_f(cu[j]), u1 = hi_f(cu[j]);
+              const float g0 = lo_f(cg[j]), g1 = hi_f(cg[j]);
+              const float s0 = sigmoidf_(g0), s1 = sigmoidf_(g1);
+              odu[j] = pack_bf16x2(dh0 * (g0 * s0), dh1 * (g1 * s1));
+              odg[j] = pack_bf16x2((dh0 * u0) * (s0 * (1.0f + g0 * (1.0f - s0))),
+                                   (dh1 * u1) * (s1 * (1.0f + g1 * (1.0f - s1))));
+              const uint32_t keep = (2 * j + 1 < valid) ? 0x7FFF7FFFu : (2 * j < valid ? 0x00007FFFu : 0u);
+              m2 = __vmaxu2(m2, __vmaxu2(odu[j] & keep, odg[j] & keep));
             }
+            amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
             __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
-            store_bf16x32_packed(pd, odu, valid, vec);
-            store_bf16x32_packed(pd + args.d_bstride, odg, valid, vec);
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            cu[i] = nu[i];
-            cg[i] = ng[i];
+            store_bf16x16_packed_h(pd, odu, valid, vec, stream);
+            store_bf16x16_packed_h(pd + args.d_bstride, odg, valid, vec, stream);
           }
         }
       }
@@ -870,7 +912,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& dev, int ctas_override,
-                int variant) {
+                int variant, int group_m) {
   if (d.M < 0 || d.N < 0 || d.K < 0) return set_error(UFP8_ERR_INVALID, "negative GEMM extent");
   if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
   if (d.batch > 1 && d.k_batches > 1)
@@ -917,6 +959,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.ug_bstride = d.ug_batch_stride;
   a.amax_bits = reinterpret_cast<unsigned int*>(d.amax_out);
   a.status = dev.status_word;
+  a.group_m = group_m > 0 ? group_m : 16;
 
   if (d.K == 0) {
     zero_outputs_kernel<<<dev.sm_count * 4, 256, 0, stream>>>(a);

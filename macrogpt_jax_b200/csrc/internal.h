@@ -29,6 +29,7 @@ int launch_quantize(const void* x, int64_t n, int fmt, const float* amax, void* 
                     cudaStream_t s, const DeviceInfo& dev);
 
 // gemm.cu
-int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t s, const DeviceInfo& dev, int ctas_override, int variant);
+int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t s, const DeviceInfo& dev, int ctas_override, int variant,
+                int group_m);
 
 }  // namespace ufp8

@@ -64,14 +64,18 @@ __global__ void __launch_bounds__(kThreads) amax_vec_kernel(const uint4* __restr
   uint32_t m2 = 0;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  // Two independent 16-byte loads in flight per thread per iteration.
-  for (; i + stride < n_vec; i += 2 * stride) {
+  // Four independent 16-byte loads in flight per thread per iteration.
+  for (; i + 3 * stride < n_vec; i += 4 * stride) {
     const uint4 a = ld_stream(x + i);
     const uint4 b = ld_stream(x + i + stride);
+    const uint4 c = ld_stream(x + i + 2 * stride);
+    const uint4 d = ld_stream(x + i + 3 * stride);
     m2 = absmax2(m2, a.x); m2 = absmax2(m2, a.y); m2 = absmax2(m2, a.z); m2 = absmax2(m2, a.w);
     m2 = absmax2(m2, b.x); m2 = absmax2(m2, b.y); m2 = absmax2(m2, b.z); m2 = absmax2(m2, b.w);
+    m2 = absmax2(m2, c.x); m2 = absmax2(m2, c.y); m2 = absmax2(m2, c.z); m2 = absmax2(m2, c.w);
+    m2 = absmax2(m2, d.x); m2 = absmax2(m2, d.y); m2 = absmax2(m2, d.z); m2 = absmax2(m2, d.w);
   }
-  if (i < n_vec) {
+  for (; i < n_vec; i += stride) {
     const uint4 a = ld_stream(x + i);
     m2 = absmax2(m2, a.x); m2 = absmax2(m2, a.y); m2 = absmax2(m2, a.z); m2 = absmax2(m2, a.w);
   }
@@ -132,8 +136,18 @@ __device__ __forceinline__ uint32_t quant_4bytes(uint32_t w0, uint32_t w1, float
   return quant_word(w0, s, fmt) | (quant_word(w1, s, fmt) << 16);
 }
 
-// Vector body: 16 bf16 (two 16-byte loads) -> 16 fp8 (one 16-byte store) per step.
+// Vector body: 32 bf16 (four 16-byte loads, all in flight before any use) -> 32 fp8 (two
+// 16-byte stores) per step; a last odd group of 16 and the < 16-element tail follow.
 // A null `amax` means a unit scale (plain cast); a null `inv_scale` is not written.
+__device__ __forceinline__ uint4 quant16(const uint4& a, const uint4& b, float s, int fmt) {
+  uint4 o;
+  o.x = quant_4bytes(a.x, a.y, s, fmt);
+  o.y = quant_4bytes(a.z, a.w, s, fmt);
+  o.z = quant_4bytes(b.x, b.y, s, fmt);
+  o.w = quant_4bytes(b.z, b.w, s, fmt);
+  return o;
+}
+
 __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __restrict__ x, int64_t n_vec16,
                                                              const uint16_t* __restrict__ x_tail,
                                                              uint8_t* __restrict__ q_tail, int n_tail,
@@ -141,16 +155,19 @@ __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __rest
                                                              uint4* __restrict__ q, float* __restrict__ inv_scale) {
   const float s = amax ? scale_from_amax(*amax, fmt) : 1.0f;
   if (inv_scale && blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = __fdiv_rn(1.0f, s);
+  const int64_t n_vec32 = n_vec16 / 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n_vec16; i += stride) {
-    const uint4 a = ld_stream(x + 2 * i);
-    const uint4 b = ld_stream(x + 2 * i + 1);
-    uint4 o;
-    o.x = quant_4bytes(a.x, a.y, s, fmt);
-    o.y = quant_4bytes(a.z, a.w, s, fmt);
-    o.z = quant_4bytes(b.x, b.y, s, fmt);
-    o.w = quant_4bytes(b.z, b.w, s, fmt);
-    q[i] = o;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n_vec32; i += stride) {
+    const uint4 a0 = ld_stream(x + 4 * i);
+    const uint4 b0 = ld_stream(x + 4 * i + 1);
+    const uint4 a1 = ld_stream(x + 4 * i + 2);
+    const uint4 b1 = ld_stream(x + 4 * i + 3);
+    q[2 * i] = quant16(a0, b0, s, fmt);
+    q[2 * i + 1] = quant16(a1, b1, s, fmt);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && (n_vec16 & 1)) {
+    const int64_t j = n_vec16 - 1;
+    q[j] = quant16(ld_stream(x + 2 * j), ld_stream(x + 2 * j + 1), s, fmt);
   }
   if (blockIdx.x == 0 && threadIdx.x < n_tail) {
     const float p = __fmul_rn(__uint_as_float(static_cast<uint32_t>(x_tail[threadIdx.x]) << 16), s);
@@ -188,7 +205,7 @@ int launch_amax(const void* x, int64_t n, float* amax, cudaStream_t s, const Dev
     const int64_t n_vec = n / 8;
     const int n_tail = static_cast<int>(n - n_vec * 8);
     const uint16_t* tail = static_cast<const uint16_t*>(x) + n_vec * 8;
-    amax_vec_kernel<<<grid_for((n_vec + 1) / 2, dev), kThreads, 0, s>>>(static_cast<const uint4*>(x), n_vec, tail,
+    amax_vec_kernel<<<grid_for((n_vec + 3) / 4, dev), kThreads, 0, s>>>(static_cast<const uint4*>(x), n_vec, tail,
                                                                        n_tail, bits);
   } else {
     amax_scalar_kernel<<<grid_for(n, dev), kThreads, 0, s>>>(static_cast<const uint16_t*>(x), n, bits);
@@ -203,7 +220,7 @@ int launch_quantize(const void* x, int64_t n, int fmt, const float* amax, void* 
   if (aligned) {
     const int64_t n_vec16 = n / 16;
     const int n_tail = static_cast<int>(n - n_vec16 * 16);
-    quant_vec_kernel<<<grid_for(n_vec16, dev), kThreads, 0, s>>>(
+    quant_vec_kernel<<<grid_for((n_vec16 + 1) / 2, dev), kThreads, 0, s>>>(
         static_cast<const uint4*>(x), n_vec16, static_cast<const uint16_t*>(x) + n_vec16 * 16,
         static_cast<uint8_t*>(q) + n_vec16 * 16, n_tail, fmt, amax, static_cast<uint4*>(q), inv_scale);
   } else {

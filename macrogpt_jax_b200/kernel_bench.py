@@ -2,15 +2,22 @@
 
     python -m macrogpt_jax_b200.kernel_bench [--tokens T] [--d D] [--hidden H]
                                              [--gemms F1,F2,B2,B1,B4,B3] [--reps R] [--warmup W]
+                                             [--variant V] [--seconds S] [--cublas]
 
 Each named GEMM of the GMLP step runs R times after W warm-up launches on seeded fp8
 operands; the script prints one line per GEMM with its mean duration and TFLOP/s.  With
---reps 1 --warmup 1 it doubles as a small, self-contained target for profilers.
+--reps 1 --warmup 1 it doubles as a small, self-contained target for profilers.  With
+--seconds S each GEMM instead loops for S seconds while nvidia-smi samples the SM clock and
+power (sustained, power-capped throughput).  --cublas adds the same-shape plain fp8 GEMM
+from cuBLAS (torch._scaled_mm, per-tensor scales, bf16 out) as a library reference point.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import statistics
+import subprocess
+import time
 
 import torch
 
@@ -47,6 +54,82 @@ def build(T, d, h, dev):
     return g
 
 
+def cublas_same_shapes(T, d, h, dev):
+    """Plain fp8 GEMMs of the GMLP shapes via cuBLAS (torch._scaled_mm), K-major operands."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1)
+    one = torch.ones((), device=dev)
+    out = {}
+    for name, (M, N, K) in {"F1": (T, 2 * h, d), "F2": (T, d, h), "B4": (T, d, 2 * h)}.items():
+        a = torch.randn((M, K), generator=gen, device=dev).to(torch.float8_e4m3fn)
+        b = (torch.randn((N, K), generator=gen, device=dev) * 0.05).to(torch.float8_e4m3fn)
+        out["cublas_" + name] = (2.0 * M * N * K, lambda a=a, b=b: torch._scaled_mm(
+            a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16))
+    return out
+
+
+def sustained(fn, seconds: float, gpu: int):
+    """Loops fn for `seconds`; returns (mean ms per call, median SM MHz, max W, samples)."""
+    smi = None
+    try:
+        smi = subprocess.Popen(["nvidia-smi", f"--id={gpu}", "--query-gpu=clocks.sm,power.draw",
+                                "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE, text=True)
+    except (OSError, FileNotFoundError):
+        smi = None
+    time.sleep(0.3)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n, t0 = 0, time.time()
+    s.record()
+    while time.time() - t0 < seconds:
+        fn()
+        n += 1
+        if n % 16 == 0:
+            torch.cuda.synchronize()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / n
+    mhz = power = None
+    samples = 0
+    if smi is not None:
+        smi.terminate()
+        rows = [r.split(", ") for r in smi.communicate()[0].strip().splitlines() if r.strip()]
+        rows = rows[4:-2] if len(rows) > 8 else rows
+        samples = len(rows)
+        if rows:
+            mhz = statistics.median(float(r[0]) for r in rows)
+            power = max(float(r[1]) for r in rows)
+    return ms, mhz, power, samples
+
+
+def quant_bench(args, dev):
+    """amax (2 B/element read) and quantize (2 B read + 1 B written per element) on the
+    tensors one GMLP step quantises; prints algorithmic GB/s per tensor."""
+    T, d, h = args.tokens, args.d, args.hidden
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2)
+    for name, shape, fmt in (("x", (T, d), C.E4M3), ("Wf", (2, d, h), C.E4M3), ("H", (T, h), C.E4M3),
+                             ("dUG", (2, T, h), C.E5M2)):
+        x = torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+        n = x.numel()
+        amax = ops.amax(x)
+        for _ in range(args.warmup):
+            ops.amax(x)
+            ops.quantize(x, fmt, amax)
+        torch.cuda.synchronize()
+        res = {}
+        for kind, fn, nbytes in (("amax", lambda: ops.amax(x), 2 * n), ("quantize", lambda: ops.quantize(x, fmt, amax), 3 * n)):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.reps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            us = s.elapsed_time(e) * 1000.0 / args.reps
+            res[kind] = {"us": us, "gbs": nbytes / us / 1e3}
+        print(json.dumps({"tensor": name, "elements": n, **res}), flush=True)
+        del x
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
@@ -56,31 +139,48 @@ def main():
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--variant", type=int, default=0, help="0 auto, 1 one CTA per tile, 2 CTA pair")
+    ap.add_argument("--seconds", type=float, default=0.0, help="sustained loop length per GEMM (0 = off)")
+    ap.add_argument("--cublas", action="store_true", help="also time cuBLAS fp8 GEMMs of the same shapes")
+    ap.add_argument("--group-m", type=int, default=0, help="tile raster group (0 = library default)")
+    ap.add_argument("--quant", action="store_true", help="time amax and quantize on the GMLP tensor sizes instead")
     args = ap.parse_args()
+    C.set_gemm_raster(args.group_m)
     C.set_gemm_variant(args.variant)
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if args.quant:
+        return quant_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)
     names = [n.strip() for n in args.gemms.split(",") if n.strip()]
     for n in names:
         if n not in g:
             raise SystemExit(f"unknown GEMM {n}; choose from {ALL}")
+    if args.cublas:
+        cb = cublas_same_shapes(args.tokens, args.d, args.hidden, dev)
+        g.update(cb)
+        names += list(cb)
     for n in names:  # warm-up, in order
         for _ in range(args.warmup):
             g[n][1]()
     torch.cuda.synchronize()
     for n in names:
         flops, fn = g[n]
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(args.reps):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        us = s.elapsed_time(e) * 1000.0 / args.reps
-        print(json.dumps({"gemm": n, "variant": args.variant, "tokens": args.tokens, "d": args.d, "hidden": args.hidden, "us": us,
-                          "tflops": flops / us / 1e6}), flush=True)
+        rec = {"gemm": n, "variant": args.variant, "group_m": args.group_m, "tokens": args.tokens, "d": args.d, "hidden": args.hidden}
+        if args.seconds > 0:
+            ms, mhz, power, samples = sustained(fn, args.seconds, 0)
+            rec.update(us=ms * 1000.0, tflops=flops / ms / 1e9, sm_mhz_median=mhz, power_w_max=power,
+                       clock_samples=samples, seconds=args.seconds)
+        else:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.reps):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            us = s.elapsed_time(e) * 1000.0 / args.reps
+            rec.update(us=us, tflops=flops / us / 1e6)
+        print(json.dumps(rec), flush=True)
     if C.device_status() != 0:
         raise SystemExit("device status word set: a kernel wait timed out")
 
