@@ -136,6 +136,41 @@ __device__ __forceinline__ uint32_t quant_4bytes(uint32_t w0, uint32_t w1, float
   return quant_word(w0, s, fmt) | (quant_word(w1, s, fmt) << 16);
 }
 
+// Converts two products that are known not to be special (plain satfinite RNE).
+__device__ __forceinline__ uint32_t cvt2_plain(float p0, float p1, int fmt) {
+  const __nv_fp8_interpretation_t kind = fmt == UFP8_E4M3 ? __NV_E4M3 : __NV_E5M2;
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(p0, p1), __NV_SATFINITE, kind));
+}
+
+__device__ __forceinline__ uint32_t quant_word_plain(uint32_t w, float s, int fmt) {
+  return cvt2_plain(__fmul_rn(bf16lo(w), s), __fmul_rn(bf16hi(w), s), fmt);
+}
+
+// Largest sign-cleared bf16 pattern b with fl(bf16(b) * s) not special, or -1 if none.
+// fl(x * s) is monotonic in |x| for s >= 0, so a group whose largest |x| is at or below this
+// bound contains no special product.  s that is NaN, inf or negative makes every group take
+// the exact per-element path.
+__device__ __forceinline__ int special_free_bound(float s, int fmt) {
+  if (!(s >= 0.0f) || isinf(s)) return -1;
+  int lo = 0, hi = 0x7F80;  // 0x7F80 = +inf
+  if (is_special(__fmul_rn(__uint_as_float(0u), s), fmt)) return -1;
+  while (hi - lo > 1) {  // invariant: lo not special, hi special (inf * s >= inf for s > 0)
+    const int mid = (lo + hi) >> 1;
+    if (is_special(__fmul_rn(__uint_as_float(static_cast<uint32_t>(mid) << 16), s), fmt))
+      hi = mid;
+    else
+      lo = mid;
+  }
+  return s == 0.0f ? 0x7F7F : lo;  // s == 0: every finite x gives 0
+}
+
+__device__ __forceinline__ uint32_t absmax16(uint32_t m, const uint4& v) {
+  m = __vmaxu2(m, v.x & 0x7FFF7FFFu);
+  m = __vmaxu2(m, v.y & 0x7FFF7FFFu);
+  m = __vmaxu2(m, v.z & 0x7FFF7FFFu);
+  return __vmaxu2(m, v.w & 0x7FFF7FFFu);
+}
+
 // Vector body: 32 bf16 (four 16-byte loads, all in flight before any use) -> 32 fp8 (two
 // 16-byte stores) per step; a last odd group of 16 and the < 16-element tail follow.
 // A null `amax` means a unit scale (plain cast); a null `inv_scale` is not written.
@@ -148,6 +183,15 @@ __device__ __forceinline__ uint4 quant16(const uint4& a, const uint4& b, float s
   return o;
 }
 
+__device__ __forceinline__ uint4 quant16_plain(const uint4& a, const uint4& b, float s, int fmt) {
+  uint4 o;
+  o.x = quant_word_plain(a.x, s, fmt) | (quant_word_plain(a.y, s, fmt) << 16);
+  o.y = quant_word_plain(a.z, s, fmt) | (quant_word_plain(a.w, s, fmt) << 16);
+  o.z = quant_word_plain(b.x, s, fmt) | (quant_word_plain(b.y, s, fmt) << 16);
+  o.w = quant_word_plain(b.z, s, fmt) | (quant_word_plain(b.w, s, fmt) << 16);
+  return o;
+}
+
 __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __restrict__ x, int64_t n_vec16,
                                                              const uint16_t* __restrict__ x_tail,
                                                              uint8_t* __restrict__ q_tail, int n_tail,
@@ -155,6 +199,8 @@ __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __rest
                                                              uint4* __restrict__ q, float* __restrict__ inv_scale) {
   const float s = amax ? scale_from_amax(*amax, fmt) : 1.0f;
   if (inv_scale && blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = __fdiv_rn(1.0f, s);
+  const int bound = special_free_bound(s, fmt);
+  const uint32_t bound2 = bound < 0 ? 0u : (static_cast<uint32_t>(bound) * 0x00010001u);
   const int64_t n_vec32 = n_vec16 / 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n_vec32; i += stride) {
@@ -162,8 +208,15 @@ __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __rest
     const uint4 b0 = ld_stream(x + 4 * i + 1);
     const uint4 a1 = ld_stream(x + 4 * i + 2);
     const uint4 b1 = ld_stream(x + 4 * i + 3);
-    q[2 * i] = quant16(a0, b0, s, fmt);
-    q[2 * i + 1] = quant16(a1, b1, s, fmt);
+    const uint32_t m = absmax16(absmax16(absmax16(absmax16(0u, a0), b0), a1), b1);
+    // both 16-bit lanes of m at or below the bound: no special product in these 32
+    if (bound >= 0 && __vcmpleu2(m, bound2) == 0xFFFFFFFFu) {
+      q[2 * i] = quant16_plain(a0, b0, s, fmt);
+      q[2 * i + 1] = quant16_plain(a1, b1, s, fmt);
+    } else {
+      q[2 * i] = quant16(a0, b0, s, fmt);
+      q[2 * i + 1] = quant16(a1, b1, s, fmt);
+    }
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && (n_vec16 & 1)) {
     const int64_t j = n_vec16 - 1;
