@@ -31,9 +31,11 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "FP8 GMLP fwd+bwd TFLOP/s/GPU (% of FP8 peak), tokens/s at 1/2/4/8 B200"
 CONFIGS = {
-    # C4 (the headline, TP GMLP) and C2 (small single-GPU GMLP)
-    "gmlp_d4096": dict(d=4096, h=14336, B=4, S=4096),
-    "gmlp_d768": dict(d=768, h=3072, B=8, S=1024),
+    # the tensor-parallel GMLP workload (headline), the small single-GPU GMLP, and the
+    # attention projections (fused QKV d -> 3d plus O d -> d, 16 heads x 128)
+    "gmlp_d4096": dict(kind="gmlp", d=4096, h=14336, B=4, S=4096),
+    "gmlp_d768": dict(kind="gmlp", d=768, h=3072, B=8, S=1024),
+    "attn_d2048": dict(kind="attn", d=2048, heads=16, head_d=128, B=16, S=1024),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -42,6 +44,11 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def flops_per_step(T, d, h):
     """Algorithmic GMLP fwd+bwd FLOPs: 18 T d h (F1 4Tdh, F2 2Tdh, backward twice that)."""
     return 18.0 * T * d * h
+
+
+def attn_flops_per_step(T, d):
+    """Attention projections fwd+bwd: QKV 2 T d 3d + O 2 T d d forward, twice that backward."""
+    return 3.0 * (2.0 * T * d * 3 * d + 2.0 * T * d * d)
 
 
 def load_peaks():
@@ -191,6 +198,8 @@ def run_ours(args, cfg, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    if cfg["kind"] == "attn":
+        return run_attn(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
     if world > 1:
@@ -301,7 +310,9 @@ def run_ours(args, cfg, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
         "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h,
-                   "parallelism": parallelism, "l2": "inputs larger than L2 (working set > 4 GB/step)"},
+                   "parallelism": parallelism,
+                   "l2": ("inputs larger than L2" if T * (6 * h + 3 * d) * 2 > 2 * 126e6 else
+                          "working set below 2x L2: no flush between steps (secondary workload)")},
         "tflops_per_gpu": tflops_gpu,
         "frac_of_fp8_peak": {"nominal_4500": tflops_gpu / FP8_NOMINAL_TFLOPS,
                              "measured_2x_bf16_sustained": tflops_gpu / peak_fp8},
@@ -334,6 +345,77 @@ def run_ours(args, cfg, rank, world, local_rank):
     return out
 
 
+def run_attn(args, cfg, rank, world, local_rank, dev):
+    """Attention projections: qkv = fused QKV Einsum(x), y = O Einsum(a), then the backward
+    of both with seeded upstream gradients.  The attention kernel between them is not part of
+    this library, so `a` is an independent seeded input of the attention-output shape."""
+    import torch
+    from macrogpt_jax_b200 import _capi, ops
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+    if world > 1:
+        raise SystemExit("the attention-projection workload runs on one GPU")
+    d, H, K, B, S = cfg["d"], cfg["heads"], cfg["head_d"], cfg["B"], cfg["S"]
+    T = B * S
+    init = Einsum.override(initializer=scaled_normal_init(d ** -0.5))
+    m = SoftmaxAttention(d, kq_d=K, kv_heads=H, rngs=Rngs(0), fused_qkv=True, qkv=init, o=init)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    rnd = lambda *shape, std=1.0: (torch.randn(shape, generator=gen, device=dev) * std).to(torch.bfloat16)  # noqa
+    x, a = rnd(B, S, d), rnd(B, S, H, 1, K)
+    dqkv, dy = rnd(3, B, S, H, K, std=1e-3), rnd(B, S, d, std=1e-3)
+    params = list(m.parameters())
+
+    def step(xb, ab):
+        xl = xb.detach().requires_grad_(True)
+        al = ab.detach().requires_grad_(True)
+        qkv = m.qkv(xl)
+        y = m.project_out(al)
+        torch.autograd.backward([qkv, y], [dqkv, dy])
+        for p in params:
+            p.grad = None
+        return y
+
+    for _ in range(args.warmup):
+        step(x, a)
+    torch.cuda.synchronize()
+    timer = ops.KernelTimer()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = _capi.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.set_timer(timer)
+    ev0.record()
+    for _ in range(args.steps):
+        step(x, a)
+    ev1.record()
+    ops.set_timer(None)
+    torch.cuda.synchronize()
+    launches = _capi.launches - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    summ = timer.summary()
+    peaks, peak_src = load_peaks()
+    fl = attn_flops_per_step(T, d)
+    tflops = fl * args.steps / (ms / 1000.0) / 1e12
+    g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
+    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
+    return {
+        "metric": "FP8 attention projections fwd+bwd tokens/s (TFLOP/s/GPU)", "value": T * args.steps / (ms / 1000.0),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
+        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "heads": H, "head_dim": K,
+                   "parallelism": "single GPU", "l2": "inputs larger than L2"},
+        "tflops_per_gpu": tflops,
+        "roofline": {"kernel": "gemm_fp8_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_fp8,
+                     "unit": "TFLOP/s", "frac": (achieved / peak_fp8) if achieved else None,
+                     "peak_source": f"2 x bf16_tflops_sustained, {peak_src}", "launches": g_n,
+                     "time_share": g_ms / ms if ms else None, "traffic": None},
+        "gpu_launches": launches, "clocks": clk,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -350,8 +432,15 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     cfg = CONFIGS[args.config]
-    args.config_desc = (f"GMLP fwd+bwd, {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
-                        f"d_model {cfg['d']}, hidden {cfg['h']}, FP8 e4m3/e5m2")
+    if cfg["kind"] == "attn":
+        args.config_desc = (f"attention projections fwd+bwd (fused QKV {cfg['d']}->{3 * cfg['d']}, O "
+                            f"{cfg['d']}->{cfg['d']}), {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
+                            f"{cfg['heads']} heads x {cfg['head_d']}, FP8 e4m3/e5m2")
+        if args.impl == "reference":
+            raise SystemExit("the CPU arm covers the GMLP workloads")
+    else:
+        args.config_desc = (f"GMLP fwd+bwd, {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
+                            f"d_model {cfg['d']}, hidden {cfg['h']}, FP8 e4m3/e5m2")
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -134,3 +134,36 @@ def test_custom_astype_fp8(cuda):
         q = custom_astype(x, dt)
         assert q.dtype == dt
         assert (torch_fp8_to_codes(q) == ofp8.f32_to_fp8(ofp8.bf16_bits_to_f32(allb), fmt)).all()
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_attention_projections(cuda, fused):
+    """Q/K/V/O projections through SoftmaxAttention (fused QKV as one batched Einsum, or the
+    reference's separate Einsums) with a stand-in attention, against the oracle."""
+    import torch
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+    d, H, K = 256, 4, 64
+    init = Einsum.override(initializer=scaled_normal_init(d ** -0.5))
+    kw = dict(qkv=init, o=init) if fused else dict(q=init, k=init, v=init, o=init)
+    m = SoftmaxAttention(d, kq_d=K, kv_heads=H, rngs=Rngs(1), fused_qkv=fused, **kw)
+    rng = np.random.default_rng(4)
+    xb = op.bf16_normal(rng, (2, 96, d))
+    x = bits_to_torch_bf16(xb, cuda).requires_grad_(True)
+    q, k, v = m.project_qkv(x)
+    assert q.shape == (2, 96, H, 1, K) and k.shape == (2, 96, H, K) and v.shape == (2, 96, H, K)
+    attn = lambda q, k, v: (q + v.unsqueeze(3)).to(torch.bfloat16)  # noqa: E731  (shape-preserving stand-in)
+    y = m.project_out(attn(q, k, v))
+    if fused:
+        ref, qx, qw = op.einsum_fp8("bnd,fdhk->fbnhk", xb, torch_bf16_to_bits(m.qkv.w))
+        got = torch.stack([q.reshape(2, 96, H, K), k, v])
+        compare(bf16_bits_to_f64(torch_bf16_to_bits(got)), bf16_bits_to_f64(ref))
+    else:
+        for t, e in ((q, m.q), (k, m.k), (v, m.v)):
+            ref, _, _ = op.einsum_fp8(e.einsum_expr, xb, torch_bf16_to_bits(e.w))
+            compare(bf16_bits_to_f64(torch_bf16_to_bits(t)), bf16_bits_to_f64(ref))
+    a_bits = torch_bf16_to_bits(attn(q, k, v))
+    ry, _, _ = op.einsum_fp8("bnhiv,hivd->bnd", a_bits, torch_bf16_to_bits(m.o.w))
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(y)), bf16_bits_to_f64(ry))
+    y.backward(bits_to_torch_bf16(op.bf16_normal(rng, (2, 96, d), 1e-2), cuda))
+    assert x.grad is not None and x.grad.shape == x.shape and torch.isfinite(x.grad.float()).all()

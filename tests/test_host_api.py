@@ -130,6 +130,23 @@ def test_mlp_builds():
     assert m.up_proj.w.shape == (8, 32) and m.down_proj.w.shape == (32, 8)
 
 
+def test_attention_projection_layouts():
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+    a = SoftmaxAttention(64, kq_d=16, kv_heads=4, kv_q_ratio=2, rngs=Rngs(0), k=Einsum.override(device=CPU),
+                         v=Einsum.override(device=CPU), q=Einsum.override(device=CPU), o=Einsum.override(device=CPU))
+    assert a.k.w.shape == (64, 4, 16) and a.v.w.shape == (64, 4, 16) and a.q.w.shape == (64, 4, 2, 16)
+    assert a.o.w.shape == (4, 2, 16, 64) and (a.o.w == 0).all()  # zeros_init (ueaj/model/soft_attn.py:118)
+    assert a.q.sharding == (None, "tensor", None, None) and a.o.sharding == (None, None, None, "tensor")
+    f = SoftmaxAttention(64, kq_d=16, kv_heads=4, rngs=Rngs(0), fused_qkv=True, qkv=Einsum.override(device=CPU),
+                         o=Einsum.override(device=CPU))
+    assert f.qkv.w.shape == (3, 64, 4, 16) and f.qkv.einsum_expr == "bnd,fdhk->fbnhk"
+    with pytest.raises(ValueError):
+        SoftmaxAttention(64, kq_d=16, kv_heads=4, kv_q_ratio=2, rngs=Rngs(0), fused_qkv=True,
+                         qkv=Einsum.override(device=CPU), o=Einsum.override(device=CPU))
+    with pytest.raises(NotImplementedError):
+        f(torch.zeros(1, 2, 64))
+
+
 # ----------------------------------------------------------------------------- gradutils
 def test_custom_scale_and_astype_on_cpu():
     x = torch.randn(5, dtype=torch.float32, requires_grad=True)
