@@ -205,8 +205,9 @@ def run_ours(args, cfg, rank, world, local_rank):
     if world > 1:
         from macrogpt_jax_b200.tp import TPGMLP
         mlp = TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
-                     fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5))
-        parallelism = f"tp{world}"
+                     fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5),
+                     fused_reduce_scatter=args.tp_rs == "p2p")
+        parallelism = f"tp{world} (reduce-scatter: {'NVLink P2P from the GEMM epilogue' if args.tp_rs == 'p2p' else 'NCCL'})"
     else:
         mlp = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(d ** -0.5)),
                             down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
@@ -428,6 +429,8 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=256)
     ap.add_argument("--ref-hidden", type=int, default=1792)
     ap.add_argument("--gemm-traffic", type=float, default=None)
+    ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="nccl",
+                    help="tensor-parallel reduce-scatter: fused into the GEMM epilogue over NVLink, or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -452,6 +455,7 @@ def main():
         out = run_reference(args, cfg, rank, world)
     else:
         if world > 1:
+            os.environ.setdefault("NCCL_DEBUG", "WARN")  # no version banner on stdout: one JSON line
             import datetime
             import torch
             import torch.distributed as dist

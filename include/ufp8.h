@@ -41,7 +41,7 @@ extern "C" {
 
 typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 
-#define UFP8_ABI_VERSION 1
+#define UFP8_ABI_VERSION 2
 
 /* return codes */
 #define UFP8_OK 0
@@ -52,7 +52,8 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_ERR_DEVICE (-5)      /* device older than sm_100 */
 
 /* bits of the device status word */
-#define UFP8_STATUS_WAIT_TIMEOUT 1
+#define UFP8_STATUS_WAIT_TIMEOUT 1 /* a GEMM pipeline wait ran out */
+#define UFP8_STATUS_PEER_TIMEOUT 2 /* a tensor-parallel peer never signalled */
 
 /* fp8 formats (values match the MMA instruction-descriptor encoding) */
 #define UFP8_E4M3 0 /* float8_e4m3fn: forward operands, max 448   */
@@ -70,6 +71,7 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_EPI_STORE 0   /* D = acc * sa * sb                                          */
 #define UFP8_EPI_SWIGLU 1  /* D[0]=U, D[1]=G, H = U * silu(G), amax_out = max|H|          */
 #define UFP8_EPI_DSWIGLU 2 /* dH = acc*sa*sb; D[0]=dU, D[1]=dG from saved U,G; amax |dUG| */
+#define UFP8_EPI_RS_PUSH 3 /* D rows stored into their owner rank's reduce-scatter staging slot */
 
 const char* ufp8_last_error(void);
 int ufp8_abi_version(void);
@@ -134,9 +136,39 @@ typedef struct ufp8_gemm_desc {
   int64_t ldug;
   int64_t ug_batch_stride;
   float* amax_out;
+  /* RS_PUSH: rows [o*R, (o+1)*R) belong to rank o (R = rs_rows_per_rank); row m is stored at
+   * rs_slots[o] + ((rs_rank * R + m - o*R) * ldd + n) elements, i.e. this rank's slot in the
+   * owner's staging buffer (rs_slots comes from ufp8_tp_begin; `d` is ignored). */
+  void* const* rs_slots;
+  int32_t rs_rank;
+  int32_t rs_reserved;
+  int64_t rs_rows_per_rank;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);
+
+/* ---- tensor-parallel reduce-scatter over NVLink peer memory ------------------------------
+ * Replaces the reduce-scatter XLA/GSPMD would insert after the row-split down projection of
+ * a tensor-parallel GMLP (implied by ueaj/model/mlp.py:96 'tensor' on the hidden axis and
+ * ueaj/model/layer.py:57 token sharding).  A context owns two staging buffers (CUDA IPC,
+ * plain peer mappings, no multicast objects), each holding one slot per source rank.
+ * Per reduce-scatter: ufp8_tp_begin -> GEMM with UFP8_EPI_RS_PUSH -> ufp8_tp_finish, which
+ * signals the peers, waits (bounded by the context timeout) for all of them, and sums the
+ * slots in fp32 in rank order into `out`.  The context allocates its buffers with cudaMalloc
+ * (the one exception to caller-owned memory). */
+#define UFP8_IPC_HANDLE_BYTES 64
+typedef struct ufp8_tp_ctx ufp8_tp_ctx;
+int ufp8_tp_create(int rank, int world, int64_t slot_bytes, ufp8_tp_ctx** ctx, uint8_t* ipc_handle_out);
+int ufp8_tp_connect(ufp8_tp_ctx* ctx, const uint8_t* ipc_handles /* world x UFP8_IPC_HANDLE_BYTES */);
+/* Connects contexts that live in one process (one process driving several GPUs with peer
+ * access, or one GPU for tests): peers[r] is the context of rank r. */
+int ufp8_tp_connect_local(ufp8_tp_ctx* ctx, ufp8_tp_ctx* const* peers);
+int ufp8_tp_destroy(ufp8_tp_ctx* ctx);
+int ufp8_tp_set_timeout_ms(ufp8_tp_ctx* ctx, int ms);
+int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* slot_bytes);
+int ufp8_tp_begin(ufp8_tp_ctx* ctx, void* const** slot_table, uint64_t* epoch);
+int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols, int64_t ld_slot, void* out,
+                   int64_t ld_out, ufp8_stream_t stream);
 
 /* Synchronises the current device, returns its status word in *status (0 = clean,
  * UFP8_STATUS_* bits otherwise) and clears it when `clear` is non-zero. */

@@ -12,11 +12,12 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libufp8.so"
 # Constants mirrored from include/ufp8.h.
 OK = 0
 ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
-STATUS_WAIT_TIMEOUT = 1
+STATUS_WAIT_TIMEOUT, STATUS_PEER_TIMEOUT = 1, 2
+IPC_HANDLE_BYTES = 64
 E4M3, E5M2 = 0, 1
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
-EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU = 0, 1, 2
+EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH = 0, 1, 2, 3
 GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR = 0, 1, 2
 
 EXPORTED_SYMBOLS = (
@@ -31,6 +32,14 @@ EXPORTED_SYMBOLS = (
     "ufp8_set_gemm_ctas",
     "ufp8_set_gemm_variant",
     "ufp8_set_gemm_raster",
+    "ufp8_tp_create",
+    "ufp8_tp_connect",
+    "ufp8_tp_connect_local",
+    "ufp8_tp_destroy",
+    "ufp8_tp_set_timeout_ms",
+    "ufp8_tp_slot_bytes",
+    "ufp8_tp_begin",
+    "ufp8_tp_finish",
 )
 
 
@@ -67,6 +76,10 @@ class GemmDesc(ctypes.Structure):
         ("ldug", ctypes.c_int64),
         ("ug_batch_stride", ctypes.c_int64),
         ("amax_out", ctypes.c_void_p),
+        ("rs_slots", ctypes.c_void_p),
+        ("rs_rank", ctypes.c_int32),
+        ("rs_reserved", ctypes.c_int32),
+        ("rs_rows_per_rank", ctypes.c_int64),
     ]
 
 
@@ -103,8 +116,18 @@ def load() -> ctypes.CDLL:
     lib.ufp8_set_gemm_ctas.argtypes = [i32]
     lib.ufp8_set_gemm_variant.argtypes = [i32]
     lib.ufp8_set_gemm_raster.argtypes = [i32]
+    lib.ufp8_tp_create.argtypes = [i32, i32, i64, ctypes.POINTER(vp), ctypes.c_char_p]
+    lib.ufp8_tp_connect.argtypes = [vp, ctypes.c_char_p]
+    lib.ufp8_tp_connect_local.argtypes = [vp, ctypes.POINTER(vp)]
+    lib.ufp8_tp_destroy.argtypes = [vp]
+    lib.ufp8_tp_set_timeout_ms.argtypes = [vp, i32]
+    lib.ufp8_tp_slot_bytes.argtypes = [vp, ctypes.POINTER(i64)]
+    lib.ufp8_tp_begin.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
+    lib.ufp8_tp_finish.argtypes = [vp, ctypes.c_uint64, i64, i64, i64, vp, i64, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
-                 "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster"):
+                 "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
+                 "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
+                 "ufp8_tp_finish"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -161,3 +184,42 @@ def set_gemm_variant(variant: int) -> None:
 
 def set_gemm_raster(group_m: int) -> None:
     check(load().ufp8_set_gemm_raster(group_m))
+
+
+class TPReduceScatter:
+    """One tensor-parallel reduce-scatter context (include/ufp8.h ufp8_tp_*): peer-mapped
+    staging slots of `slot_bytes` per source rank, double-buffered."""
+
+    def __init__(self, rank: int, world: int, slot_bytes: int):
+        self.ctx = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(load().ufp8_tp_create(rank, world, slot_bytes, ctypes.byref(self.ctx), handle))
+        self.handle = handle.raw
+        self.rank, self.world, self.slot_bytes = rank, world, slot_bytes
+
+    def connect(self, handles) -> None:
+        check(load().ufp8_tp_connect(self.ctx, b"".join(handles)))
+
+    def connect_local(self, contexts) -> None:
+        """Peers in this process: contexts[r] is the TPReduceScatter of rank r."""
+        arr = (ctypes.c_void_p * len(contexts))(*[c.ctx.value for c in contexts])
+        check(load().ufp8_tp_connect_local(self.ctx, arr))
+
+    def set_timeout_ms(self, ms: int) -> None:
+        check(load().ufp8_tp_set_timeout_ms(self.ctx, ms))
+
+    def begin(self):
+        """-> (device address of this epoch's slot table, epoch)"""
+        table = ctypes.c_void_p()
+        epoch = ctypes.c_uint64()
+        check(load().ufp8_tp_begin(self.ctx, ctypes.byref(table), ctypes.byref(epoch)))
+        return table.value, epoch.value
+
+    def finish(self, epoch: int, rows: int, cols: int, ld_slot: int, out_ptr: int, ld_out: int, stream: int) -> None:
+        check(load().ufp8_tp_finish(self.ctx, epoch, rows, cols, ld_slot, out_ptr, ld_out, stream))
+        _count(1)
+
+    def close(self) -> None:
+        if self.ctx:
+            load().ufp8_tp_destroy(self.ctx)
+            self.ctx = ctypes.c_void_p()

@@ -52,6 +52,9 @@ struct GemmArgs {
   unsigned int* amax_bits;
   int* status;
   int group_m;  // tile raster: M tiles per group swept before moving along N
+  void* const* rs_slots;  // RS_PUSH: owners' staging slots
+  int rs_rank;
+  long long rs_rows;
 };
 
 __device__ __forceinline__ void map_tile(int tile, const GemmArgs& a, int& g, int& mb, int& nb) {
@@ -684,7 +687,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
 
-      if (args.mode == UFP8_EPI_STORE) {
+      if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH) {
+        // RS_PUSH: this row goes to its owner's staging slot for this rank (peer memory).
+        __nv_bfloat16* rs_row = nullptr;
+        if (args.mode == UFP8_EPI_RS_PUSH && row_ok) {
+          const long long owner = row / args.rs_rows;
+          rs_row = static_cast<__nv_bfloat16*>(args.rs_slots[owner]) +
+                   (args.rs_rank * args.rs_rows + (row - owner * args.rs_rows)) * args.ldd;
+        }
 #pragma unroll 1
         for (int c = chalf * 128; c < chalf * 128 + 128; c += 32) {
           uint32_t r[32];
@@ -711,7 +721,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j)
                 o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
-              __nv_bfloat16* p = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
+              __nv_bfloat16* p = rs_row ? rs_row + col0
+                                        : static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
               store_bf16x32_packed_h(p, o, valid, vec, stream);
             }
           }
@@ -810,6 +821,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       amax = __reduce_max_sync(0xFFFFFFFFu, amax);
       if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
     }
+    // Peer stores must be visible system-wide before the finish kernel's flag write.
+    if (args.mode == UFP8_EPI_RS_PUSH) __threadfence_system();
   }
 
   tc_fence_before();
@@ -917,19 +930,28 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
   if (d.batch > 1 && d.k_batches > 1)
     return set_error(UFP8_ERR_UNSUPPORTED, "batch > 1 together with k_batches > 1 is not supported");
-  if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU)
+  if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU &&
+      d.epilogue != UFP8_EPI_RS_PUSH)
     return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
+  const bool rs = d.epilogue == UFP8_EPI_RS_PUSH;
+  if (rs && (!d.rs_slots || d.rs_rows_per_rank <= 0 || d.rs_rank < 0 || d.d_dtype != UFP8_OUT_BF16 ||
+             d.batch != 1 || d.M % d.rs_rows_per_rank != 0 || d.rs_rank >= d.M / d.rs_rows_per_rank))
+    return set_error(UFP8_ERR_INVALID, "RS_PUSH needs rs_slots, bf16 output, batch 1, and M a multiple of "
+                                       "rs_rows_per_rank with rs_rank < M / rs_rows_per_rank");
+  if (rs && variant == UFP8_GEMM_SINGLE_CTA)
+    return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH runs on the CTA-pair kernel only");
   if (d.d_dtype != UFP8_OUT_BF16 && d.d_dtype != UFP8_OUT_F32)
     return set_error(UFP8_ERR_INVALID, "unknown output dtype %d", d.d_dtype);
-  if (d.epilogue != UFP8_EPI_STORE && (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1 || d.k_batches != 1))
+  if ((d.epilogue == UFP8_EPI_SWIGLU || d.epilogue == UFP8_EPI_DSWIGLU) &&
+      (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1 || d.k_batches != 1))
     return set_error(UFP8_ERR_INVALID, "SWIGLU/DSWIGLU epilogues need bf16 output, batch 1, k_batches 1");
-  if (!d.d) return set_error(UFP8_ERR_INVALID, "null output pointer");
+  if (!d.d && !rs) return set_error(UFP8_ERR_INVALID, "null output pointer");
   if (d.ldd < d.N) return set_error(UFP8_ERR_INVALID, "ldd < N");
   if (d.epilogue == UFP8_EPI_SWIGLU && (!d.h || d.ldh < d.N))
     return set_error(UFP8_ERR_INVALID, "SWIGLU needs h with ldh >= N");
   if (d.epilogue == UFP8_EPI_DSWIGLU && (!d.ug || d.ldug < d.N))
     return set_error(UFP8_ERR_INVALID, "DSWIGLU needs ug with ldug >= N");
-  if (d.epilogue != UFP8_EPI_STORE && !d.amax_out)
+  if ((d.epilogue == UFP8_EPI_SWIGLU || d.epilogue == UFP8_EPI_DSWIGLU) && !d.amax_out)
     return set_error(UFP8_ERR_INVALID, "SWIGLU/DSWIGLU need amax_out");
   if (d.M >= (int64_t(1) << 31) || d.N >= (int64_t(1) << 31) || d.K >= (int64_t(1) << 31))
     return set_error(UFP8_ERR_INVALID, "extent exceeds 2^31");
@@ -960,8 +982,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.amax_bits = reinterpret_cast<unsigned int*>(d.amax_out);
   a.status = dev.status_word;
   a.group_m = group_m > 0 ? group_m : 16;
+  a.rs_slots = d.rs_slots;
+  a.rs_rank = d.rs_rank;
+  a.rs_rows = d.rs_rows_per_rank;
 
   if (d.K == 0) {
+    if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");
     zero_outputs_kernel<<<dev.sm_count * 4, 256, 0, stream>>>(a);
     e = cudaGetLastError();
     return e == cudaSuccess ? UFP8_OK : cuda_error(e, "zero-fill launch");
@@ -995,7 +1021,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
             | (static_cast<uint32_t>(bm >> 4) << 24);       // M = 128 (one CTA) or 256 (CTA pair)
 
   const int esz = a.d_f32 ? 4 : 2;
-  bool vec = aligned16(d.d) && (d.ldd * esz) % 16 == 0 && (d.d_batch_stride * esz) % 16 == 0;
+  bool vec = (rs || aligned16(d.d)) && (d.ldd * esz) % 16 == 0 && (d.d_batch_stride * esz) % 16 == 0;
   if (swiglu) vec = vec && aligned16(d.h) && (d.ldh * 2) % 16 == 0;
   if (d.epilogue == UFP8_EPI_DSWIGLU) vec = vec && aligned16(d.ug) && (d.ldug * 2) % 16 == 0 && (d.ug_batch_stride * 2) % 16 == 0;
   a.vec_ok = vec ? 1 : 0;

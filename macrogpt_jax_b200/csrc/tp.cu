@@ -1,0 +1,257 @@
+// Tensor-parallel reduce-scatter support: peer-mapped staging buffers over NVLink (CUDA IPC,
+// no multicast objects) and the owner-side finish kernel.
+//
+// Protocol for one reduce-scatter of a [T, C] bf16 partial sum over k ranks (rows split in
+// k contiguous blocks of R = T / k):
+//   1. every rank's GEMM epilogue (UFP8_EPI_RS_PUSH) stores row m of its partial into the
+//      owner o = m / R, in o's staging buffer, slot = its own rank:  slot[src][m - o*R][c];
+//   2. ufp8_tp_finish on every rank: each CTA first publishes "my partials for epoch e are
+//      written" by storing e into every peer's flag[src = me] (after a system-scope fence),
+//      then waits until its own flag[src] == e for all src (bounded by a timeout; on expiry
+//      it sets UFP8_STATUS_PEER_TIMEOUT in the status word and stops), then sums the k slots
+//      in fp32 in rank order and writes the bf16 result.
+// Two staging buffers alternate by epoch, so a fast rank that moves on to the next
+// reduce-scatter writes into the other buffer while slower owners are still summing.
+#include <cuda_bf16.h>
+
+#include <cstring>
+#include <vector>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace ufp8 {
+
+constexpr int kMaxRanks = 8;
+constexpr size_t kFlagBytes = 256;  // flag[src] (u32) per buffer, padded
+
+struct TPContext {
+  int device = -1;
+  int rank = 0;
+  int world = 1;
+  size_t slot_bytes = 0;     // one source rank's block in one buffer
+  size_t buffer_bytes = 0;   // flags + world slots
+  char* base = nullptr;      // own allocation: 2 buffers
+  char* peer_base[kMaxRanks] = {};
+  bool peer_opened[kMaxRanks] = {};
+  void** d_slot_ptrs = nullptr;  // device array [2][world]: data region of buffer b on each rank
+  uint64_t epoch = 0;
+  int timeout_ms = 5000;
+};
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct FinishArgs {
+  uint32_t* flags_local;            // this rank's flags of the buffer in use
+  uint32_t* flags_peer[kMaxRanks];  // every rank's flags of the buffer in use
+  const __nv_bfloat16* slots;       // this rank's data region of the buffer in use
+  long long slot_elems;             // elements per slot (R * ld_slot)
+  long long ld_slot;
+  int world, rank;
+  uint32_t epoch;
+  long long rows, cols;
+  __nv_bfloat16* out;
+  long long ld_out;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+__global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
+  __shared__ int ok_shared;
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank, a.epoch);
+    int ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int src = 0; src < a.world && ok; ++src) {
+      while (ld_acquire_sys(a.flags_local + src) != a.epoch) {
+        if (globaltimer_ns() - t0 > a.timeout_ns) {
+          ok = 0;
+          atomicOr(a.status, UFP8_STATUS_PEER_TIMEOUT);
+          break;
+        }
+      }
+    }
+    ok_shared = ok;
+  }
+  __syncthreads();
+  if (!ok_shared) return;
+  const long long cols2 = a.cols / 2;  // bf16 pairs (cols is even)
+  const long long total = a.rows * cols2;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols2, c = (i - r * cols2) * 2;
+    float s0 = 0.0f, s1 = 0.0f;
+    for (int src = 0; src < a.world; ++src) {
+      const __nv_bfloat162 v =
+          *reinterpret_cast<const __nv_bfloat162*>(a.slots + src * a.slot_elems + r * a.ld_slot + c);
+      s0 += __bfloat162float(v.x);
+      s1 += __bfloat162float(v.y);
+    }
+    *reinterpret_cast<__nv_bfloat162*>(a.out + r * a.ld_out + c) = __floats2bfloat162_rn(s0, s1);
+  }
+}
+
+}  // namespace
+
+}  // namespace ufp8
+
+using namespace ufp8;
+
+extern "C" {
+
+int ufp8_tp_create(int rank, int world, int64_t slot_bytes, ufp8_tp_ctx** out, uint8_t* ipc_handle_out) {
+  if (!out || !ipc_handle_out) return set_error(UFP8_ERR_INVALID, "ufp8_tp_create: null pointer");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_create: rank %d / world %d (world must be 1..%d)", rank, world,
+                     kMaxRanks);
+  if (slot_bytes <= 0 || slot_bytes % 256) return set_error(UFP8_ERR_INVALID, "ufp8_tp_create: slot_bytes must be a positive multiple of 256");
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  TPContext* c = new TPContext();
+  c->device = dev->device;
+  c->rank = rank;
+  c->world = world;
+  c->slot_bytes = static_cast<size_t>(slot_bytes);
+  c->buffer_bytes = kFlagBytes + c->slot_bytes * world;
+  cudaError_t e = cudaMalloc(&c->base, 2 * c->buffer_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->buffer_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_slot_ptrs, 2 * kMaxRanks * sizeof(void*));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
+  if (e != cudaSuccess) {
+    if (c->base) cudaFree(c->base);
+    if (c->d_slot_ptrs) cudaFree(c->d_slot_ptrs);
+    delete c;
+    return cuda_error(e, "ufp8_tp_create");
+  }
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  c->peer_base[rank] = c->base;
+  *out = reinterpret_cast<ufp8_tp_ctx*>(c);
+  return UFP8_OK;
+}
+
+int ufp8_tp_connect(ufp8_tp_ctx* ctx, const uint8_t* ipc_handles) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !ipc_handles) return set_error(UFP8_ERR_INVALID, "ufp8_tp_connect: null pointer");
+  cudaError_t e;
+  for (int p = 0; p < c->world; ++p) {
+    if (p == c->rank || c->peer_opened[p]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, ipc_handles + p * UFP8_IPC_HANDLE_BYTES, sizeof(h));
+    void* ptr = nullptr;
+    if ((e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+      return cuda_error(e, "ufp8_tp_connect: cudaIpcOpenMemHandle");
+    c->peer_base[p] = static_cast<char*>(ptr);
+    c->peer_opened[p] = true;
+  }
+  void* host[2 * kMaxRanks] = {};
+  for (int b = 0; b < 2; ++b)
+    for (int p = 0; p < c->world; ++p) host[b * kMaxRanks + p] = c->peer_base[p] + b * c->buffer_bytes + kFlagBytes;
+  if ((e = cudaMemcpy(c->d_slot_ptrs, host, sizeof(host), cudaMemcpyHostToDevice)) != cudaSuccess)
+    return cuda_error(e, "ufp8_tp_connect: peer table");
+  return UFP8_OK;
+}
+
+int ufp8_tp_connect_local(ufp8_tp_ctx* ctx, ufp8_tp_ctx* const* peers) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !peers) return set_error(UFP8_ERR_INVALID, "ufp8_tp_connect_local: null pointer");
+  for (int p = 0; p < c->world; ++p) {
+    const TPContext* q = reinterpret_cast<const TPContext*>(peers[p]);
+    if (!q || q->world != c->world || q->rank != p || q->slot_bytes != c->slot_bytes)
+      return set_error(UFP8_ERR_INVALID, "ufp8_tp_connect_local: peers[%d] is not rank %d of this group", p, p);
+    if (p != c->rank) c->peer_base[p] = q->base;
+  }
+  void* host[2 * kMaxRanks] = {};
+  for (int b = 0; b < 2; ++b)
+    for (int p = 0; p < c->world; ++p) host[b * kMaxRanks + p] = c->peer_base[p] + b * c->buffer_bytes + kFlagBytes;
+  cudaError_t e = cudaMemcpy(c->d_slot_ptrs, host, sizeof(host), cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "ufp8_tp_connect_local: peer table");
+}
+
+int ufp8_tp_destroy(ufp8_tp_ctx* ctx) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c) return UFP8_OK;
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (c->peer_opened[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
+  if (c->d_slot_ptrs) cudaFree(c->d_slot_ptrs);
+  if (c->base) cudaFree(c->base);
+  delete c;
+  return UFP8_OK;
+}
+
+int ufp8_tp_set_timeout_ms(ufp8_tp_ctx* ctx, int ms) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || ms <= 0) return set_error(UFP8_ERR_INVALID, "ufp8_tp_set_timeout_ms: bad argument");
+  c->timeout_ms = ms;
+  return UFP8_OK;
+}
+
+int ufp8_tp_begin(ufp8_tp_ctx* ctx, void* const** slot_table, uint64_t* epoch) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !slot_table || !epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_begin: null pointer");
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_begin: rank %d is not connected", p);
+  c->epoch += 1;
+  *epoch = c->epoch;
+  *slot_table = c->d_slot_ptrs + (c->epoch & 1) * kMaxRanks;
+  return UFP8_OK;
+}
+
+int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols, int64_t ld_slot, void* out,
+                   int64_t ld_out, ufp8_stream_t stream) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !out) return set_error(UFP8_ERR_INVALID, "ufp8_tp_finish: null pointer");
+  if (epoch == 0 || epoch > c->epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_finish: epoch not begun");
+  if (rows < 0 || cols <= 0 || cols % 2 || ld_slot < cols || ld_out < cols || ld_slot % 2 || ld_out % 2)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_finish: bad extents (cols and pitches must be even)");
+  if (static_cast<size_t>(rows * ld_slot * 2) > c->slot_bytes)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_finish: %lld x %lld rows exceed the staging slot", (long long)rows,
+                     (long long)ld_slot);
+  if (reinterpret_cast<uintptr_t>(out) & 3u) return set_error(UFP8_ERR_ALIGN, "ufp8_tp_finish: out not 4-byte aligned");
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_finish: rank %d is not connected", p);
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  const int b = static_cast<int>(epoch & 1);
+  FinishArgs a{};
+  a.flags_local = reinterpret_cast<uint32_t*>(c->base + b * c->buffer_bytes);
+  for (int p = 0; p < c->world; ++p) a.flags_peer[p] = reinterpret_cast<uint32_t*>(c->peer_base[p] + b * c->buffer_bytes);
+  a.slots = reinterpret_cast<const __nv_bfloat16*>(c->base + b * c->buffer_bytes + kFlagBytes);
+  a.slot_elems = static_cast<long long>(c->slot_bytes / 2);
+  a.ld_slot = ld_slot;
+  a.world = c->world;
+  a.rank = c->rank;
+  a.epoch = static_cast<uint32_t>(epoch);
+  a.rows = rows;
+  a.cols = cols;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ld_out = ld_out;
+  a.timeout_ns = static_cast<uint64_t>(c->timeout_ms) * 1000000ull;
+  a.status = dev->status_word;
+  long long pairs = rows * (cols / 2);
+  int grid = static_cast<int>((pairs + 255) / 256);
+  if (grid > dev->sm_count) grid = dev->sm_count;  // every CTA resident: each one only waits on flags
+  if (grid < 1) grid = 1;
+  tp_finish_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "tp finish launch");
+}
+
+int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* out) {
+  const TPContext* c = reinterpret_cast<const TPContext*>(ctx);
+  if (!c || !out) return set_error(UFP8_ERR_INVALID, "ufp8_tp_slot_bytes: null pointer");
+  *out = static_cast<int64_t>(c->slot_bytes);
+  return UFP8_OK;
+}
+
+}  // extern "C"

@@ -110,13 +110,14 @@ def operand(t: Fp8Tensor, major: int, ld: int, batch_stride: int = 0, batch_coun
 def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ldd: int,
          d_batch_stride: int = 0, batch: int = 1, k_batches: int = 1, epilogue: int = C.EPI_STORE,
          h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
-         ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None) -> None:
+         ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None, rs_slots: int | None = None,
+         rs_rank: int = 0, rs_rows_per_rank: int = 0) -> None:
     desc = C.GemmDesc()
     desc.M, desc.N, desc.K = M, N, K
     desc.batch, desc.k_batches = batch, k_batches
     desc.a, desc.b = a, b
-    desc.d = d.data_ptr()
-    desc.d_dtype = C.OUT_F32 if d.dtype == torch.float32 else C.OUT_BF16
+    desc.d = d.data_ptr() if d is not None else None
+    desc.d_dtype = C.OUT_F32 if (d is not None and d.dtype == torch.float32) else C.OUT_BF16
     desc.epilogue = epilogue
     desc.ldd, desc.d_batch_stride = ldd, d_batch_stride
     desc.h = h.data_ptr() if h is not None else None
@@ -124,6 +125,8 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
     desc.ug = ug.data_ptr() if ug is not None else None
     desc.ldug, desc.ug_batch_stride = ldug, ug_batch_stride
     desc.amax_out = amax_out.data_ptr() if amax_out is not None else None
+    if rs_slots is not None:
+        desc.rs_slots, desc.rs_rank, desc.rs_rows_per_rank = rs_slots, rs_rank, rs_rows_per_rank
     n_eff = 2 * N if epilogue == C.EPI_SWIGLU else N
     flops = 2.0 * M * n_eff * K * batch * k_batches
     _launch("gemm", flops, lambda: C.gemm(desc, _stream()))
@@ -211,6 +214,22 @@ def gmlp_b2(qdy: Fp8Tensor, qwd: Fp8Tensor, ug: torch.Tensor):
     gemm(operand(qdy, C.K_MAJOR, d), operand(qwd, C.K_MAJOR, d), T, h, d, dug, h, T * h,
          epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug)
     return dug, amax_dug
+
+
+def gmlp_f2_push(qh: Fp8Tensor, qwd: Fp8Tensor, rs_slots: int, rank: int, rows_per_rank: int) -> None:
+    """y partial = H Wd with every row stored into its owner rank's staging slot (RS_PUSH)."""
+    T, h = qh.q.shape
+    d = qwd.q.shape[1]
+    gemm(operand(qh, C.K_MAJOR, h), operand(qwd, C.MN_MAJOR, d), T, d, h, None, d, epilogue=C.EPI_RS_PUSH,
+         rs_slots=rs_slots, rs_rank=rank, rs_rows_per_rank=rows_per_rank)
+
+
+def gmlp_b4_push(qdug: Fp8Tensor, qwf: Fp8Tensor, rs_slots: int, rank: int, rows_per_rank: int) -> None:
+    """dx partial = sum_i dUG[i] Wf[i]^T stored into the owners' staging slots (RS_PUSH)."""
+    _, T, h = qdug.q.shape
+    d = qwf.q.shape[1]
+    gemm(operand(qdug, C.K_MAJOR, h, T * h, 2), operand(qwf, C.K_MAJOR, h, d * h, 2), T, d, h, None, d,
+         k_batches=2, epilogue=C.EPI_RS_PUSH, rs_slots=rs_slots, rs_rank=rank, rs_rows_per_rank=rows_per_rank)
 
 
 def gmlp_b1(qh: Fp8Tensor, qdy: Fp8Tensor) -> torch.Tensor:

@@ -34,13 +34,50 @@ from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 
 
 class TPContext:
-    """Process group, rank layout and compute backend of one tensor-parallel block."""
+    """Process group, rank layout and compute backend of one tensor-parallel block.
 
-    def __init__(self, group=None, backend=None):
+    With the CUDA backend and `fused_reduce_scatter` the reduce-scatters run over NVLink peer
+    memory: the down-projection / dx GEMM epilogues store each partial row straight into its
+    owner's staging slot (UFP8_EPI_RS_PUSH) and ufp8_tp_finish sums the slots on the owner,
+    so the transfer overlaps the GEMM tile by tile.  Otherwise NCCL's reduce-scatter runs
+    after the GEMM."""
+
+    def __init__(self, group=None, backend=None, fused_reduce_scatter: bool = True):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.be = backend if backend is not None else cuda_ops
+        self.fused_rs = fused_reduce_scatter and backend is None and self.world > 1
+        self._rs = None
+
+    def _rs_ctx(self, slot_bytes: int) -> C.TPReduceScatter:
+        """Collective: (re)creates the peer-mapped staging when a larger slot is needed."""
+        if self._rs is None or self._rs.slot_bytes < slot_bytes:
+            if self._rs is not None:
+                torch.cuda.synchronize()
+                self._rs.close()
+            rs = C.TPReduceScatter(self.rank, self.world, slot_bytes)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, rs.handle, group=self.group)
+            rs.connect(handles)
+            self._rs = rs
+        return self._rs
+
+    def push_reduce_scatter(self, push, rows: int, cols: int, dtype, device) -> torch.Tensor:
+        """Runs `push(slot_table, rank, rows_per_rank)` (a GEMM with the RS_PUSH epilogue over
+        all `rows`) and returns this rank's summed block [rows / k, cols]."""
+        rl = rows // self.world
+        rs = self._rs_ctx(((rl * cols * 2 + 255) // 256) * 256)
+        table, epoch = rs.begin()
+        push(table, self.rank, rl)
+        out = torch.empty((rl, cols), dtype=dtype, device=device)
+        rs.finish(epoch, rl, cols, cols, out.data_ptr(), cols, torch.cuda.current_stream().cuda_stream)
+        return out
+
+    def close(self) -> None:
+        if self._rs is not None:
+            self._rs.close()
+            self._rs = None
 
     def global_amax(self, t: torch.Tensor) -> torch.Tensor:
         a = self.be.amax(t)
@@ -49,6 +86,12 @@ class TPContext:
 
     def quant_global(self, t: torch.Tensor, fmt: int):
         return self.be.quantize(t, fmt, self.global_amax(t))
+
+    def quant_global_many(self, tensors_fmts):
+        """Quantises several tensors with whole-tensor scales using ONE MAX all-reduce."""
+        amaxes = torch.cat([self.be.amax(t) for t, _ in tensors_fmts])
+        dist.all_reduce(amaxes, op=dist.ReduceOp.MAX, group=self.group)
+        return [self.be.quantize(t, f, amaxes[i:i + 1]) for i, (t, f) in enumerate(tensors_fmts)]
 
     def all_gather_tokens(self, q):
         """Concatenates every rank's fp8 token shard [T/k, d] into [T, d] (rank order)."""
@@ -70,13 +113,17 @@ class _TPGMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, wf, wd, tp: TPContext):
         be = tp.be
-        qx = tp.all_gather_tokens(tp.quant_global(x, C.E4M3))
-        qwf = tp.quant_global(wf, C.E4M3)
+        qx_local, qwf, qwd = tp.quant_global_many([(x, C.E4M3), (wf, C.E4M3), (wd, C.E4M3)])
+        qx = tp.all_gather_tokens(qx_local)
         ug, hid, amax_h = be.gmlp_f1(qx, qwf)
         dist.all_reduce(amax_h, op=dist.ReduceOp.MAX, group=tp.group)
         qh = be.quantize(hid, C.E4M3, amax_h)
-        qwd = tp.quant_global(wd, C.E4M3)
-        y = tp.reduce_scatter_tokens(be.gmlp_f2(qh, qwd))
+        if tp.fused_rs:
+            T, d = qh.q.shape[0], qwd.q.shape[1]
+            y = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_f2_push(qh, qwd, tab, r, rl), T, d,
+                                       torch.bfloat16, qh.q.device)
+        else:
+            y = tp.reduce_scatter_tokens(be.gmlp_f2(qh, qwd))
         ctx.tp = tp
         ctx.saved = (qx, qwf, ug, qh, qwd)
         return y
@@ -92,7 +139,12 @@ class _TPGMLPFn(torch.autograd.Function):
         dist.all_reduce(amax_dug, op=dist.ReduceOp.MAX, group=tp.group)
         dwd = be.gmlp_b1(qh, qdy)
         qdug = be.quantize(dug, C.E5M2, amax_dug)
-        dx = tp.reduce_scatter_tokens(be.gmlp_b4(qdug, qwf))
+        if tp.fused_rs:
+            T, d = qdug.q.shape[1], qwf.q.shape[1]
+            dx = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_b4_push(qdug, qwf, tab, r, rl), T, d,
+                                        torch.bfloat16, qdug.q.device)
+        else:
+            dx = tp.reduce_scatter_tokens(be.gmlp_b4(qdug, qwf))
         dwf = be.gmlp_b3(qx, qdug)
         return dx, dwf, dwd, None
 
@@ -110,11 +162,11 @@ class TPGMLP(torch.nn.Module):
 
     def __init__(self, model_d: int, hidden_d: Optional[int] = None, activation_fn: Callable = None,
                  param_dtype: torch.dtype = torch.bfloat16, *, rngs: Rngs, mesh=None, group=None, device=None,
-                 fused_init=lecun_normal_init, down_init=zeros_init, backend=None):
+                 fused_init=lecun_normal_init, down_init=zeros_init, backend=None, fused_reduce_scatter: bool = True):
         super().__init__()
         hidden_d = 4 * model_d if hidden_d is None else hidden_d
         group = group if group is not None else mesh
-        self.tp = TPContext(group, backend)
+        self.tp = TPContext(group, backend, fused_reduce_scatter)
         k, r = self.tp.world, self.tp.rank
         if hidden_d % k:
             raise ValueError(f"hidden {hidden_d} is not divisible by the tensor-parallel size {k}")

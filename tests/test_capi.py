@@ -42,7 +42,7 @@ def test_header_constants_match_binding():
 def test_struct_layout_matches_header():
     """Sizes and offsets as gcc lays out ufp8_operand / ufp8_gemm_desc on x86-64."""
     assert ctypes.sizeof(C.Operand) == 48
-    assert ctypes.sizeof(C.GemmDesc) == 208
+    assert ctypes.sizeof(C.GemmDesc) == 232
     assert (C.GemmDesc.a.offset, C.GemmDesc.b.offset, C.GemmDesc.d.offset, C.GemmDesc.amax_out.offset) == \
         (32, 80, 128, 200)
 

@@ -21,7 +21,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, fused=True):
     import sys
     import torch.distributed as dist
     sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
@@ -35,7 +35,8 @@ def _worker(rank, world, port, outdir):
         from oracle import path as op
         dev = torch.device("cuda", rank)
         m = TPGMLP(D, H, rngs=Rngs(7), device=dev, fused_init=scaled_normal_init(D ** -0.5),
-                   down_init=scaled_normal_init(H ** -0.5))
+                   down_init=scaled_normal_init(H ** -0.5), fused_reduce_scatter=fused)
+        assert m.tp.fused_rs == fused
         rng = np.random.default_rng(0)
         xb = op.bf16_normal(rng, (T, D))
         dyb = op.bf16_normal(rng, (T, D), 1e-3)
@@ -45,13 +46,17 @@ def _worker(rank, world, port, outdir):
         y.backward(m.shard_tokens(to_t(dyb)))
         torch.cuda.synchronize()
         bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        from macrogpt_jax_b200 import _capi
+        assert _capi.device_status() == 0
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=bits(y), dx=bits(x.grad),
                  dwf=bits(m.fused_proj.w.grad), dwd=bits(m.down_proj.w.grad))
+        m.tp.close()
     finally:
         dist.destroy_process_group()
 
 
-def test_tp2_gpu_matches_oracle(cuda, tmp_path):
+@pytest.mark.parametrize("fused", [True, False], ids=["p2p_reduce_scatter", "nccl_reduce_scatter"])
+def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -60,7 +65,7 @@ def test_tp2_gpu_matches_oracle(cuda, tmp_path):
     from macrogpt_jax_b200.mlp import GMLP
     from oracle import path as op
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), fused), nprocs=2, join=True)
     r = [np.load(tmp_path / f"rank{i}.npz") for i in range(2)]
     cpu = torch.device("cpu")
     full = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5), device=cpu),

@@ -1,0 +1,66 @@
+"""Reduce-scatter contexts on one GPU: the RS_PUSH epilogue + finish data path (world size 1)
+and the failure path — a peer that never signals makes the bounded wait run out and report
+UFP8_STATUS_PEER_TIMEOUT instead of hanging.  No kernel here waits on another kernel."""
+import time
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_rs_push_world1_matches_store(cuda):
+    """F2 with the RS_PUSH epilogue into a one-rank staging slot, then finish: bit-identical
+    to the plain-store epilogue (one slot summed in fp32 is exact)."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200 import ops
+    T, h, d = 512, 384, 256
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(3)
+    qh = ops.quantize(torch.randn((T, h), generator=gen, device=cuda).to(torch.bfloat16), C.E4M3)
+    qwd = ops.quantize((torch.randn((h, d), generator=gen, device=cuda) * 0.05).to(torch.bfloat16), C.E4M3)
+    y_ref = ops.gmlp_f2(qh, qwd)
+    rs = C.TPReduceScatter(0, 1, T * d * 2)
+    rs.connect([rs.handle])
+    for _ in range(3):  # both staging buffers, then reuse
+        table, epoch = rs.begin()
+        ops.gmlp_f2_push(qh, qwd, table, 0, T)
+        out = torch.empty(T, d, dtype=torch.bfloat16, device=cuda)
+        rs.finish(epoch, T, d, d, out.data_ptr(), d, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(out, y_ref)
+    assert C.device_status() == 0
+    rs.close()
+
+
+def test_missing_peer_times_out(cuda):
+    """Rank 0 of a two-rank group whose rank 1 never finishes: rank 0's finish gives up after
+    its 200 ms limit, sets the peer-timeout status bit, and the GPU stays usable."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    rows, cols = 64, 64
+    a = C.TPReduceScatter(0, 2, rows * cols * 2)
+    b = C.TPReduceScatter(1, 2, rows * cols * 2)
+    a.connect_local([a, b])
+    b.connect_local([a, b])
+    a.set_timeout_ms(200)
+    _, epoch = a.begin()
+    out = torch.zeros(rows, cols, dtype=torch.bfloat16, device=cuda)
+    t0 = time.time()
+    a.finish(epoch, rows, cols, cols, out.data_ptr(), cols, torch.cuda.current_stream().cuda_stream)
+    status = C.device_status(clear=True)
+    assert status & C.STATUS_PEER_TIMEOUT
+    assert time.time() - t0 < 10
+    assert C.device_status() == 0
+    x = torch.ones(10, device=cuda)
+    assert float((x * 2).sum()) == 20.0
+    a.close()
+    b.close()
+
+
+def test_unconnected_context_is_refused(cuda):
+    from macrogpt_jax_b200 import _capi as C
+    a = C.TPReduceScatter(0, 2, 256)
+    with pytest.raises(C.UFP8Error, match="not connected"):
+        a.begin()
+    a.close()
