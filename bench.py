@@ -451,11 +451,15 @@ def main():
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
 
+    # Libraries (NCCL's version banner, for one) write to file descriptor 1; send all of that
+    # to stderr so that stdout carries exactly the one JSON line printed below.
+    sys.stdout.flush()
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.impl == "reference":
         out = run_reference(args, cfg, rank, world)
     else:
         if world > 1:
-            os.environ.setdefault("NCCL_DEBUG", "WARN")  # no version banner on stdout: one JSON line
             import datetime
             import torch
             import torch.distributed as dist
@@ -469,7 +473,7 @@ def main():
                 import torch.distributed as dist
                 dist.destroy_process_group()
     if out is not None:
-        print(json.dumps(out), flush=True)
+        print(json.dumps(out), file=json_out, flush=True)
 
 
 if __name__ == "__main__":

@@ -401,12 +401,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 // issues tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 32) and signals its commits to
 // both CTAs' barriers; both CTAs' loads complete on the even CTA's "full" barrier.  Eight
 // epilogue warps per CTA (two per TMEM lane quadrant, splitting the columns).
+//
+// The RS_PUSH instantiation (STAGED) trades two ring stages for a per-warp staging area:
+// each epilogue warp converts 64 columns of its 32 rows into shared memory (rows padded to
+// 144 B, so the 16-byte writes of a warp spread over all banks) and every lane then sends
+// its own 128-byte row segment with one cp.async.bulk store.  Stores into a peer GPU's
+// memory then leave as bulk transfers issued by the copy engine of the SM, not as 16-byte
+// writes that stall the epilogue warp (plain remote stores reach ~170 GB/s; bulk ones run
+// at link rate), and the warp moves on as soon as the row has been read out of shared memory.
 constexpr int kPStages = 7;
+constexpr int kPStagesStaged = 5;
 constexpr int kPHalfBytes = 128 * kBK;            // 16 KiB: 128 rows x 128 B
 constexpr int kPStageBytes = 2 * kPHalfBytes;     // A half + B half
 constexpr int kPEpiWarps = 8;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;   // 320
-constexpr int kPSmemBytes = kPStages * kPStageBytes + kBarrierBytes + 1024;
+constexpr int kPStgCols = 64;                     // columns per staged row segment
+constexpr int kPStgStride = kPStgCols * 2 + 16;   // 144 B: padded row pitch
+constexpr int kPStgWarpBytes = 32 * kPStgStride;  // 4.5 KiB per epilogue warp
+constexpr int kPStgBytes = kPEpiWarps * kPStgWarpBytes;
+constexpr int pair_smem_bytes(int stages, bool staged) {
+  return stages * kPStageBytes + (staged ? kPStgBytes : 0) + kBarrierBytes + 1024;
+}
+constexpr int kPSmemBytes = pair_smem_bytes(kPStages, false);
+constexpr int kPSmemBytesStaged = pair_smem_bytes(kPStagesStaged, true);
+static_assert(kPSmemBytesStaged <= 232448, "staged CTA-pair kernel exceeds shared memory");
+static_assert(kPSmemBytes <= 232448, "CTA-pair kernel exceeds shared memory");
 
 // Stores 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]).
 __device__ __forceinline__ void store_bf16x32_packed(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
@@ -514,14 +533,16 @@ __device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[16], int j) {
   return (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
 }
 
+template <int NSTAGES, bool kStaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPStages * kPStageBytes);
-  uint64_t* empty = full + kPStages;
-  uint64_t* tfull = empty + kPStages;
+  uint8_t* staging = smem + NSTAGES * kPStageBytes;  // kStaged only
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + (kStaged ? kPStgBytes : 0));
+  uint64_t* empty = full + NSTAGES;
+  uint64_t* tfull = empty + NSTAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -533,7 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   const bool leader = rank == 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPStages; ++s) {
+    for (int s = 0; s < NSTAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -604,7 +625,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             tma_load_3d_pair(sb, &tmB, bar, k0, n0, bz);
           else
             tma_load_3d_pair(sb, &tmB, bar, n0, k0, bz);
-          if (++stage == kPStages) {
+          if (++stage == NSTAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -614,7 +635,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         // Both CTAs' loads for a stage complete on the leader's barrier: wait for every
         // armed stage so that no load is still in flight when the cluster exits.
         volatile int never = 0;
-        for (int s = 0; s < kPStages; ++s)
+        for (int s = 0; s < NSTAGES; ++s)
           if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never);
       }
     }
@@ -649,7 +670,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | kk) != 0 ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
-          if (++stage == kPStages) {
+          if (++stage == NSTAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -687,7 +708,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
 
-      if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH) {
+      if (kStaged) {
+        // RS_PUSH through shared memory: 64-column row segments leave as bulk stores.
+        __nv_bfloat16* rs_row = nullptr;
+        if (row_ok) {
+          const long long owner = row / args.rs_rows;
+          rs_row = static_cast<__nv_bfloat16*>(args.rs_slots[owner]) +
+                   (args.rs_rank * args.rs_rows + (row - owner * args.rs_rows)) * args.ldd;
+        }
+        uint8_t* stg_row = staging + e * kPStgWarpBytes + lane * kPStgStride;
+#pragma unroll 1
+        for (int c = chalf * 128; c < chalf * 128 + 128; c += kPStgCols) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(tbase + c, r0);
+          tmem_ld_32x32b_x32(tbase + c + 32, r1);
+          tmem_ld_wait();
+          const int col0 = nb * kBN + c;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            uint32_t o0[16], o1[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              o0[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * alpha, __uint_as_float(r0[2 * j + 1]) * alpha);
+              o1[j] = pack_bf16x2(__uint_as_float(r1[2 * j]) * alpha, __uint_as_float(r1[2 * j + 1]) * alpha);
+            }
+            if (valid >= kPStgCols) {
+              bulk_wait_read_all();  // the previous segment has left this row's staging
+              uint4* srow = reinterpret_cast<uint4*>(stg_row);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                srow[i] = make_uint4(o0[4 * i], o0[4 * i + 1], o0[4 * i + 2], o0[4 * i + 3]);
+                srow[4 + i] = make_uint4(o1[4 * i], o1[4 * i + 1], o1[4 * i + 2], o1[4 * i + 3]);
+              }
+              fence_proxy_async_smem();
+              bulk_store_s2g(rs_row + col0, smem_u32(stg_row), kPStgCols * 2);
+              bulk_commit();
+            } else {
+              store_bf16x32_packed(rs_row + col0, o0, valid, true);
+              if (valid > 32) store_bf16x32_packed(rs_row + col0 + 32, o1, valid - 32, true);
+            }
+          }
+        }
+      } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH) {
         // RS_PUSH: this row goes to its owner's staging slot for this rank (peer memory).
         __nv_bfloat16* rs_row = nullptr;
         if (args.mode == UFP8_EPI_RS_PUSH && row_ok) {
@@ -821,7 +883,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       amax = __reduce_max_sync(0xFFFFFFFFu, amax);
       if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
     }
-    // Peer stores must be visible system-wide before the finish kernel's flag write.
+    // Peer stores must be complete and visible system-wide before the finish kernel's flag write.
+    if (kStaged) bulk_wait_all();
     if (args.mode == UFP8_EPI_RS_PUSH) __threadfence_system();
   }
 
@@ -1036,33 +1099,48 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (attr_device != dev.device) {
     e = cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kPSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesStaged, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesStaged);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
+  // RS_PUSH goes through the staged kernel whenever its rows are 16-byte aligned.
+  const bool staged = rs && vec;
+  const void* pair_fn = staged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, true>)
+                               : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, false>);
+  const int pair_smem = staged ? kPSmemBytesStaged : kPSmemBytes;
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device = -1, max_clusters = 0;
-    if (occ_device != dev.device) {
+    static thread_local int occ_device[2] = {-1, -1}, occ_clusters[2] = {0, 0};
+    const int oi = staged ? 1 : 0;
+    if (occ_device[oi] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
       cfg.blockDim = dim3(kPThreads, 1, 1);
-      cfg.dynamicSmemBytes = kPSmemBytes;
+      cfg.dynamicSmemBytes = pair_smem;
       int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, gemm_fp8_pair_kernel, &cfg);
+      e = cudaOccupancyMaxActiveClusters(&n, pair_fn, &cfg);
       if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
       if (n < 1) return set_error(UFP8_ERR_DEVICE, "no CTA pair of the GEMM kernel fits on this device");
-      max_clusters = n;
-      occ_device = dev.device;
+      occ_clusters[oi] = n;
+      occ_device[oi] = dev.device;
     }
+    const int max_clusters = occ_clusters[oi];
     // Persistent grid: no more clusters than can be resident at once.
     if (ctas_override <= 0 || ctas > 2 * max_clusters) ctas = 2 * max_clusters;
     long long clusters = ctas / 2;
     if (clusters < 1) clusters = 1;
     if (num_tiles < clusters) clusters = num_tiles;
-    gemm_fp8_pair_kernel<<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytes, stream>>>(tmA, tmB, a);
+    if (staged)
+      gemm_fp8_pair_kernel<kPStagesStaged, true>
+          <<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytesStaged, stream>>>(tmA, tmB, a);
+    else
+      gemm_fp8_pair_kernel<kPStages, false><<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytes, stream>>>(tmA, tmB, a);
   } else {
     if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
     gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);

@@ -63,6 +63,7 @@ struct FinishArgs {
   long long ld_out;
   uint64_t timeout_ns;
   int* status;
+  int vec8;  // cols, pitches and out allow 16-byte accesses
 };
 
 __global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
@@ -85,10 +86,41 @@ __global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
   }
   __syncthreads();
   if (!ok_shared) return;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  if (a.vec8) {
+    // 8 columns per thread: one 16-byte load per slot, fp32 sums, one 16-byte store.
+    const long long cols8 = a.cols / 8;
+    const long long total8 = a.rows * cols8;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total8; i += stride) {
+      const long long r = i / cols8, c = (i - r * cols8) * 8;
+      uint4 v8[kMaxRanks];
+#pragma unroll
+      for (int src = 0; src < kMaxRanks; ++src)  // all loads in flight before the sums
+        if (src < a.world) v8[src] = *reinterpret_cast<const uint4*>(a.slots + src * a.slot_elems + r * a.ld_slot + c);
+      float acc[8] = {};
+#pragma unroll
+      for (int src = 0; src < kMaxRanks; ++src) {
+        if (src >= a.world) break;
+        const uint32_t w[4] = {v8[src].x, v8[src].y, v8[src].z, v8[src].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] += __uint_as_float(w[j] << 16);
+          acc[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+        o[j] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+      *reinterpret_cast<uint4*>(a.out + r * a.ld_out + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    return;
+  }
   const long long cols2 = a.cols / 2;  // bf16 pairs (cols is even)
   const long long total = a.rows * cols2;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
     const long long r = i / cols2, c = (i - r * cols2) * 2;
     float s0 = 0.0f, s1 = 0.0f;
     for (int src = 0; src < a.world; ++src) {
@@ -238,9 +270,13 @@ int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols,
   a.ld_out = ld_out;
   a.timeout_ns = static_cast<uint64_t>(c->timeout_ms) * 1000000ull;
   a.status = dev->status_word;
-  long long pairs = rows * (cols / 2);
-  int grid = static_cast<int>((pairs + 255) / 256);
-  if (grid > dev->sm_count) grid = dev->sm_count;  // every CTA resident: each one only waits on flags
+  a.vec8 = (cols % 8 == 0 && ld_slot % 8 == 0 && ld_out % 8 == 0 && (c->slot_bytes % 16) == 0 &&
+            (reinterpret_cast<uintptr_t>(out) & 15u) == 0)
+               ? 1
+               : 0;
+  const long long items = a.vec8 ? rows * (cols / 8) : rows * (cols / 2);
+  int grid = static_cast<int>((items + 255) / 256);
+  if (grid > 4 * dev->sm_count) grid = 4 * dev->sm_count;  // all resident (256 threads, no shared memory)
   if (grid < 1) grid = 1;
   tp_finish_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   cudaError_t e = cudaGetLastError();

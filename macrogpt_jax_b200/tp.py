@@ -63,16 +63,19 @@ class TPContext:
             self._rs = rs
         return self._rs
 
-    def push_reduce_scatter(self, push, rows: int, cols: int, dtype, device) -> torch.Tensor:
+    def push_reduce_scatter(self, push, rows: int, cols: int, dtype, device, between=None):
         """Runs `push(slot_table, rank, rows_per_rank)` (a GEMM with the RS_PUSH epilogue over
-        all `rows`) and returns this rank's summed block [rows / k, cols]."""
+        all `rows`), then `between()` if given (independent work that runs while the peers'
+        pushes land), then the finish; returns (this rank's summed block [rows / k, cols],
+        between's result)."""
         rl = rows // self.world
         rs = self._rs_ctx(((rl * cols * 2 + 255) // 256) * 256)
         table, epoch = rs.begin()
         push(table, self.rank, rl)
+        mid = between() if between is not None else None
         out = torch.empty((rl, cols), dtype=dtype, device=device)
         rs.finish(epoch, rl, cols, cols, out.data_ptr(), cols, torch.cuda.current_stream().cuda_stream)
-        return out
+        return out, mid
 
     def close(self) -> None:
         if self._rs is not None:
@@ -120,8 +123,8 @@ class _TPGMLPFn(torch.autograd.Function):
         qh = be.quantize(hid, C.E4M3, amax_h)
         if tp.fused_rs:
             T, d = qh.q.shape[0], qwd.q.shape[1]
-            y = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_f2_push(qh, qwd, tab, r, rl), T, d,
-                                       torch.bfloat16, qh.q.device)
+            y, _ = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_f2_push(qh, qwd, tab, r, rl), T, d,
+                                          torch.bfloat16, qh.q.device)
         else:
             y = tp.reduce_scatter_tokens(be.gmlp_f2(qh, qwd))
         ctx.tp = tp
@@ -141,11 +144,11 @@ class _TPGMLPFn(torch.autograd.Function):
         qdug = be.quantize(dug, C.E5M2, amax_dug)
         if tp.fused_rs:
             T, d = qdug.q.shape[1], qwf.q.shape[1]
-            dx = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_b4_push(qdug, qwf, tab, r, rl), T, d,
-                                        torch.bfloat16, qdug.q.device)
+            dx, dwf = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_b4_push(qdug, qwf, tab, r, rl), T, d,
+                                             torch.bfloat16, qdug.q.device, between=lambda: be.gmlp_b3(qx, qdug))
         else:
             dx = tp.reduce_scatter_tokens(be.gmlp_b4(qdug, qwf))
-        dwf = be.gmlp_b3(qx, qdug)
+            dwf = be.gmlp_b3(qx, qdug)
         return dx, dwf, dwd, None
 
 
