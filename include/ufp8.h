@@ -178,11 +178,14 @@ int ufp8_device_status(int* status, int clear);
 int ufp8_set_gemm_ctas(int ctas);
 
 /* GEMM kernel variant for this process: UFP8_GEMM_AUTO (default: the CTA-pair kernel),
- * UFP8_GEMM_SINGLE_CTA (128 x 256 tiles, one CTA each) or UFP8_GEMM_CTA_PAIR (256 x 256
- * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2). */
+ * UFP8_GEMM_SINGLE_CTA (128 x 256 tiles, one CTA each), UFP8_GEMM_CTA_PAIR (256 x 256
+ * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2; RS_PUSH rows leave through
+ * shared memory as bulk async stores) or UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with
+ * RS_PUSH rows written by plain 16-byte stores from registers). */
 #define UFP8_GEMM_AUTO 0
 #define UFP8_GEMM_SINGLE_CTA 1
 #define UFP8_GEMM_CTA_PAIR 2
+#define UFP8_GEMM_CTA_PAIR_DIRECT 3
 int ufp8_set_gemm_variant(int variant);
 
 /* Tile raster of the persistent GEMM: how many M tiles form a group that is swept along N

@@ -18,7 +18,7 @@ E4M3, E5M2 = 0, 1
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH = 0, 1, 2, 3
-GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR = 0, 1, 2
+GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT = 0, 1, 2, 3
 
 EXPORTED_SYMBOLS = (
     "ufp8_last_error",

@@ -709,7 +709,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
 
       if (kStaged) {
-        // RS_PUSH through shared memory: 64-column row segments leave as bulk stores.
+        // RS_PUSH through shared memory: 64-column row segments leave as bulk stores into
+        // the row owner's staging slot.
         __nv_bfloat16* rs_row = nullptr;
         if (row_ok) {
           const long long owner = row / args.rs_rows;
@@ -1107,8 +1108,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
-  // RS_PUSH goes through the staged kernel whenever its rows are 16-byte aligned.
-  const bool staged = rs && vec;
+  // RS_PUSH goes through the staged kernel whenever its rows are 16-byte aligned.  (Local
+  // outputs keep the direct stores and the deeper ring: at these tile sizes their stores
+  // never limit the epilogue, while two more ring stages help the long-K contractions.)
+  const bool staged = pair && variant != UFP8_GEMM_CTA_PAIR_DIRECT && vec && rs;
   const void* pair_fn = staged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, true>)
                                : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, false>);
   const int pair_smem = staged ? kPSmemBytesStaged : kPSmemBytes;

@@ -138,7 +138,7 @@ def main():
     ap.add_argument("--gemms", default=",".join(ALL))
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=2)
-    ap.add_argument("--variant", type=int, default=0, help="0 auto, 1 one CTA per tile, 2 CTA pair")
+    ap.add_argument("--variant", type=int, default=0, help="0 auto, 1 one CTA per tile, 2 CTA pair, 3 CTA pair with direct stores")
     ap.add_argument("--seconds", type=float, default=0.0, help="sustained loop length per GEMM (0 = off)")
     ap.add_argument("--cublas", action="store_true", help="also time cuBLAS fp8 GEMMs of the same shapes")
     ap.add_argument("--group-m", type=int, default=0, help="tile raster group (0 = library default)")

@@ -8,29 +8,37 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_rs_push_world1_matches_store(cuda):
+@pytest.mark.parametrize("variant", [0, 3], ids=["staged", "direct"])
+@pytest.mark.parametrize("d", [256, 208], ids=["d256", "ragged_cols"])
+def test_rs_push_world1_matches_store(cuda, variant, d):
     """F2 with the RS_PUSH epilogue into a one-rank staging slot, then finish: bit-identical
-    to the plain-store epilogue (one slot summed in fp32 is exact)."""
+    to the plain-store epilogue (one slot summed in fp32 is exact).  Covers the staged
+    (bulk-store) and direct kernels and a ragged last column block (208 = 3 x 64 + 16, whose
+    last 16 columns take the plain-store fallback)."""
     import torch
     from macrogpt_jax_b200 import _capi as C
     from macrogpt_jax_b200 import ops
-    T, h, d = 512, 384, 256
+    C.set_gemm_variant(variant)
+    T, h = 512, 384
     gen = torch.Generator(device=cuda)
     gen.manual_seed(3)
     qh = ops.quantize(torch.randn((T, h), generator=gen, device=cuda).to(torch.bfloat16), C.E4M3)
     qwd = ops.quantize((torch.randn((h, d), generator=gen, device=cuda) * 0.05).to(torch.bfloat16), C.E4M3)
     y_ref = ops.gmlp_f2(qh, qwd)
-    rs = C.TPReduceScatter(0, 1, T * d * 2)
+    rs = C.TPReduceScatter(0, 1, ((T * d * 2 + 255) // 256) * 256)
     rs.connect([rs.handle])
-    for _ in range(3):  # both staging buffers, then reuse
-        table, epoch = rs.begin()
-        ops.gmlp_f2_push(qh, qwd, table, 0, T)
-        out = torch.empty(T, d, dtype=torch.bfloat16, device=cuda)
-        rs.finish(epoch, T, d, d, out.data_ptr(), d, torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
-        assert torch.equal(out, y_ref)
-    assert C.device_status() == 0
-    rs.close()
+    try:
+        for _ in range(3):  # both staging buffers, then reuse
+            table, epoch = rs.begin()
+            ops.gmlp_f2_push(qh, qwd, table, 0, T)
+            out = torch.empty(T, d, dtype=torch.bfloat16, device=cuda)
+            rs.finish(epoch, T, d, d, out.data_ptr(), d, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            assert torch.equal(out, y_ref)
+        assert C.device_status() == 0
+    finally:
+        rs.close()
+        C.set_gemm_variant(0)
 
 
 def test_missing_peer_times_out(cuda):
