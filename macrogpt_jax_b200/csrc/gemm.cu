@@ -52,6 +52,7 @@ struct GemmArgs {
   unsigned int* amax_bits;
   int* status;
   int group_m;  // tile raster: M tiles per group swept before moving along N
+  int m_shift;  // rotation of the M tile index (RS_PUSH: start at this rank's own rows)
   void* const* rs_slots;  // RS_PUSH: owners' staging slots
   int rs_rank;
   long long rs_rows;
@@ -68,6 +69,8 @@ __device__ __forceinline__ void map_tile(int tile, const GemmArgs& a, int& g, in
   const int rr = r - grp * span;
   mb = first_m + rr % gm;
   nb = rr / gm;
+  mb += a.m_shift;
+  if (mb >= a.tiles_m) mb -= a.tiles_m;
 }
 
 __device__ __forceinline__ uint32_t bf16_bits(float v) {
@@ -1076,6 +1079,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   const int bn = swiglu ? 128 : kBN;
   a.tiles_n = static_cast<int>((d.N + bn - 1) / bn);
   a.ksteps = static_cast<int>((d.K + kBK - 1) / kBK);
+  // RS_PUSH: every rank computes the same tile sequence, so without a rotation all ranks
+  // would push into the same owner at the same time and share its inbound links.  Rank r
+  // starts at its own rows instead; at any moment the ranks then write to different owners.
+  a.m_shift = rs ? static_cast<int>((static_cast<int64_t>(d.rs_rank) * d.rs_rows_per_rank / bm) % a.tiles_m) : 0;
   a.idesc = (1u << 4)                                       // f32 accumulator
             | (static_cast<uint32_t>(d.a.fmt) << 7)         // A format
             | (static_cast<uint32_t>(d.b.fmt) << 10)        // B format

@@ -34,17 +34,44 @@ def test_header_constants_match_binding():
     assert int(consts["UFP8_ERR_ALIGN"]) == C.ERR_ALIGN
     assert (int(consts["UFP8_E4M3"]), int(consts["UFP8_E5M2"])) == (C.E4M3, C.E5M2)
     assert (int(consts["UFP8_K_MAJOR"]), int(consts["UFP8_MN_MAJOR"])) == (C.K_MAJOR, C.MN_MAJOR)
-    assert (int(consts["UFP8_EPI_STORE"]), int(consts["UFP8_EPI_SWIGLU"]), int(consts["UFP8_EPI_DSWIGLU"])) == \
-        (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU)
+    assert (int(consts["UFP8_EPI_STORE"]), int(consts["UFP8_EPI_SWIGLU"]), int(consts["UFP8_EPI_DSWIGLU"]),
+            int(consts["UFP8_EPI_RS_PUSH"])) == (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU, C.EPI_RS_PUSH)
+    assert tuple(int(consts[k]) for k in ("UFP8_GEMM_AUTO", "UFP8_GEMM_SINGLE_CTA", "UFP8_GEMM_CTA_PAIR",
+                                          "UFP8_GEMM_CTA_PAIR_DIRECT")) == \
+        (C.GEMM_AUTO, C.GEMM_SINGLE_CTA, C.GEMM_CTA_PAIR, C.GEMM_CTA_PAIR_DIRECT)
+    assert (int(consts["UFP8_STATUS_WAIT_TIMEOUT"]), int(consts["UFP8_STATUS_PEER_TIMEOUT"]),
+            int(consts["UFP8_IPC_HANDLE_BYTES"])) == (C.STATUS_WAIT_TIMEOUT, C.STATUS_PEER_TIMEOUT, C.IPC_HANDLE_BYTES)
     assert int(consts["UFP8_ABI_VERSION"]) == C.load().ufp8_abi_version()
 
 
-def test_struct_layout_matches_header():
-    """Sizes and offsets as gcc lays out ufp8_operand / ufp8_gemm_desc on x86-64."""
-    assert ctypes.sizeof(C.Operand) == 48
-    assert ctypes.sizeof(C.GemmDesc) == 232
-    assert (C.GemmDesc.a.offset, C.GemmDesc.b.offset, C.GemmDesc.d.offset, C.GemmDesc.amax_out.offset) == \
-        (32, 80, 128, 200)
+def test_struct_layout_matches_header(tmp_path):
+    """Every field offset and struct size of the ctypes mirrors equals what the C compiler
+    makes of include/ufp8.h."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    checks = [("ufp8_operand", C.Operand), ("ufp8_gemm_desc", C.GemmDesc)]
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ufp8.h"', "int main(void) {"]
+    for cname, py in checks:
+        lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in py._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    include = Path(__file__).resolve().parents[1] / "include"
+    subprocess.run([cc, "-I", str(include), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        struct, field, value = line.split()
+        got[(struct, field)] = int(value)
+    for cname, py in checks:
+        assert got[(cname, "sizeof")] == ctypes.sizeof(py), cname
+        for fname, _ in py._fields_:
+            assert got[(cname, fname)] == getattr(py, fname).offset, (cname, fname)
 
 
 @pytest.mark.parametrize("call,code,msg", [
