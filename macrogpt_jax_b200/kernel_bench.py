@@ -3,6 +3,7 @@
     python -m macrogpt_jax_b200.kernel_bench [--tokens T] [--d D] [--hidden H]
                                              [--gemms F1,F2,B2,B1,B4,B3] [--reps R] [--warmup W]
                                              [--variant V] [--seconds S] [--cublas]
+                                             [--quant | --rs-push]
 
 Each named GEMM of the GMLP step runs R times after W warm-up launches on seeded fp8
 operands; the script prints one line per GEMM with its mean duration and TFLOP/s.  With
@@ -101,6 +102,68 @@ def sustained(fn, seconds: float, gpu: int):
     return ms, mhz, power, samples
 
 
+def _time_us(fn, reps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) * 1000.0 / reps
+
+
+def rs_push_bench(args, dev):
+    """The down-projection (F2) and dx (B4) GEMMs of a TP-k GMLP shard (hidden h/k) on GPU 0,
+    storing locally vs pushing every row into its owner's reduce-scatter slot (RS_PUSH) with
+    owner 0 on GPU 0 and owners 1..k-1 on GPU 1 through a peer mapping; checks the pushed rows
+    bit for bit and prints the achieved remote bytes per second.  Needs 2 GPUs with peer access."""
+    if torch.cuda.device_count() < 2 or not torch.cuda.can_device_access_peer(0, 1):
+        raise SystemExit("--rs-push needs two GPUs with peer access")
+    from cuda.bindings import runtime as rt
+    err = rt.cudaDeviceEnablePeerAccess(1, 0)[0]
+    if err not in (rt.cudaError_t.cudaSuccess, rt.cudaError_t.cudaErrorPeerAccessAlreadyEnabled):
+        raise SystemExit(f"cudaDeviceEnablePeerAccess: {err}")
+    T, d = args.tokens, args.d
+    peer = torch.device("cuda", 1)
+    for world in (2, 4, 8):
+        hl = args.hidden // world
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(3)
+        qh = _fp8((T, hl), C.E4M3, dev, gen)
+        qwd = _fp8((hl, d), C.E4M3, dev, gen, hl ** -0.5)
+        qdug = _fp8((2, T, hl), C.E5M2, dev, gen, 1e-3)
+        qwf = _fp8((2, d, hl), C.E4M3, dev, gen, d ** -0.5)
+        rl = T // world
+        own = torch.empty((rl * world, d), dtype=torch.bfloat16, device=dev)
+        remote = torch.zeros((world, rl * world, d), dtype=torch.bfloat16, device=peer)
+        torch.cuda.synchronize(peer)
+        table = torch.tensor([own.data_ptr()] + [remote[o].data_ptr() for o in range(1, world)],
+                             dtype=torch.int64, device=dev)
+        y_ref = ops.gmlp_f2(qh, qwd)
+        ops.gmlp_f2_push(qh, qwd, table.data_ptr(), 0, rl)
+        torch.cuda.synchronize()
+        exact = torch.equal(own[:rl], y_ref[:rl]) and all(
+            torch.equal(remote[o][:rl].cpu(), y_ref[o * rl:(o + 1) * rl].cpu()) for o in range(1, world))
+        remote_bytes = T * d * 2 * (world - 1) / world
+        rec = {"mode": "rs_push", "tp": world, "tokens": T, "d": d, "hidden_local": hl, "pushed_rows_exact": exact}
+        for name, flops, local_fn, push_fn in (
+                ("F2", 2.0 * T * d * hl, lambda: ops.gmlp_f2(qh, qwd),
+                 lambda: ops.gmlp_f2_push(qh, qwd, table.data_ptr(), 0, rl)),
+                ("B4", 4.0 * T * d * hl, lambda: ops.gmlp_b4(qdug, qwf),
+                 lambda: ops.gmlp_b4_push(qdug, qwf, table.data_ptr(), 0, rl))):
+            t_local = _time_us(local_fn, args.reps, args.warmup)
+            t_push = _time_us(push_fn, args.reps, args.warmup)
+            rec[name] = {"local_us": t_local, "push_us": t_push, "local_tflops": flops / t_local / 1e6,
+                         "push_remote_gbs": remote_bytes / t_push / 1e3}
+        print(json.dumps(rec), flush=True)
+        del remote
+    if C.device_status() != 0:
+        raise SystemExit("device status word set: a kernel wait timed out")
+
+
 def quant_bench(args, dev):
     """amax (2 B/element read) and quantize (2 B read + 1 B written per element) on the
     tensors one GMLP step quantises; prints algorithmic GB/s per tensor."""
@@ -143,6 +206,8 @@ def main():
     ap.add_argument("--cublas", action="store_true", help="also time cuBLAS fp8 GEMMs of the same shapes")
     ap.add_argument("--group-m", type=int, default=0, help="tile raster group (0 = library default)")
     ap.add_argument("--quant", action="store_true", help="time amax and quantize on the GMLP tensor sizes instead")
+    ap.add_argument("--rs-push", action="store_true",
+                    help="time the TP-2/4/8 F2 and B4 GEMMs storing locally vs pushing rows to a peer GPU")
     args = ap.parse_args()
     C.set_gemm_raster(args.group_m)
     C.set_gemm_variant(args.variant)
@@ -151,6 +216,8 @@ def main():
     torch.cuda.set_device(dev)
     if args.quant:
         return quant_bench(args, dev)
+    if args.rs_push:
+        return rs_push_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)
     names = [n.strip() for n in args.gemms.split(",") if n.strip()]
     for n in names:
