@@ -170,6 +170,15 @@ int ufp8_tp_begin(ufp8_tp_ctx* ctx, void* const** slot_table, uint64_t* epoch);
 int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols, int64_t ld_slot, void* out,
                    int64_t ld_out, ufp8_stream_t stream);
 
+/* MAX all-reduce of n (1..8) non-negative f32 values (per-tensor amax values) over the group
+ * of a connected context: every rank's `out` receives the elementwise maximum of all ranks'
+ * `in` (NaN propagates).  One single-warp kernel: P2P stores with a system-scope release into
+ * each peer's exchange slot, then a bounded wait for all of them (UFP8_STATUS_PEER_TIMEOUT on
+ * expiry, `out` then unchanged).  Replaces the MAX all-reduces of the local amax values that
+ * global per-tensor scales need under tensor parallelism (the all-reduce GSPMD would insert
+ * for a max over a sharded tensor).  Every rank must make the same sequence of calls. */
+int ufp8_tp_allreduce_max(ufp8_tp_ctx* ctx, const float* in, float* out, int n, ufp8_stream_t stream);
+
 /* Synchronises the current device, returns its status word in *status (0 = clean,
  * UFP8_STATUS_* bits otherwise) and clears it when `clear` is non-zero. */
 int ufp8_device_status(int* status, int clear);
@@ -180,8 +189,9 @@ int ufp8_set_gemm_ctas(int ctas);
 /* GEMM kernel variant for this process: UFP8_GEMM_AUTO (default: the CTA-pair kernel),
  * UFP8_GEMM_SINGLE_CTA (128 x 256 tiles, one CTA each), UFP8_GEMM_CTA_PAIR (256 x 256
  * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2; RS_PUSH rows leave through
- * shared memory as bulk async stores) or UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with
- * RS_PUSH rows written by plain 16-byte stores from registers). */
+ * shared memory as bulk async stores and DSWIGLU reads the saved U / G through TMA) or
+ * UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with plain 16-byte loads and stores in every
+ * epilogue). */
 #define UFP8_GEMM_AUTO 0
 #define UFP8_GEMM_SINGLE_CTA 1
 #define UFP8_GEMM_CTA_PAIR 2

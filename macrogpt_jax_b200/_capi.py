@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "ufp8_tp_slot_bytes",
     "ufp8_tp_begin",
     "ufp8_tp_finish",
+    "ufp8_tp_allreduce_max",
 )
 
 
@@ -124,10 +125,11 @@ def load() -> ctypes.CDLL:
     lib.ufp8_tp_slot_bytes.argtypes = [vp, ctypes.POINTER(i64)]
     lib.ufp8_tp_begin.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
     lib.ufp8_tp_finish.argtypes = [vp, ctypes.c_uint64, i64, i64, i64, vp, i64, vp]
+    lib.ufp8_tp_allreduce_max.argtypes = [vp, vp, vp, i32, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
-                 "ufp8_tp_finish"):
+                 "ufp8_tp_finish", "ufp8_tp_allreduce_max"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -217,6 +219,11 @@ class TPReduceScatter:
 
     def finish(self, epoch: int, rows: int, cols: int, ld_slot: int, out_ptr: int, ld_out: int, stream: int) -> None:
         check(load().ufp8_tp_finish(self.ctx, epoch, rows, cols, ld_slot, out_ptr, ld_out, stream))
+        _count(1)
+
+    def allreduce_max(self, in_ptr: int, out_ptr: int, n: int, stream: int) -> None:
+        """Elementwise MAX over the group of n (1..8) non-negative device f32 values."""
+        check(load().ufp8_tp_allreduce_max(self.ctx, in_ptr, out_ptr, n, stream))
         _count(1)
 
     def close(self) -> None:

@@ -15,6 +15,8 @@
 // transposed copy is ever made.  Every mbarrier wait is bounded (see ptx.cuh).
 #include <cuda_bf16.h>
 
+#include <cstring>
+
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -422,12 +424,32 @@ constexpr int kPStgCols = 64;                     // columns per staged row segm
 constexpr int kPStgStride = kPStgCols * 2 + 16;   // 144 B: padded row pitch
 constexpr int kPStgWarpBytes = 32 * kPStgStride;  // 4.5 KiB per epilogue warp
 constexpr int kPStgBytes = kPEpiWarps * kPStgWarpBytes;
-constexpr int pair_smem_bytes(int stages, bool staged) {
-  return stages * kPStageBytes + (staged ? kPStgBytes : 0) + kBarrierBytes + 1024;
+//
+// The DSWIGLU instantiation (kVarUgStaged) likewise gives up two ring stages so that the saved
+// U / G the gating backward reads arrive by TMA instead of by per-thread global loads: each
+// epilogue warp streams 32-row x 32-column bf16 boxes of U and G (64-byte swizzle, so the
+// lanes' 16-byte reads of their own rows are bank-conflict free) into a double buffer two
+// chunks ahead of its TMEM reads, including across tiles, so the loads of the next tile run
+// while this tile's MMAs are still in flight.
+constexpr int kVarDirect = 0;     // every epilogue, plain stores from registers
+constexpr int kVarRsStaged = 1;   // RS_PUSH rows through shared memory, bulk stores
+constexpr int kVarUgStaged = 2;   // DSWIGLU with U / G staged by TMA
+constexpr int kPUgCols = 32;                        // columns per U / G chunk
+constexpr int kPUgBoxBytes = 32 * kPUgCols * 2;     // 2 KiB: 32 rows x 32 bf16
+constexpr int kPUgBufBytes = 2 * kPUgBoxBytes;      // U box + G box
+constexpr int kPUgWarpBytes = 2 * kPUgBufBytes;     // double buffer: 8 KiB per warp
+constexpr int kPUgBytes = kPEpiWarps * kPUgWarpBytes + 256;  // + the warps' mbarriers
+__host__ __device__ constexpr int pair_extra_bytes(int var) {
+  return var == kVarRsStaged ? kPStgBytes : (var == kVarUgStaged ? kPUgBytes : 0);
 }
-constexpr int kPSmemBytes = pair_smem_bytes(kPStages, false);
-constexpr int kPSmemBytesStaged = pair_smem_bytes(kPStagesStaged, true);
+__host__ __device__ constexpr int pair_smem_bytes(int stages, int var) {
+  return stages * kPStageBytes + pair_extra_bytes(var) + kBarrierBytes + 1024;
+}
+constexpr int kPSmemBytes = pair_smem_bytes(kPStages, kVarDirect);
+constexpr int kPSmemBytesStaged = pair_smem_bytes(kPStagesStaged, kVarRsStaged);
+constexpr int kPSmemBytesUg = pair_smem_bytes(kPStagesStaged, kVarUgStaged);
 static_assert(kPSmemBytesStaged <= 232448, "staged CTA-pair kernel exceeds shared memory");
+static_assert(kPSmemBytesUg <= 232448, "U/G-staged CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytes <= 232448, "CTA-pair kernel exceeds shared memory");
 
 // Stores 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]).
@@ -536,14 +558,17 @@ __device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[16], int j) {
   return (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
 }
 
-template <int NSTAGES, bool kStaged>
+template <int NSTAGES, int kVar>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const GemmArgs args) {
+                         const __grid_constant__ CUtensorMap tmUG, const GemmArgs args) {
+  constexpr bool kStaged = kVar == kVarRsStaged;
+  constexpr bool kUgStaged = kVar == kVarUgStaged;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + NSTAGES * kPStageBytes;  // kStaged only
-  uint64_t* full = reinterpret_cast<uint64_t*>(staging + (kStaged ? kPStgBytes : 0));
+  uint8_t* staging = smem + NSTAGES * kPStageBytes;  // staged variants only
+  uint64_t* ugbar_all = reinterpret_cast<uint64_t*>(staging + kPEpiWarps * kPUgWarpBytes);  // kUgStaged only
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + pair_extra_bytes(kVar));
   uint64_t* empty = full + NSTAGES;
   uint64_t* tfull = empty + NSTAGES;
   uint64_t* tempty = tfull + 2;
@@ -566,12 +591,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       mbar_init(&tempty[b], 2 * kPEpiWarps);
     }
     mbar_init(drain, 1);
+    if (kUgStaged)
+      for (int i = 0; i < 2 * kPEpiWarps; ++i) mbar_init(&ugbar_all[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (kUgStaged) tma_prefetch_desc(&tmUG);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -697,6 +725,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint64_t stream = l2_policy_evict_first();  // outputs are not re-read by this kernel
     uint32_t amax = 0;
+    // kUgStaged: this warp's U / G chunk stream.  Chunk j (4 per tile: 32 of this warp's 128
+    // columns each) lands in buffer j & 1 on mbarrier ugbar[j & 1], phase (j >> 1) & 1.
+    uint8_t* ugw = staging + e * kPUgWarpBytes;
+    uint64_t* ugbar = ugbar_all + 2 * e;
+    int ug_issued = 0;  // chunks issued (lane 0)
+    int ug_used = 0;    // chunks consumed
+    auto ug_issue = [&](int j) -> bool {
+      const int t = cluster_id + (j >> 2) * num_clusters;
+      if (t >= num_tiles) return false;
+      int g_, mb_, nb_;
+      map_tile(t, args, g_, mb_, nb_);
+      const int b = j & 1;
+      uint8_t* dst = ugw + b * kPUgBufBytes;
+      const int x = nb_ * kBN + chalf * 128 + (j & 3) * kPUgCols;
+      const int y = mb_ * 2 * kBM + static_cast<int>(rank) * kBM + quad * 32;
+      mbar_arrive_expect_tx(&ugbar[b], kPUgBufBytes);
+      tma_load_3d(dst, &tmUG, &ugbar[b], x, y, 0);
+      tma_load_3d(dst + kPUgBoxBytes, &tmUG, &ugbar[b], x, y, 1);
+      return true;
+    };
+    if (kUgStaged && lane == 0) {
+      if (ug_issue(0)) ug_issued = 1;
+      if (ug_issued == 1 && ug_issue(1)) ug_issued = 2;
+    }
     int local = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
       const int buf = local & 1;
@@ -711,7 +763,66 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const bool row_ok = row < args.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
 
-      if (kStaged) {
+      if (kUgStaged) {
+        // DSWIGLU with U / G from shared memory (TMA-staged two chunks ahead).
+        bool ug_ok = true;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          const int j = local * 4 + c;
+          const int b = j & 1;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + chalf * 128 + c * kPUgCols, r);
+          bool okc = mbar_wait(&ugbar[b], (j >> 1) & 1, abort_flag);
+          okc = __all_sync(0xFFFFFFFFu, okc);
+          tmem_ld_wait();
+          if (!okc) {
+            ug_ok = false;
+            break;
+          }
+          ug_used = j + 1;
+          const int col0 = nb * kBN + chalf * 128 + c * kPUgCols;
+          if (row_ok && col0 < args.N) {
+            const int valid = args.N - col0;
+            const uint8_t* su = ugw + b * kPUgBufBytes + lane * (kPUgCols * 2);
+            const uint8_t* sg = su + kPUgBoxBytes;
+            const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this row's 16-byte granules
+            uint32_t odu[16], odg[16];
+            uint32_t m2 = 0;  // packed 2 x 16-bit max of |dU|, |dG|
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 uq = *reinterpret_cast<const uint4*>(su + ((q ^ sw) << 4));
+              const uint4 gq = *reinterpret_cast<const uint4*>(sg + ((q ^ sw) << 4));
+              const uint32_t cu[4] = {uq.x, uq.y, uq.z, uq.w};
+              const uint32_t cg[4] = {gq.x, gq.y, gq.z, gq.w};
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const int jj = q * 4 + w;  // output word: columns 2jj, 2jj + 1
+                const uint32_t dhw =
+                    pack_bf16x2(__uint_as_float(r[2 * jj]) * alpha, __uint_as_float(r[2 * jj + 1]) * alpha);
+                const float dh0 = lo_f(dhw), dh1 = hi_f(dhw);
+                const float u0 = lo_f(cu[w]), u1 = hi_f(cu[w]);
+                const float g0 = lo_f(cg[w]), g1 = hi_f(cg[w]);
+                const float s0 = sigmoidf_(g0), s1 = sigmoidf_(g1);
+                odu[jj] = pack_bf16x2(dh0 * (g0 * s0), dh1 * (g1 * s1));
+                odg[jj] = pack_bf16x2((dh0 * u0) * (s0 * (1.0f + g0 * (1.0f - s0))),
+                                      (dh1 * u1) * (s1 * (1.0f + g1 * (1.0f - s1))));
+                const uint32_t keep = (2 * jj + 1 < valid) ? 0x7FFF7FFFu : (2 * jj < valid ? 0x00007FFFu : 0u);
+                m2 = __vmaxu2(m2, __vmaxu2(odu[jj] & keep, odg[jj] & keep));
+              }
+            }
+            amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
+            __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
+            store_bf16x32_packed_h(pd, odu, valid, vec, stream);
+            store_bf16x32_packed_h(pd + args.d_bstride, odg, valid, vec, stream);
+          }
+          __syncwarp();  // every lane has read buffer b: it may be refilled
+          if (lane == 0) {
+            fence_proxy_async_smem();
+            if (ug_issued == j + 2 && ug_issue(j + 2)) ug_issued = j + 3;
+          }
+        }
+        if (!ug_ok) break;
+      } else if (kStaged) {
         // RS_PUSH through shared memory: 64-column row segments leave as bulk stores into
         // the row owner's staging slot.
         __nv_bfloat16* rs_row = nullptr;
@@ -887,6 +998,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       amax = __reduce_max_sync(0xFFFFFFFFu, amax);
       if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
     }
+    // kUgStaged after an abort: wait (bounded) for this warp's U / G loads still in flight, so
+    // that no TMA write lands in shared memory after the CTA has exited.
+    if (kUgStaged && lane == 0) {
+      volatile int never = 0;
+      for (int j = ug_used; j < ug_issued; ++j) mbar_wait(&ugbar[j & 1], (j >> 1) & 1, &never);
+    }
     // Peer stores must be complete and visible system-wide before the finish kernel's flag write.
     if (kStaged) bulk_wait_all();
     if (args.mode == UFP8_EPI_RS_PUSH) __threadfence_system();
@@ -959,6 +1076,23 @@ int encode_operand(CUtensorMap* map, const ufp8_operand& op, int64_t rows, int64
   if (r != CUDA_SUCCESS)
     return set_error(UFP8_ERR_INVALID, "cuTensorMapEncodeTiled failed for operand %s (CUresult %d)", name,
                      static_cast<int>(r));
+  return UFP8_OK;
+}
+
+// 3-D map over the saved bf16 U / G of a DSWIGLU GEMM: x = column (N), y = row (M), z = slice
+// (0 = U, 1 = G).  Box = 32 x 32 x 1 elements (64-byte rows) with 64-byte swizzle.
+int encode_ug(CUtensorMap* map, const ufp8_gemm_desc& d) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(UFP8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d.N), static_cast<cuuint64_t>(d.M), 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(d.ldug) * 2, static_cast<cuuint64_t>(d.ug_batch_stride) * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(d.ug), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(UFP8_ERR_INVALID, "cuTensorMapEncodeTiled failed for U/G (CUresult %d)", static_cast<int>(r));
   return UFP8_OK;
 }
 
@@ -1107,28 +1241,42 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (attr_device != dev.device) {
     e = cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStages, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kPSmemBytes);
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStages, kVarDirect>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytes);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesStaged, true>,
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesStaged);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesUg);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
-  // RS_PUSH goes through the staged kernel whenever its rows are 16-byte aligned.  (Local
-  // outputs keep the direct stores and the deeper ring: at these tile sizes their stores
-  // never limit the epilogue, while two more ring stages help the long-K contractions.)
-  const bool staged = pair && variant != UFP8_GEMM_CTA_PAIR_DIRECT && vec && rs;
-  const void* pair_fn = staged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, true>)
-                               : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, false>);
-  const int pair_smem = staged ? kPSmemBytesStaged : kPSmemBytes;
+  // Staged variants of the CTA-pair kernel, whenever the rows they touch are 16-byte aligned:
+  // RS_PUSH rows leave through shared memory as bulk stores; DSWIGLU reads U / G through TMA.
+  // (Plain local outputs keep the direct stores and the deeper ring: at these tile sizes their
+  // stores never limit the epilogue, while two more ring stages help the long-K contractions.)
+  int var = kVarDirect;
+  if (pair && variant != UFP8_GEMM_CTA_PAIR_DIRECT && vec) {
+    if (rs) var = kVarRsStaged;
+    if (d.epilogue == UFP8_EPI_DSWIGLU) var = kVarUgStaged;
+  }
+  CUtensorMap tmUG;
+  std::memset(&tmUG, 0, sizeof(tmUG));
+  if (var == kVarUgStaged) {
+    rc = encode_ug(&tmUG, d);
+    if (rc) return rc;
+  }
+  const void* pair_fn = var == kVarRsStaged   ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>)
+                        : var == kVarUgStaged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>)
+                                              : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, kVarDirect>);
+  const int pair_smem = var == kVarRsStaged ? kPSmemBytesStaged : (var == kVarUgStaged ? kPSmemBytesUg : kPSmemBytes);
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device[2] = {-1, -1}, occ_clusters[2] = {0, 0};
-    const int oi = staged ? 1 : 0;
-    if (occ_device[oi] != dev.device) {
+    static thread_local int occ_device[3] = {-1, -1, -1}, occ_clusters[3] = {0, 0, 0};
+    if (occ_device[var] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
       cfg.blockDim = dim3(kPThreads, 1, 1);
@@ -1137,20 +1285,22 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
       e = cudaOccupancyMaxActiveClusters(&n, pair_fn, &cfg);
       if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
       if (n < 1) return set_error(UFP8_ERR_DEVICE, "no CTA pair of the GEMM kernel fits on this device");
-      occ_clusters[oi] = n;
-      occ_device[oi] = dev.device;
+      occ_clusters[var] = n;
+      occ_device[var] = dev.device;
     }
-    const int max_clusters = occ_clusters[oi];
+    const int max_clusters = occ_clusters[var];
     // Persistent grid: no more clusters than can be resident at once.
     if (ctas_override <= 0 || ctas > 2 * max_clusters) ctas = 2 * max_clusters;
     long long clusters = ctas / 2;
     if (clusters < 1) clusters = 1;
     if (num_tiles < clusters) clusters = num_tiles;
-    if (staged)
-      gemm_fp8_pair_kernel<kPStagesStaged, true>
-          <<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytesStaged, stream>>>(tmA, tmB, a);
+    const int grid = static_cast<int>(2 * clusters);
+    if (var == kVarRsStaged)
+      gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
+    else if (var == kVarUgStaged)
+      gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
     else
-      gemm_fp8_pair_kernel<kPStages, false><<<static_cast<int>(2 * clusters), kPThreads, kPSmemBytes, stream>>>(tmA, tmB, a);
+      gemm_fp8_pair_kernel<kPStages, kVarDirect><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
   } else {
     if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
     gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);

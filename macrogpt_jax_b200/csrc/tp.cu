@@ -24,6 +24,11 @@ namespace ufp8 {
 
 constexpr int kMaxRanks = 8;
 constexpr size_t kFlagBytes = 256;  // flag[src] (u32) per buffer, padded
+// Small-value exchange region after the two staging buffers: [2 buffers][kMaxRanks sources]
+// entries of 64 bytes, {u32 epoch, u32 pad, u32 value bits[kMaxExchange]}.
+constexpr int kMaxExchange = 8;
+constexpr size_t kExEntryBytes = 64;
+constexpr size_t kExBytes = 2 * kMaxRanks * kExEntryBytes;
 
 struct TPContext {
   int device = -1;
@@ -36,7 +41,9 @@ struct TPContext {
   bool peer_opened[kMaxRanks] = {};
   void** d_slot_ptrs = nullptr;  // device array [2][world]: data region of buffer b on each rank
   uint64_t epoch = 0;
+  uint64_t ex_epoch = 0;          // small-value exchanges issued
   int timeout_ms = 5000;
+  char* ex_region(int p) const { return peer_base[p] + 2 * buffer_bytes; }
 };
 
 namespace {
@@ -133,6 +140,69 @@ __global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
   }
 }
 
+struct ExchangeArgs {
+  char* entry_peer[kMaxRanks];  // &peer p's exchange entry [b][rank]
+  const char* entry_local;      // &own exchange entry [b][0]
+  const uint32_t* in;           // n f32 bit patterns (non-negative values or NaN)
+  uint32_t* out;
+  int n, world;
+  uint32_t epoch;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+// MAX all-reduce of n <= 8 non-negative f32 values (amax values) over the group: one warp.
+// Lane p stores the values into peer p's entry [b][rank] and then the epoch with a system-scope
+// release; lane s waits (bounded) for entry [b][s] of this rank to carry the epoch and reads
+// it.  Unsigned max of the bit patterns = float max for non-negative values, and propagates
+// NaN (0x7FC00000 is above every finite value and inf), as the amax kernel does.
+__global__ void __launch_bounds__(32) tp_exchange_max_kernel(const ExchangeArgs a) {
+  const int lane = threadIdx.x;
+  uint32_t v[kMaxExchange];
+#pragma unroll
+  for (int i = 0; i < kMaxExchange; ++i) v[i] = i < a.n ? a.in[i] : 0u;
+  if (lane < a.world) {
+    uint32_t* e = reinterpret_cast<uint32_t*>(a.entry_peer[lane]);
+#pragma unroll
+    for (int i = 0; i < kMaxExchange; ++i)
+      if (i < a.n) asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(e + 2 + i), "r"(v[i]) : "memory");
+    st_release_sys(e, a.epoch);
+  }
+  bool ok = true;
+  uint32_t m[kMaxExchange];
+#pragma unroll
+  for (int i = 0; i < kMaxExchange; ++i) m[i] = 0u;
+  if (lane < a.world) {
+    const uint32_t* e = reinterpret_cast<const uint32_t*>(a.entry_local + lane * kExEntryBytes);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(e) != a.epoch) {
+      if (globaltimer_ns() - t0 > a.timeout_ns) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok) {
+#pragma unroll
+      for (int i = 0; i < kMaxExchange; ++i)
+        if (i < a.n) {
+          uint32_t x;
+          asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(x) : "l"(e + 2 + i) : "memory");
+          m[i] = x;
+        }
+    }
+  }
+  ok = __all_sync(0xFFFFFFFFu, ok);
+  if (!ok) {
+    if (lane == 0) atomicOr(a.status, UFP8_STATUS_PEER_TIMEOUT);
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxExchange; ++i) {
+    const uint32_t r = __reduce_max_sync(0xFFFFFFFFu, m[i]);
+    if (lane == 0 && i < a.n) a.out[i] = r;
+  }
+}
+
 }  // namespace
 
 }  // namespace ufp8
@@ -155,8 +225,8 @@ int ufp8_tp_create(int rank, int world, int64_t slot_bytes, ufp8_tp_ctx** out, u
   c->world = world;
   c->slot_bytes = static_cast<size_t>(slot_bytes);
   c->buffer_bytes = kFlagBytes + c->slot_bytes * world;
-  cudaError_t e = cudaMalloc(&c->base, 2 * c->buffer_bytes);
-  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->buffer_bytes);
+  cudaError_t e = cudaMalloc(&c->base, 2 * c->buffer_bytes + kExBytes);
+  if (e == cudaSuccess) e = cudaMemset(c->base, 0, 2 * c->buffer_bytes + kExBytes);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_slot_ptrs, 2 * kMaxRanks * sizeof(void*));
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c->base);
@@ -281,6 +351,33 @@ int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols,
   tp_finish_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? UFP8_OK : cuda_error(e, "tp finish launch");
+}
+
+int ufp8_tp_allreduce_max(ufp8_tp_ctx* ctx, const float* in, float* out, int n, ufp8_stream_t stream) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !in || !out) return set_error(UFP8_ERR_INVALID, "ufp8_tp_allreduce_max: null pointer");
+  if (n < 1 || n > kMaxExchange)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_allreduce_max: n = %d (1..%d)", n, kMaxExchange);
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_allreduce_max: rank %d is not connected", p);
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  c->ex_epoch += 1;
+  const int b = static_cast<int>(c->ex_epoch & 1);
+  ExchangeArgs a{};
+  for (int p = 0; p < c->world; ++p)
+    a.entry_peer[p] = c->ex_region(p) + (b * kMaxRanks + c->rank) * kExEntryBytes;
+  a.entry_local = c->ex_region(c->rank) + b * kMaxRanks * kExEntryBytes;
+  a.in = reinterpret_cast<const uint32_t*>(in);
+  a.out = reinterpret_cast<uint32_t*>(out);
+  a.n = n;
+  a.world = c->world;
+  a.epoch = static_cast<uint32_t>(c->ex_epoch);
+  a.timeout_ns = static_cast<uint64_t>(c->timeout_ms) * 1000000ull;
+  a.status = dev->status_word;
+  tp_exchange_max_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "tp exchange launch");
 }
 
 int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* out) {

@@ -39,8 +39,9 @@ class TPContext:
     With the CUDA backend and `fused_reduce_scatter` the reduce-scatters run over NVLink peer
     memory: the down-projection / dx GEMM epilogues store each partial row straight into its
     owner's staging slot (UFP8_EPI_RS_PUSH) and ufp8_tp_finish sums the slots on the owner,
-    so the transfer overlaps the GEMM tile by tile.  Otherwise NCCL's reduce-scatter runs
-    after the GEMM."""
+    so the transfer overlaps the GEMM tile by tile; the MAX all-reduces of the amax values
+    are then single-warp P2P exchanges (ufp8_tp_allreduce_max) instead of NCCL calls.
+    Otherwise NCCL's reduce-scatter runs after the GEMM and NCCL all-reduces the amax values."""
 
     def __init__(self, group=None, backend=None, fused_reduce_scatter: bool = True):
         self.group = group
@@ -49,6 +50,7 @@ class TPContext:
         self.be = backend if backend is not None else cuda_ops
         self.fused_rs = fused_reduce_scatter and backend is None and self.world > 1
         self._rs = None
+        self._ex = None  # small-value (amax) exchange context
 
     def _rs_ctx(self, slot_bytes: int) -> C.TPReduceScatter:
         """Collective: (re)creates the peer-mapped staging when a larger slot is needed."""
@@ -78,22 +80,36 @@ class TPContext:
         return out, mid
 
     def close(self) -> None:
-        if self._rs is not None:
-            self._rs.close()
-            self._rs = None
+        for ctx in (self._rs, self._ex):
+            if ctx is not None:
+                ctx.close()
+        self._rs = self._ex = None
 
-    def global_amax(self, t: torch.Tensor) -> torch.Tensor:
-        a = self.be.amax(t)
+    def allreduce_max_(self, a: torch.Tensor) -> torch.Tensor:
+        """In-place MAX all-reduce of a few amax values (f32, non-negative): over NVLink peer
+        memory with the CUDA backend and fused collectives, else a NCCL/gloo all-reduce."""
+        if self.fused_rs and a.numel() <= 8:
+            if self._ex is None:  # collective: every rank creates it at the same call
+                ex = C.TPReduceScatter(self.rank, self.world, 256)
+                handles = [None] * self.world
+                dist.all_gather_object(handles, ex.handle, group=self.group)
+                ex.connect(handles)
+                self._ex = ex
+            a = a.contiguous()
+            self._ex.allreduce_max(a.data_ptr(), a.data_ptr(), a.numel(), torch.cuda.current_stream().cuda_stream)
+            return a
         dist.all_reduce(a, op=dist.ReduceOp.MAX, group=self.group)
         return a
+
+    def global_amax(self, t: torch.Tensor) -> torch.Tensor:
+        return self.allreduce_max_(self.be.amax(t))
 
     def quant_global(self, t: torch.Tensor, fmt: int):
         return self.be.quantize(t, fmt, self.global_amax(t))
 
     def quant_global_many(self, tensors_fmts):
         """Quantises several tensors with whole-tensor scales using ONE MAX all-reduce."""
-        amaxes = torch.cat([self.be.amax(t) for t, _ in tensors_fmts])
-        dist.all_reduce(amaxes, op=dist.ReduceOp.MAX, group=self.group)
+        amaxes = self.allreduce_max_(torch.cat([self.be.amax(t) for t, _ in tensors_fmts]))
         return [self.be.quantize(t, f, amaxes[i:i + 1]) for i, (t, f) in enumerate(tensors_fmts)]
 
     def all_gather_tokens(self, q):
@@ -119,7 +135,7 @@ class _TPGMLPFn(torch.autograd.Function):
         qx_local, qwf, qwd = tp.quant_global_many([(x, C.E4M3), (wf, C.E4M3), (wd, C.E4M3)])
         qx = tp.all_gather_tokens(qx_local)
         ug, hid, amax_h = be.gmlp_f1(qx, qwf)
-        dist.all_reduce(amax_h, op=dist.ReduceOp.MAX, group=tp.group)
+        amax_h = tp.allreduce_max_(amax_h)
         qh = be.quantize(hid, C.E4M3, amax_h)
         if tp.fused_rs:
             T, d = qh.q.shape[0], qwd.q.shape[1]
@@ -139,7 +155,7 @@ class _TPGMLPFn(torch.autograd.Function):
         ctx.saved = None
         qdy = tp.all_gather_tokens(tp.quant_global(dy.to(torch.bfloat16).contiguous(), C.E5M2))
         dug, amax_dug = be.gmlp_b2(qdy, qwd, ug)
-        dist.all_reduce(amax_dug, op=dist.ReduceOp.MAX, group=tp.group)
+        amax_dug = tp.allreduce_max_(amax_dug)
         dwd = be.gmlp_b1(qh, qdy)
         qdug = be.quantize(dug, C.E5M2, amax_dug)
         if tp.fused_rs:

@@ -72,3 +72,46 @@ def test_unconnected_context_is_refused(cuda):
     with pytest.raises(C.UFP8Error, match="not connected"):
         a.begin()
     a.close()
+
+
+def test_allreduce_max_world1_and_nan(cuda):
+    """The P2P MAX exchange of a one-rank group returns its input, NaN included, bit for bit."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    ex = C.TPReduceScatter(0, 1, 256)
+    ex.connect([ex.handle])
+    try:
+        stream = torch.cuda.current_stream().cuda_stream
+        for vals in ([3.5], [0.0, 448.0, 1e-30], [1.0, float("nan"), float("inf"), 2.0, 0.5, 7.0, 8.0, 9.0]):
+            a = torch.tensor(vals, dtype=torch.float32, device=cuda)
+            out = torch.full_like(a, -1.0)
+            ex.allreduce_max(a.data_ptr(), out.data_ptr(), a.numel(), stream)
+            torch.cuda.synchronize()
+            assert torch.equal(out.view(torch.int32), a.view(torch.int32))
+        with pytest.raises(C.UFP8Error, match="n = 9"):
+            ex.allreduce_max(a.data_ptr(), out.data_ptr(), 9, stream)
+        assert C.device_status() == 0
+    finally:
+        ex.close()
+
+
+def test_allreduce_max_missing_peer_times_out(cuda):
+    """Rank 0 of a two-rank group whose rank 1 never calls: the exchange gives up after its
+    200 ms limit, sets the peer-timeout bit, leaves `out` unchanged, and the GPU stays usable."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    a = C.TPReduceScatter(0, 2, 256)
+    b = C.TPReduceScatter(1, 2, 256)
+    a.connect_local([a, b])
+    b.connect_local([a, b])
+    a.set_timeout_ms(200)
+    try:
+        x = torch.tensor([1.0, 2.0], device=cuda)
+        out = torch.full_like(x, -1.0)
+        a.allreduce_max(x.data_ptr(), out.data_ptr(), 2, torch.cuda.current_stream().cuda_stream)
+        assert C.device_status(clear=True) & C.STATUS_PEER_TIMEOUT
+        assert torch.equal(out.cpu(), torch.tensor([-1.0, -1.0]))
+        assert C.device_status() == 0
+    finally:
+        a.close()
+        b.close()
