@@ -92,6 +92,19 @@ int ufp8_quantize(const void* x_bf16, int64_t n, int fmt, const float* amax, voi
 int ufp8_amax_quant(const void* x_bf16, int64_t n, int fmt, void* q, float* amax, float* inv_scale,
                     ufp8_stream_t stream);
 
+/* ufp8_amax_quant without the caller's amax buffer and without any allocation: the amax
+ * scratch (one partial max per 65 536 elements, plus the reduced amax) lives in static
+ * device arrays of the library (16 KiB per device), so n is limited to 268 435 456 elements
+ * (larger n returns UFP8_ERR_UNSUPPORTED and launches nothing).  q and *inv_scale are
+ * bit-identical to ufp8_amax_quant's.  No scratch word has to start at zero.  For callers that
+ * may not allocate device memory nor hold a spare device word, e.g. an XLA FFI handler whose
+ * buffers all come from XLA.  This entry point has no counterpart in the reference (XLA's cast
+ * needs no scratch).  Overlapping calls on one device race on the shared scratch: calls must be
+ * ordered (one stream, or synchronised).  The first call on a device looks up the scratch
+ * address (cudaGetSymbolAddress, with that device current); make it outside any stream capture. */
+int ufp8_amax_quant_noalloc(const void* x_bf16, int64_t n, int fmt, void* q, float* inv_scale,
+                            ufp8_stream_t stream);
+
 /* q = fp8(x) with a unit scale: the plain element-type conversion of custom_astype
  * (ueaj/utils/gradutils.py:34,41,49 `lax.convert_element_type`) to float8_e4m3fn /
  * float8_e5m2, round to nearest even with the ml_dtypes overflow rules. */

@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "ufp8_tp_begin",
     "ufp8_tp_finish",
     "ufp8_tp_allreduce_max",
+    "ufp8_amax_quant_noalloc",
 )
 
 
@@ -112,6 +113,7 @@ def load() -> ctypes.CDLL:
     lib.ufp8_quantize.argtypes = [vp, i64, i32, vp, vp, vp, vp]
     lib.ufp8_amax_quant.argtypes = [vp, i64, i32, vp, vp, vp, vp]
     lib.ufp8_cast.argtypes = [vp, i64, i32, vp, vp]
+    lib.ufp8_amax_quant_noalloc.argtypes = [vp, i64, i32, vp, vp, vp]
     lib.ufp8_gemm.argtypes = [ctypes.POINTER(GemmDesc), vp]
     lib.ufp8_device_status.argtypes = [ctypes.POINTER(ctypes.c_int), i32]
     lib.ufp8_set_gemm_ctas.argtypes = [i32]
@@ -129,7 +131,7 @@ def load() -> ctypes.CDLL:
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
-                 "ufp8_tp_finish", "ufp8_tp_allreduce_max"):
+                 "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -158,6 +160,12 @@ def quantize(x_ptr: int, n: int, fmt: int, amax_ptr: int, q_ptr: int, inv_ptr: i
 def amax_quant(x_ptr: int, n: int, fmt: int, q_ptr: int, amax_ptr: int, inv_ptr: int, stream: int) -> None:
     check(load().ufp8_amax_quant(x_ptr, n, fmt, q_ptr, amax_ptr, inv_ptr, stream))
     _count(2 if n > 0 else 1)
+
+
+def amax_quant_noalloc(x_ptr: int, n: int, fmt: int, q_ptr: int, inv_ptr: int, stream: int) -> None:
+    """ufp8_amax_quant with the amax scratch in the library's static device arrays."""
+    check(load().ufp8_amax_quant_noalloc(x_ptr, n, fmt, q_ptr, inv_ptr, stream))
+    _count(3 if n > 0 else 2)
 
 
 def cast(x_ptr: int, n: int, fmt: int, q_ptr: int, stream: int) -> None:
