@@ -199,6 +199,7 @@ def run_ours(args, cfg, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    _capi.set_gemm_variant(args.gemm_variant)
     if cfg["kind"] == "attn":
         return run_attn(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
@@ -437,6 +438,9 @@ def main():
     ap.add_argument("--gemm-traffic", type=float, default=None,
                     help="DRAM bytes per GEMM launch to report as roofline.traffic (default: the "
                          "captured figure for gmlp_d4096 on one GPU, else null)")
+    ap.add_argument("--gemm-variant", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="GEMM kernel variant (ufp8_set_gemm_variant): 0 auto, 1 one CTA per tile, "
+                         "2 CTA pair, 3 CTA pair with direct epilogue loads/stores")
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p",
                     help="tensor-parallel reduce-scatter: fused into the GEMM epilogue over NVLink, or NCCL")
     args = ap.parse_args()

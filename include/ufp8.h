@@ -41,7 +41,7 @@ extern "C" {
 
 typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 
-#define UFP8_ABI_VERSION 2
+#define UFP8_ABI_VERSION 3
 
 /* return codes */
 #define UFP8_OK 0
@@ -156,6 +156,15 @@ typedef struct ufp8_gemm_desc {
   int32_t rs_rank;
   int32_t rs_reserved;
   int64_t rs_rows_per_rank;
+  /* All-gathered A (CTA-pair kernel only): rows [s*R, (s+1)*R) of A (R = ag_rows_per_rank, a
+   * multiple of 256) arrive from rank s through ufp8_tp_ag_push; before the first load of a
+   * block s != ag_rank the producer waits (bounded; UFP8_STATUS_PEER_TIMEOUT) until
+   * ag_flags[s] == ag_epoch (ag_flags from ufp8_tp_local).  The tile order starts at this
+   * rank's own block.  ag_flags == NULL: no waits.  Not combinable with RS_PUSH. */
+  const uint32_t* ag_flags;
+  uint32_t ag_epoch;
+  int32_t ag_rank;
+  int64_t ag_rows_per_rank;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);
@@ -182,6 +191,20 @@ int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* slot_bytes);
 int ufp8_tp_begin(ufp8_tp_ctx* ctx, void* const** slot_table, uint64_t* epoch);
 int ufp8_tp_finish(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t rows, int64_t cols, int64_t ld_slot, void* out,
                    int64_t ld_out, ufp8_stream_t stream);
+
+/* This rank's buffer of `epoch`: *data = its slot region (slot s at *data + s * slot_bytes),
+ * *flags = its k arrival flags.  Used by the all-gather below. */
+int ufp8_tp_local(ufp8_tp_ctx* ctx, uint64_t epoch, void** data, uint32_t** flags);
+
+/* All-gather over the same staging layout (replaces the all-gather GSPMD would insert before
+ * the column-split gate/up projection and the down projection's input gradient, implied by
+ * ueaj/model/layer.py:57 token sharding and ueaj/model/mlp.py:85 'tensor' on hidden): the
+ * caller has written this rank's block (`bytes` <= slot_bytes) into its own slot [rank] of the
+ * buffer of `epoch`; this call copies it into slot [rank] of every peer, in the order rank-1,
+ * rank-2, ... (mod k), each copy followed by a stream write of `epoch` into that peer's
+ * flag[rank] (with a memory fence before the write).  Copy engines move the data, so `stream`
+ * can run beside a GEMM that consumes the blocks as they arrive (ufp8_gemm_desc.ag_*). */
+int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, ufp8_stream_t stream);
 
 /* MAX all-reduce of n (1..8) non-negative f32 values (per-tensor amax values) over the group
  * of a connected context: every rank's `out` receives the elementwise maximum of all ranks'

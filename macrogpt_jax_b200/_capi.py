@@ -41,6 +41,8 @@ EXPORTED_SYMBOLS = (
     "ufp8_tp_begin",
     "ufp8_tp_finish",
     "ufp8_tp_allreduce_max",
+    "ufp8_tp_local",
+    "ufp8_tp_ag_push",
     "ufp8_amax_quant_noalloc",
 )
 
@@ -82,6 +84,10 @@ class GemmDesc(ctypes.Structure):
         ("rs_rank", ctypes.c_int32),
         ("rs_reserved", ctypes.c_int32),
         ("rs_rows_per_rank", ctypes.c_int64),
+        ("ag_flags", ctypes.c_void_p),
+        ("ag_epoch", ctypes.c_uint32),
+        ("ag_rank", ctypes.c_int32),
+        ("ag_rows_per_rank", ctypes.c_int64),
     ]
 
 
@@ -128,10 +134,13 @@ def load() -> ctypes.CDLL:
     lib.ufp8_tp_begin.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
     lib.ufp8_tp_finish.argtypes = [vp, ctypes.c_uint64, i64, i64, i64, vp, i64, vp]
     lib.ufp8_tp_allreduce_max.argtypes = [vp, vp, vp, i32, vp]
+    lib.ufp8_tp_local.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
+    lib.ufp8_tp_ag_push.argtypes = [vp, ctypes.c_uint64, i64, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
-                 "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc"):
+                 "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
+                 "ufp8_tp_local", "ufp8_tp_ag_push"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -197,8 +206,9 @@ def set_gemm_raster(group_m: int) -> None:
 
 
 class TPReduceScatter:
-    """One tensor-parallel reduce-scatter context (include/ufp8.h ufp8_tp_*): peer-mapped
-    staging slots of `slot_bytes` per source rank, double-buffered."""
+    """One tensor-parallel context (include/ufp8.h ufp8_tp_*): peer-mapped staging slots of
+    `slot_bytes` per source rank, double-buffered; serves reduce-scatters (RS_PUSH + finish),
+    all-gathers (ag_push) and small MAX all-reduces."""
 
     def __init__(self, rank: int, world: int, slot_bytes: int):
         self.ctx = ctypes.c_void_p()
@@ -206,6 +216,7 @@ class TPReduceScatter:
         check(load().ufp8_tp_create(rank, world, slot_bytes, ctypes.byref(self.ctx), handle))
         self.handle = handle.raw
         self.rank, self.world, self.slot_bytes = rank, world, slot_bytes
+        self.epoch = 0  # last epoch begun
 
     def connect(self, handles) -> None:
         check(load().ufp8_tp_connect(self.ctx, b"".join(handles)))
@@ -223,11 +234,23 @@ class TPReduceScatter:
         table = ctypes.c_void_p()
         epoch = ctypes.c_uint64()
         check(load().ufp8_tp_begin(self.ctx, ctypes.byref(table), ctypes.byref(epoch)))
+        self.epoch = epoch.value
         return table.value, epoch.value
 
     def finish(self, epoch: int, rows: int, cols: int, ld_slot: int, out_ptr: int, ld_out: int, stream: int) -> None:
         check(load().ufp8_tp_finish(self.ctx, epoch, rows, cols, ld_slot, out_ptr, ld_out, stream))
         _count(1)
+
+    def local(self, epoch: int):
+        """(data pointer, flags pointer) of this rank's buffer of `epoch`."""
+        data, flags = ctypes.c_void_p(), ctypes.c_void_p()
+        check(load().ufp8_tp_local(self.ctx, epoch, ctypes.byref(data), ctypes.byref(flags)))
+        return data.value, flags.value
+
+    def ag_push(self, epoch: int, nbytes: int, stream: int) -> None:
+        """Copies this rank's slot of `epoch`'s buffer into every peer's (copy engines), each
+        copy followed by the arrival flag."""
+        check(load().ufp8_tp_ag_push(self.ctx, epoch, nbytes, stream))
 
     def allreduce_max(self, in_ptr: int, out_ptr: int, n: int, stream: int) -> None:
         """Elementwise MAX over the group of n (1..8) non-negative device f32 values."""

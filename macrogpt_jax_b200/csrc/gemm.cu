@@ -15,6 +15,7 @@
 // transposed copy is ever made.  Every mbarrier wait is bounded (see ptx.cuh).
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "internal.h"
@@ -58,7 +59,36 @@ struct GemmArgs {
   void* const* rs_slots;  // RS_PUSH: owners' staging slots
   int rs_rank;
   long long rs_rows;
+  const uint32_t* ag_flags;  // all-gathered A: arrival flags per source rank (null = none)
+  uint32_t ag_epoch;
+  int ag_rank;
+  long long ag_rows;
 };
+
+// Waits until the all-gather block of rank s has arrived (flag == epoch), bounded like the
+// pipeline waits; on expiry raises abort_flag and the peer-timeout status bit.  After the
+// acquire, a proxy fence orders the TMA (async-proxy) reads of the block after it.
+__device__ __forceinline__ bool ag_wait(const GemmArgs& a, int s, volatile int* abort_flag) {
+  const uint32_t* f = a.ag_flags + s;
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  if (v != a.ag_epoch) {
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+      if (v == a.ag_epoch) break;
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        *abort_flag = 1;
+        atomicOr(a.status, UFP8_STATUS_PEER_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
 
 __device__ __forceinline__ void map_tile(int tile, const GemmArgs& a, int& g, int& mb, int& nb) {
   const int tpb = a.tiles_m * a.tiles_n;
@@ -623,10 +653,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t armed = 0, armed_parity = 0;
+      uint32_t arrived = 0;  // all-gather blocks seen complete (bit per source rank)
       for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters) {
         int g, mb, nb;
         map_tile(tile, args, g, mb, nb);
         const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        if (args.ag_flags != nullptr && row0 < args.M) {
+          const int src = static_cast<int>(row0 / args.ag_rows);
+          if (src != args.ag_rank && !((arrived >> src) & 1u)) {
+            if (!ag_wait(args, src, abort_flag)) break;
+            arrived |= 1u << src;
+          }
+        }
         for (int ks = 0; ks < total_k; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
           const int kb = ks / args.ksteps;
@@ -1139,6 +1177,13 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
              d.batch != 1 || d.M % d.rs_rows_per_rank != 0 || d.rs_rank >= d.M / d.rs_rows_per_rank))
     return set_error(UFP8_ERR_INVALID, "RS_PUSH needs rs_slots, bf16 output, batch 1, and M a multiple of "
                                        "rs_rows_per_rank with rs_rank < M / rs_rows_per_rank");
+  const bool ag = d.ag_flags != nullptr;
+  if (ag && (rs || variant == UFP8_GEMM_SINGLE_CTA || d.batch != 1 || d.k_batches != 1 || d.ag_rows_per_rank <= 0 ||
+             d.ag_rows_per_rank % (2 * kBM) != 0 || d.M % d.ag_rows_per_rank != 0 || d.ag_rank < 0 ||
+             d.ag_rank >= d.M / d.ag_rows_per_rank || d.M / d.ag_rows_per_rank > 32))
+    return set_error(UFP8_ERR_INVALID, "all-gathered A needs the CTA-pair kernel, no RS_PUSH, batch 1, k_batches 1, "
+                                       "ag_rows_per_rank a multiple of 256 dividing M into at most 32 blocks, and "
+                                       "ag_rank < M / ag_rows_per_rank");
   if (rs && variant == UFP8_GEMM_SINGLE_CTA)
     return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH runs on the CTA-pair kernel only");
   if (d.d_dtype != UFP8_OUT_BF16 && d.d_dtype != UFP8_OUT_F32)
@@ -1186,6 +1231,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.rs_slots = d.rs_slots;
   a.rs_rank = d.rs_rank;
   a.rs_rows = d.rs_rows_per_rank;
+  a.ag_flags = d.ag_flags;
+  a.ag_epoch = d.ag_epoch;
+  a.ag_rank = d.ag_rank;
+  a.ag_rows = d.ag_rows_per_rank;
 
   if (d.K == 0) {
     if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");
@@ -1217,6 +1266,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   // would push into the same owner at the same time and share its inbound links.  Rank r
   // starts at its own rows instead; at any moment the ranks then write to different owners.
   a.m_shift = rs ? static_cast<int>((static_cast<int64_t>(d.rs_rank) * d.rs_rows_per_rank / bm) % a.tiles_m) : 0;
+  if (ag) {
+    // All-gathered A: start at this rank's own rows (no wait), then the blocks in the order
+    // ufp8_tp_ag_push delivers them (rank + 1, rank + 2, ...), one block per raster group.
+    a.m_shift = static_cast<int>((static_cast<int64_t>(d.ag_rank) * d.ag_rows_per_rank / bm) % a.tiles_m);
+    a.group_m = static_cast<int>(std::min<int64_t>(a.group_m, d.ag_rows_per_rank / bm));
+  }
   a.idesc = (1u << 4)                                       // f32 accumulator
             | (static_cast<uint32_t>(d.a.fmt) << 7)         // A format
             | (static_cast<uint32_t>(d.b.fmt) << 10)        // B format

@@ -5,13 +5,17 @@
 // k contiguous blocks of R = T / k):
 //   1. every rank's GEMM epilogue (UFP8_EPI_RS_PUSH) stores row m of its partial into the
 //      owner o = m / R, in o's staging buffer, slot = its own rank:  slot[src][m - o*R][c];
-//   2. ufp8_tp_finish on every rank: each CTA first publishes "my partials for epoch e are
-//      written" by storing e into every peer's flag[src = me] (after a system-scope fence),
-//      then waits until its own flag[src] == e for all src (bounded by a timeout; on expiry
-//      it sets UFP8_STATUS_PEER_TIMEOUT in the status word and stops), then sums the k slots
-//      in fp32 in rank order and writes the bf16 result.
+//   2. ufp8_tp_finish on every rank: CTA 0 first publishes "my partials for epoch e are
+//      written" by storing e into every peer's flag[src = me] (after a system-scope fence);
+//      every CTA then waits until its own flag[src] == e for all src (bounded by a timeout; on
+//      expiry it sets UFP8_STATUS_PEER_TIMEOUT in the status word and stops), then sums the k
+//      slots in fp32 in rank order and writes the bf16 result.
 // Two staging buffers alternate by epoch, so a fast rank that moves on to the next
 // reduce-scatter writes into the other buffer while slower owners are still summing.
+//
+// The all-gather (ufp8_tp_ag_push) uses the same layout the other way round: slot [s] of
+// every rank's buffer receives rank s's block, by copy engine, and flag[s] = epoch follows
+// each copy; the consuming GEMM waits per row block (ufp8_gemm_desc.ag_*).
 #include <cuda_bf16.h>
 
 #include <cstring>
@@ -51,6 +55,12 @@ namespace {
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -76,12 +86,17 @@ struct FinishArgs {
 __global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
   __shared__ int ok_shared;
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank, a.epoch);
+    // One signal per rank (CTA 0); every CTA then polls the k local flags with relaxed
+    // system-scope loads and takes a single acquire fence once all of them carry the epoch.
+    // (All CTAs are resident: the grid is capped at 4 CTAs of 256 threads per SM.)
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags_peer[p] + a.rank, a.epoch);
+    }
     int ok = 1;
     const uint64_t t0 = globaltimer_ns();
     for (int src = 0; src < a.world && ok; ++src) {
-      while (ld_acquire_sys(a.flags_local + src) != a.epoch) {
+      while (ld_relaxed_sys(a.flags_local + src) != a.epoch) {
         if (globaltimer_ns() - t0 > a.timeout_ns) {
           ok = 0;
           atomicOr(a.status, UFP8_STATUS_PEER_TIMEOUT);
@@ -89,6 +104,7 @@ __global__ void __launch_bounds__(256) tp_finish_kernel(const FinishArgs a) {
         }
       }
     }
+    fence_acq_rel_sys();
     ok_shared = ok;
   }
   __syncthreads();
@@ -378,6 +394,52 @@ int ufp8_tp_allreduce_max(ufp8_tp_ctx* ctx, const float* in, float* out, int n, 
   tp_exchange_max_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? UFP8_OK : cuda_error(e, "tp exchange launch");
+}
+
+int ufp8_tp_local(ufp8_tp_ctx* ctx, uint64_t epoch, void** data, uint32_t** flags) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || !data || !flags) return set_error(UFP8_ERR_INVALID, "ufp8_tp_local: null pointer");
+  if (epoch == 0 || epoch > c->epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_local: epoch not begun");
+  char* buf = c->base + (epoch & 1) * c->buffer_bytes;
+  *flags = reinterpret_cast<uint32_t*>(buf);
+  *data = buf + kFlagBytes;
+  return UFP8_OK;
+}
+
+int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, ufp8_stream_t stream) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: null context");
+  if (epoch == 0 || epoch > c->epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: epoch not begun");
+  if (bytes < 0 || static_cast<size_t>(bytes) > c->slot_bytes)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: %lld bytes exceed the slot", static_cast<long long>(bytes));
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: rank %d is not connected", p);
+  using WriteValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+  static WriteValueFn write_value = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<WriteValueFn>(nullptr);
+    return reinterpret_cast<WriteValueFn>(fn);
+  }();
+  if (!write_value) return set_error(UFP8_ERR_CUDA, "cuStreamWriteValue32 is unavailable from the driver");
+  const size_t off = (epoch & 1) * c->buffer_bytes;
+  const char* src = c->base + off + kFlagBytes + c->rank * c->slot_bytes;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = 1; i < c->world; ++i) {
+    const int p = (c->rank - i + c->world) % c->world;
+    char* dst = c->peer_base[p] + off + kFlagBytes + c->rank * c->slot_bytes;
+    if (bytes > 0) {
+      cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice, s);
+      if (e != cudaSuccess) return cuda_error(e, "ufp8_tp_ag_push: peer copy");
+    }
+    const CUdeviceptr flag = reinterpret_cast<CUdeviceptr>(c->peer_base[p] + off) + c->rank * sizeof(uint32_t);
+    CUresult r = write_value(reinterpret_cast<CUstream>(s), flag, static_cast<cuuint32_t>(epoch),
+                             CU_STREAM_WRITE_VALUE_DEFAULT);
+    if (r != CUDA_SUCCESS) return set_error(UFP8_ERR_CUDA, "ufp8_tp_ag_push: cuStreamWriteValue32 (CUresult %d)", r);
+  }
+  return UFP8_OK;
 }
 
 int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* out) {

@@ -86,10 +86,17 @@ def amax(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def quantize(x: torch.Tensor, fmt: int, amax_t: torch.Tensor | None = None) -> Fp8Tensor:
-    """Per-tensor current scaling: amax (unless given) -> s = FMAX/amax -> fp8(x*s)."""
+def quantize(x: torch.Tensor, fmt: int, amax_t: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> Fp8Tensor:
+    """Per-tensor current scaling: amax (unless given) -> s = FMAX/amax -> fp8(x*s).
+    `out` (optional): a contiguous fp8 tensor of x's element count to write q into."""
     x = _check_bf16_cuda(x, "quantize")
-    q = torch.empty(x.shape, dtype=FP8_DTYPE[fmt], device=x.device)
+    if out is None:
+        q = torch.empty(x.shape, dtype=FP8_DTYPE[fmt], device=x.device)
+    else:
+        if out.dtype != FP8_DTYPE[fmt] or out.numel() != x.numel() or not out.is_contiguous():
+            raise ValueError("quantize: `out` must be a contiguous fp8 tensor of the input's size and format")
+        q = out
     inv = torch.empty(1, dtype=torch.float32, device=x.device)
     n = x.numel()
     if amax_t is None:
@@ -111,7 +118,7 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
          d_batch_stride: int = 0, batch: int = 1, k_batches: int = 1, epilogue: int = C.EPI_STORE,
          h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
          ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None, rs_slots: int | None = None,
-         rs_rank: int = 0, rs_rows_per_rank: int = 0) -> None:
+         rs_rank: int = 0, rs_rows_per_rank: int = 0, ag: tuple | None = None) -> None:
     desc = C.GemmDesc()
     desc.M, desc.N, desc.K = M, N, K
     desc.batch, desc.k_batches = batch, k_batches
@@ -127,6 +134,8 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
     desc.amax_out = amax_out.data_ptr() if amax_out is not None else None
     if rs_slots is not None:
         desc.rs_slots, desc.rs_rank, desc.rs_rows_per_rank = rs_slots, rs_rank, rs_rows_per_rank
+    if ag is not None:  # (flags pointer, epoch, rank, rows per rank): A rows arrive by all-gather
+        desc.ag_flags, desc.ag_epoch, desc.ag_rank, desc.ag_rows_per_rank = ag
     n_eff = 2 * N if epilogue == C.EPI_SWIGLU else N
     flops = 2.0 * M * n_eff * K * batch * k_batches
     _launch("gemm", flops, lambda: C.gemm(desc, _stream()))
@@ -182,8 +191,9 @@ def einsum_backward(plan: EinsumPlan, dout: torch.Tensor, saved, bwd_fmt: int, n
 # ----------------------------------------------------------------------------- GMLP
 # The six contractions of one GMLP step (ueaj/model/mlp.py:100-115 and the backward JAX
 # derives for it).  Shapes: x [T, d], Wf [2, d, h] (index 0 = up, 1 = gate), Wd [h, d].
-def gmlp_f1(qx: Fp8Tensor, qwf: Fp8Tensor):
-    """[U, G] = x Wf with H = U * swish(G) and max|H| from the epilogue."""
+def gmlp_f1(qx: Fp8Tensor, qwf: Fp8Tensor, ag: tuple | None = None):
+    """[U, G] = x Wf with H = U * swish(G) and max|H| from the epilogue.  `ag`: x's row
+    blocks arrive by ufp8_tp_ag_push (flags, epoch, rank, rows per rank)."""
     T, d = qx.q.shape
     h = qwf.q.shape[2]
     dev = qx.q.device
@@ -191,7 +201,7 @@ def gmlp_f1(qx: Fp8Tensor, qwf: Fp8Tensor):
     hid = torch.empty((T, h), dtype=torch.bfloat16, device=dev)
     amax_h = torch.empty(1, dtype=torch.float32, device=dev)
     gemm(operand(qx, C.K_MAJOR, d), operand(qwf, C.MN_MAJOR, h, d * h, 2), T, h, d, ug, h, T * h,
-         epilogue=C.EPI_SWIGLU, h=hid, ldh=h, amax_out=amax_h)
+         epilogue=C.EPI_SWIGLU, h=hid, ldh=h, amax_out=amax_h, ag=ag)
     return ug, hid, amax_h
 
 
@@ -204,15 +214,16 @@ def gmlp_f2(qh: Fp8Tensor, qwd: Fp8Tensor) -> torch.Tensor:
     return y
 
 
-def gmlp_b2(qdy: Fp8Tensor, qwd: Fp8Tensor, ug: torch.Tensor):
-    """dH = dY Wd^T fused with the gating backward -> [dU, dG] and max|dU, dG|."""
+def gmlp_b2(qdy: Fp8Tensor, qwd: Fp8Tensor, ug: torch.Tensor, ag: tuple | None = None):
+    """dH = dY Wd^T fused with the gating backward -> [dU, dG] and max|dU, dG|.  `ag`: dY's
+    row blocks arrive by ufp8_tp_ag_push."""
     T, d = qdy.q.shape
     h = qwd.q.shape[0]
     dev = qdy.q.device
     dug = torch.empty((2, T, h), dtype=torch.bfloat16, device=dev)
     amax_dug = torch.empty(1, dtype=torch.float32, device=dev)
     gemm(operand(qdy, C.K_MAJOR, d), operand(qwd, C.K_MAJOR, d), T, h, d, dug, h, T * h,
-         epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug)
+         epilogue=C.EPI_DSWIGLU, ug=ug, ldug=h, ug_batch_stride=T * h, amax_out=amax_dug, ag=ag)
     return dug, amax_dug
 
 

@@ -33,6 +33,18 @@ from .configurator import config
 from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 
 
+class _DeviceBytes:
+    """A raw device allocation seen through __cuda_array_interface__ (no ownership)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": "|u1",
+                                         "strides": None, "version": 3}
+
+
+def _device_bytes(ptr: int, shape, device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceBytes(ptr, shape), device=device)
+
+
 class TPContext:
     """Process group, rank layout and compute backend of one tensor-parallel block.
 
@@ -51,6 +63,8 @@ class TPContext:
         self.fused_rs = fused_reduce_scatter and backend is None and self.world > 1
         self._rs = None
         self._ex = None  # small-value (amax) exchange context
+        self._ag = {}    # all-gather contexts by tensor role ("x", "dy")
+        self._side = None
 
     def _rs_ctx(self, slot_bytes: int) -> C.TPReduceScatter:
         """Collective: (re)creates the peer-mapped staging when a larger slot is needed."""
@@ -58,11 +72,7 @@ class TPContext:
             if self._rs is not None:
                 torch.cuda.synchronize()
                 self._rs.close()
-            rs = C.TPReduceScatter(self.rank, self.world, slot_bytes)
-            handles = [None] * self.world
-            dist.all_gather_object(handles, rs.handle, group=self.group)
-            rs.connect(handles)
-            self._rs = rs
+            self._rs = self._connect(slot_bytes)
         return self._rs
 
     def push_reduce_scatter(self, push, rows: int, cols: int, dtype, device, between=None):
@@ -80,21 +90,63 @@ class TPContext:
         return out, mid
 
     def close(self) -> None:
-        for ctx in (self._rs, self._ex):
+        for ctx in (self._rs, self._ex, *self._ag.values()):
             if ctx is not None:
                 ctx.close()
         self._rs = self._ex = None
+        self._ag = {}
+
+    def _connect(self, slot_bytes: int) -> C.TPReduceScatter:
+        """Collective: a new peer-mapped context, its IPC handles exchanged over the group."""
+        ctx = C.TPReduceScatter(self.rank, self.world, slot_bytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, ctx.handle, group=self.group)
+        ctx.connect(handles)
+        return ctx
+
+    def gather_tokens_p2p(self, role: str, x: torch.Tensor, fmt: int, amax_t: torch.Tensor):
+        """Quantizes this rank's token shard x [T/k, d] straight into its slot of the
+        all-gather buffer and starts copying it to every peer on a side stream (copy engines).
+        Returns (the gathered Fp8Tensor [T, d] over the staging memory, the `ag` tuple for
+        the consuming GEMM, the side stream's completion event, the epoch), or None when the
+        shapes do not allow it (T/k not a multiple of 256, or T/k * d not of 256 bytes)."""
+        rl, d = x.shape
+        nbytes = rl * d
+        if rl % 256 or nbytes % 256 or self.world > 32:
+            return None
+        ctx = self._ag.get(role)
+        if ctx is None or ctx.slot_bytes != nbytes:  # the gathered view needs slot == block
+            if ctx is not None:
+                torch.cuda.synchronize()
+                ctx.close()
+            ctx = self._ag[role] = self._connect(nbytes)
+        _, epoch = ctx.begin()
+        data, flags = ctx.local(epoch)
+        full = _device_bytes(data, (rl * self.world, d), x.device).view(cuda_ops.FP8_DTYPE[fmt])
+        q = self.be.quantize(x, fmt, amax_t, out=full[self.rank * rl:(self.rank + 1) * rl])
+        main = torch.cuda.current_stream()
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=x.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        self._side.wait_event(ready)
+        ctx.ag_push(epoch, nbytes, self._side.cuda_stream)
+        done = torch.cuda.Event()
+        done.record(self._side)
+        return cuda_ops.Fp8Tensor(full, q.inv_scale, q.amax), (flags, epoch, self.rank, rl), done, epoch
+
+    def gathered_still_valid(self, role: str, epoch: int) -> bool:
+        """The all-gather buffer of `epoch` is one of two that alternate: it is overwritten by
+        the gather two epochs later."""
+        ctx = self._ag.get(role)
+        return ctx is not None and ctx.epoch - epoch < 2
 
     def allreduce_max_(self, a: torch.Tensor) -> torch.Tensor:
         """In-place MAX all-reduce of a few amax values (f32, non-negative): over NVLink peer
         memory with the CUDA backend and fused collectives, else a NCCL/gloo all-reduce."""
         if self.fused_rs and a.numel() <= 8:
             if self._ex is None:  # collective: every rank creates it at the same call
-                ex = C.TPReduceScatter(self.rank, self.world, 256)
-                handles = [None] * self.world
-                dist.all_gather_object(handles, ex.handle, group=self.group)
-                ex.connect(handles)
-                self._ex = ex
+                self._ex = self._connect(256)
             a = a.contiguous()
             self._ex.allreduce_max(a.data_ptr(), a.data_ptr(), a.numel(), torch.cuda.current_stream().cuda_stream)
             return a
@@ -132,9 +184,26 @@ class _TPGMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, wf, wd, tp: TPContext):
         be = tp.be
-        qx_local, qwf, qwd = tp.quant_global_many([(x, C.E4M3), (wf, C.E4M3), (wd, C.E4M3)])
-        qx = tp.all_gather_tokens(qx_local)
-        ug, hid, amax_h = be.gmlp_f1(qx, qwf)
+        gathered = None
+        if tp.fused_rs:
+            # one exchange for the three amax values, then x quantized into the all-gather
+            # buffer; F1 consumes the peers' blocks as the copy engines deliver them.
+            amaxes = tp.allreduce_max_(torch.cat([be.amax(x), be.amax(wf), be.amax(wd)]))
+            gathered = tp.gather_tokens_p2p("x", x, C.E4M3, amaxes[0:1])
+            qwf = be.quantize(wf, C.E4M3, amaxes[1:2])
+            qwd = be.quantize(wd, C.E4M3, amaxes[2:3])
+        if gathered is not None:
+            qx, ag, done, ctx.x_epoch = gathered
+            ug, hid, amax_h = be.gmlp_f1(qx, qwf, ag=ag)
+            torch.cuda.current_stream().wait_event(done)
+        else:
+            if tp.fused_rs:
+                qx_local = be.quantize(x, C.E4M3, amaxes[0:1])
+            else:
+                qx_local, qwf, qwd = tp.quant_global_many([(x, C.E4M3), (wf, C.E4M3), (wd, C.E4M3)])
+            qx = tp.all_gather_tokens(qx_local)
+            ctx.x_epoch = None
+            ug, hid, amax_h = be.gmlp_f1(qx, qwf)
         amax_h = tp.allreduce_max_(amax_h)
         qh = be.quantize(hid, C.E4M3, amax_h)
         if tp.fused_rs:
@@ -153,8 +222,20 @@ class _TPGMLPFn(torch.autograd.Function):
         be = tp.be
         qx, qwf, ug, qh, qwd = ctx.saved
         ctx.saved = None
-        qdy = tp.all_gather_tokens(tp.quant_global(dy.to(torch.bfloat16).contiguous(), C.E5M2))
-        dug, amax_dug = be.gmlp_b2(qdy, qwd, ug)
+        if ctx.x_epoch is not None and not tp.gathered_still_valid("x", ctx.x_epoch):
+            raise RuntimeError("TPGMLP: the all-gathered input of this forward pass was overwritten; with "
+                               "the NVLink all-gather at most two forward passes may await their backward")
+        dyb = dy.to(torch.bfloat16).contiguous()
+        gathered = None
+        if tp.fused_rs:
+            gathered = tp.gather_tokens_p2p("dy", dyb, C.E5M2, tp.global_amax(dyb))
+        if gathered is not None:
+            qdy, ag, done, _ = gathered
+            dug, amax_dug = be.gmlp_b2(qdy, qwd, ug, ag=ag)
+            torch.cuda.current_stream().wait_event(done)
+        else:
+            qdy = tp.all_gather_tokens(tp.quant_global(dyb, C.E5M2))
+            dug, amax_dug = be.gmlp_b2(qdy, qwd, ug)
         amax_dug = tp.allreduce_max_(amax_dug)
         dwd = be.gmlp_b1(qh, qdy)
         qdug = be.quantize(dug, C.E5M2, amax_dug)

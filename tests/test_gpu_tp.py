@@ -41,11 +41,20 @@ def _worker(rank, world, port, outdir, fused=True):
         xb = op.bf16_normal(rng, (T, D))
         dyb = op.bf16_normal(rng, (T, D), 1e-3)
         to_t = lambda b: torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).to(dev)  # noqa: E731
-        x = m.shard_tokens(to_t(xb)).requires_grad_(True)
-        y = m(x)
-        y.backward(m.shard_tokens(to_t(dyb)))
-        torch.cuda.synchronize()
         bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        first = None
+        for it in range(3):  # every staging buffer used at least twice: results must repeat bit for bit
+            for p in m.parameters():
+                p.grad = None
+            x = m.shard_tokens(to_t(xb)).requires_grad_(True)
+            y = m(x)
+            y.backward(m.shard_tokens(to_t(dyb)))
+            torch.cuda.synchronize()
+            now = [bits(t) for t in (y, x.grad, m.fused_proj.w.grad, m.down_proj.w.grad)]
+            if first is None:
+                first = now
+            else:
+                assert all(np.array_equal(a, b) for a, b in zip(first, now)), f"iteration {it} differs"
         from macrogpt_jax_b200 import _capi
         assert _capi.device_status() == 0
         np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=bits(y), dx=bits(x.grad),

@@ -115,3 +115,68 @@ def test_allreduce_max_missing_peer_times_out(cuda):
     finally:
         a.close()
         b.close()
+
+
+def _ag_setup(cuda, world, rows_per_rank, d):
+    """A connected group of `world` contexts on this GPU; returns rank 0's context, epoch and
+    its arrival flags as an int32 tensor view."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200.tp import _device_bytes
+    ctxs = [C.TPReduceScatter(r, world, rows_per_rank * d) for r in range(world)]
+    for c in ctxs:
+        c.connect_local(ctxs)
+    _, epoch = ctxs[0].begin()
+    _, flags_ptr = ctxs[0].local(epoch)
+    flags = _device_bytes(flags_ptr, (4 * world,), cuda).view(torch.int32)
+    return ctxs, epoch, flags_ptr, flags
+
+
+@pytest.mark.parametrize("ag_rank", [0, 2])
+def test_all_gathered_f1_matches_plain(cuda, ag_rank):
+    """F1 whose x row blocks are marked arrived through the all-gather flags (tile order
+    rotated to this rank's block, one block per raster group) equals the plain F1 bit for bit."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200 import ops
+    world, rl, d, h = 4, 256, 256, 384
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(5)
+    qx = ops.quantize(torch.randn((world * rl, d), generator=gen, device=cuda).to(torch.bfloat16), C.E4M3)
+    qwf = ops.quantize((torch.randn((2, d, h), generator=gen, device=cuda) * 0.06).to(torch.bfloat16), C.E4M3)
+    ref = ops.gmlp_f1(qx, qwf)
+    ctxs, epoch, flags_ptr, flags = _ag_setup(cuda, world, rl, d)
+    try:
+        flags.fill_(epoch)
+        got = ops.gmlp_f1(qx, qwf, ag=(flags_ptr, epoch, ag_rank, rl))
+        torch.cuda.synchronize()
+        for a, b in zip(got, ref):
+            assert torch.equal(a, b)
+        assert C.device_status() == 0
+    finally:
+        for c in ctxs:
+            c.close()
+
+
+def test_all_gather_missing_block_times_out(cuda):
+    """A row block whose arrival flag nothing sets: the GEMM producer gives up after its bounded
+    wait, the peer-timeout bit is set and the GPU stays usable."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200 import ops
+    world, rl, d, h = 2, 256, 128, 128
+    qx = ops.quantize(torch.ones((world * rl, d), dtype=torch.bfloat16, device=cuda), C.E4M3)
+    qwf = ops.quantize(torch.ones((2, d, h), dtype=torch.bfloat16, device=cuda), C.E4M3)
+    ctxs, epoch, flags_ptr, flags = _ag_setup(cuda, world, rl, d)
+    try:
+        flags.zero_()
+        t0 = time.time()
+        ops.gmlp_f1(qx, qwf, ag=(flags_ptr, epoch, 0, rl))
+        status = C.device_status(clear=True)
+        assert status & C.STATUS_PEER_TIMEOUT
+        assert time.time() - t0 < 30
+        assert C.device_status() == 0
+        assert float((torch.ones(8, device=cuda) * 3).sum()) == 24.0
+    finally:
+        for c in ctxs:
+            c.close()
