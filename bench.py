@@ -205,11 +205,15 @@ def run_ours(args, cfg, rank, world, local_rank):
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
     if world > 1:
+        from macrogpt_jax_b200 import tp as tp_mod
         from macrogpt_jax_b200.tp import TPGMLP
+        tp_mod.AG_ENGINE = _capi.AG_SM if args.tp_ag == "sm" else _capi.AG_COPY_ENGINE
         mlp = TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
                      fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5),
                      fused_reduce_scatter=args.tp_rs == "p2p")
-        parallelism = f"tp{world} (reduce-scatter: {'NVLink P2P from the GEMM epilogue' if args.tp_rs == 'p2p' else 'NCCL'})"
+        parallelism = (f"tp{world} (all-gather + reduce-scatter: NVLink P2P fused with the GEMMs, all-gather by "
+                       f"{'SM push kernel' if args.tp_ag == 'sm' else 'copy engines'})" if args.tp_rs == "p2p"
+                       else f"tp{world} (NCCL all-gather / reduce-scatter / all-reduce)")
     else:
         mlp = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(d ** -0.5)),
                             down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
@@ -441,6 +445,8 @@ def main():
     ap.add_argument("--gemm-variant", type=int, default=0, choices=[0, 1, 2, 3],
                     help="GEMM kernel variant (ufp8_set_gemm_variant): 0 auto, 1 one CTA per tile, "
                          "2 CTA pair, 3 CTA pair with direct epilogue loads/stores")
+    ap.add_argument("--tp-ag", choices=["sm", "ce"], default="ce",
+                    help="P2P all-gather engine: an SM push kernel beside the GEMM, or copy engines")
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p",
                     help="tensor-parallel reduce-scatter: fused into the GEMM epilogue over NVLink, or NCCL")
     args = ap.parse_args()

@@ -199,12 +199,20 @@ int ufp8_tp_local(ufp8_tp_ctx* ctx, uint64_t epoch, void** data, uint32_t** flag
 /* All-gather over the same staging layout (replaces the all-gather GSPMD would insert before
  * the column-split gate/up projection and the down projection's input gradient, implied by
  * ueaj/model/layer.py:57 token sharding and ueaj/model/mlp.py:85 'tensor' on hidden): the
- * caller has written this rank's block (`bytes` <= slot_bytes) into its own slot [rank] of the
- * buffer of `epoch`; this call copies it into slot [rank] of every peer, in the order rank-1,
- * rank-2, ... (mod k), each copy followed by a stream write of `epoch` into that peer's
- * flag[rank] (with a memory fence before the write).  Copy engines move the data, so `stream`
- * can run beside a GEMM that consumes the blocks as they arrive (ufp8_gemm_desc.ag_*). */
-int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, ufp8_stream_t stream);
+ * caller has written this rank's block (`bytes` <= slot_bytes, a multiple of 16) into its own
+ * slot [rank] of the buffer of `epoch`; this call copies it into slot [rank] of the peers
+ * rank-1, rank-2, ..., rank-(k-1) (mod k), in that order, and sets each peer's flag[rank] to
+ * `epoch` once its copy is complete.  `stream` can run beside a GEMM that consumes the blocks
+ * as they arrive (ufp8_gemm_desc.ag_*).  Engines:
+ *   UFP8_AG_COPY_ENGINE  one cudaMemcpyAsync per peer, each followed by a stream write of the
+ *                        flag (with a memory fence before it);
+ *   UFP8_AG_SM           one small kernel (256-thread CTAs, no shared memory, so its CTAs fit
+ *                        beside a persistent GEMM): 16-byte coalesced stores into the peers,
+ *                        the last CTA of each destination sets its flag with a system-scope
+ *                        release. */
+#define UFP8_AG_COPY_ENGINE 0
+#define UFP8_AG_SM 1
+int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine, ufp8_stream_t stream);
 
 /* MAX all-reduce of n (1..8) non-negative f32 values (per-tensor amax values) over the group
  * of a connected context: every rank's `out` receives the elementwise maximum of all ranks'

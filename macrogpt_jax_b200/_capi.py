@@ -14,6 +14,7 @@ OK = 0
 ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
 STATUS_WAIT_TIMEOUT, STATUS_PEER_TIMEOUT = 1, 2
 IPC_HANDLE_BYTES = 64
+AG_COPY_ENGINE, AG_SM = 0, 1
 E4M3, E5M2 = 0, 1
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
@@ -135,7 +136,7 @@ def load() -> ctypes.CDLL:
     lib.ufp8_tp_finish.argtypes = [vp, ctypes.c_uint64, i64, i64, i64, vp, i64, vp]
     lib.ufp8_tp_allreduce_max.argtypes = [vp, vp, vp, i32, vp]
     lib.ufp8_tp_local.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
-    lib.ufp8_tp_ag_push.argtypes = [vp, ctypes.c_uint64, i64, vp]
+    lib.ufp8_tp_ag_push.argtypes = [vp, ctypes.c_uint64, i64, i32, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
@@ -247,10 +248,11 @@ class TPReduceScatter:
         check(load().ufp8_tp_local(self.ctx, epoch, ctypes.byref(data), ctypes.byref(flags)))
         return data.value, flags.value
 
-    def ag_push(self, epoch: int, nbytes: int, stream: int) -> None:
-        """Copies this rank's slot of `epoch`'s buffer into every peer's (copy engines), each
-        copy followed by the arrival flag."""
-        check(load().ufp8_tp_ag_push(self.ctx, epoch, nbytes, stream))
+    def ag_push(self, epoch: int, nbytes: int, stream: int, engine: int = AG_COPY_ENGINE) -> None:
+        """Copies this rank's slot of `epoch`'s buffer into every peer's (AG_SM: a small kernel;
+        AG_COPY_ENGINE: copy engines), each followed by the arrival flag."""
+        check(load().ufp8_tp_ag_push(self.ctx, epoch, nbytes, engine, stream))
+        _count(1 if engine == AG_SM and self.world > 1 else 0)
 
     def allreduce_max(self, in_ptr: int, out_ptr: int, n: int, stream: int) -> None:
         """Elementwise MAX over the group of n (1..8) non-negative device f32 values."""

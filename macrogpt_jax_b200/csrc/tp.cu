@@ -219,6 +219,49 @@ __global__ void __launch_bounds__(32) tp_exchange_max_kernel(const ExchangeArgs 
   }
 }
 
+constexpr int kAgThreads = 256;
+constexpr int kAgCtasPerDst = 16;
+constexpr size_t kAgCounterOffset = 128;  // per-destination counters inside the flags area
+
+struct AgPushArgs {
+  const uint4* src;
+  uint4* dst[kMaxRanks];        // [i-1]: slot [rank] of peer rank-i
+  uint32_t* flag[kMaxRanks];    // [i-1]: flag[rank] of peer rank-i
+  unsigned int* counter;        // [i-1]: CTAs of destination i done (own memory, self-resetting)
+  long long n16;
+  uint32_t epoch;
+};
+
+// Copies this rank's all-gather block to the k-1 peers; CTAs [ (i-1)*C, i*C ) serve peer
+// rank-i, so the earliest destinations are scheduled first.  Each CTA: coalesced 16-byte
+// loads and remote stores, then (thread 0, after __syncthreads) a system-scope fence and a
+// count; the destination's last CTA resets the count and releases the peer's flag.
+__global__ void __launch_bounds__(kAgThreads) tp_ag_push_kernel(const AgPushArgs a) {
+  const int di = blockIdx.x / kAgCtasPerDst;
+  const int cb = blockIdx.x - di * kAgCtasPerDst;
+  uint4* dst = a.dst[di];
+  const long long stride = static_cast<long long>(kAgCtasPerDst) * kAgThreads;
+  long long i = static_cast<long long>(cb) * kAgThreads + threadIdx.x;
+  for (; i + 3 * stride < a.n16; i += 4 * stride) {
+    const uint4 v0 = a.src[i], v1 = a.src[i + stride], v2 = a.src[i + 2 * stride], v3 = a.src[i + 3 * stride];
+    dst[i] = v0;
+    dst[i + stride] = v1;
+    dst[i + 2 * stride] = v2;
+    dst[i + 3 * stride] = v3;
+  }
+  for (; i < a.n16; i += stride) dst[i] = a.src[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(a.counter + di, 1u);
+    if (prev == kAgCtasPerDst - 1) {
+      a.counter[di] = 0u;
+      __threadfence_system();
+      st_release_sys(a.flag[di], a.epoch);
+    }
+  }
+}
+
 }  // namespace
 
 }  // namespace ufp8
@@ -406,14 +449,34 @@ int ufp8_tp_local(ufp8_tp_ctx* ctx, uint64_t epoch, void** data, uint32_t** flag
   return UFP8_OK;
 }
 
-int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, ufp8_stream_t stream) {
+int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine, ufp8_stream_t stream) {
   TPContext* c = reinterpret_cast<TPContext*>(ctx);
   if (!c) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: null context");
+  if (engine != UFP8_AG_COPY_ENGINE && engine != UFP8_AG_SM)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: unknown engine %d", engine);
+  if (bytes % 16) return set_error(UFP8_ERR_ALIGN, "ufp8_tp_ag_push: bytes must be a multiple of 16");
   if (epoch == 0 || epoch > c->epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: epoch not begun");
   if (bytes < 0 || static_cast<size_t>(bytes) > c->slot_bytes)
     return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: %lld bytes exceed the slot", static_cast<long long>(bytes));
   for (int p = 0; p < c->world; ++p)
     if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_ag_push: rank %d is not connected", p);
+  if (engine == UFP8_AG_SM) {
+    if (c->world == 1) return UFP8_OK;
+    const size_t off = (epoch & 1) * c->buffer_bytes;
+    AgPushArgs a{};
+    a.src = reinterpret_cast<const uint4*>(c->base + off + kFlagBytes + c->rank * c->slot_bytes);
+    for (int i = 1; i < c->world; ++i) {
+      const int p = (c->rank - i + c->world) % c->world;
+      a.dst[i - 1] = reinterpret_cast<uint4*>(c->peer_base[p] + off + kFlagBytes + c->rank * c->slot_bytes);
+      a.flag[i - 1] = reinterpret_cast<uint32_t*>(c->peer_base[p] + off) + c->rank;
+    }
+    a.counter = reinterpret_cast<unsigned int*>(c->base + off + kAgCounterOffset);
+    a.n16 = bytes / 16;
+    a.epoch = static_cast<uint32_t>(epoch);
+    tp_ag_push_kernel<<<(c->world - 1) * kAgCtasPerDst, kAgThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? UFP8_OK : cuda_error(e, "all-gather push launch");
+  }
   using WriteValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
   static WriteValueFn write_value = [] {
     void* fn = nullptr;

@@ -33,6 +33,13 @@ from .configurator import config
 from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 
 
+# How the all-gather moves each rank's block to its peers: C.AG_COPY_ENGINE (cudaMemcpyAsync
+# per peer, no SM resources) or C.AG_SM (a small push kernel).  The copy engines win at TP 8:
+# the push kernel's CTAs hold the SMs that the consuming GEMM (one CTA pair per two SMs with
+# ~225 KiB of shared memory each) needs, so the GEMM starts only when the push ends.
+AG_ENGINE = C.AG_COPY_ENGINE
+
+
 class _DeviceBytes:
     """A raw device allocation seen through __cuda_array_interface__ (no ownership)."""
 
@@ -106,9 +113,9 @@ class TPContext:
 
     def gather_tokens_p2p(self, role: str, x: torch.Tensor, fmt: int, amax_t: torch.Tensor):
         """Quantizes this rank's token shard x [T/k, d] straight into its slot of the
-        all-gather buffer and starts copying it to every peer on a side stream (copy engines).
+        all-gather buffer and starts copying it to every peer on a side stream (AG_ENGINE).
         Returns (the gathered Fp8Tensor [T, d] over the staging memory, the `ag` tuple for
-        the consuming GEMM, the side stream's completion event, the epoch), or None when the
+        the consuming GEMM, [the side stream's completion event], the epoch), or None when the
         shapes do not allow it (T/k not a multiple of 256, or T/k * d not of 256 bytes)."""
         rl, d = x.shape
         nbytes = rl * d
@@ -130,10 +137,10 @@ class TPContext:
         ready = torch.cuda.Event()
         ready.record(main)
         self._side.wait_event(ready)
-        ctx.ag_push(epoch, nbytes, self._side.cuda_stream)
+        ctx.ag_push(epoch, nbytes, self._side.cuda_stream, AG_ENGINE)
         done = torch.cuda.Event()
         done.record(self._side)
-        return cuda_ops.Fp8Tensor(full, q.inv_scale, q.amax), (flags, epoch, self.rank, rl), done, epoch
+        return cuda_ops.Fp8Tensor(full, q.inv_scale, q.amax), (flags, epoch, self.rank, rl), [done], epoch
 
     def gathered_still_valid(self, role: str, epoch: int) -> bool:
         """The all-gather buffer of `epoch` is one of two that alternate: it is overwritten by
@@ -195,7 +202,8 @@ class _TPGMLPFn(torch.autograd.Function):
         if gathered is not None:
             qx, ag, done, ctx.x_epoch = gathered
             ug, hid, amax_h = be.gmlp_f1(qx, qwf, ag=ag)
-            torch.cuda.current_stream().wait_event(done)
+            for ev in done:
+                torch.cuda.current_stream().wait_event(ev)
         else:
             if tp.fused_rs:
                 qx_local = be.quantize(x, C.E4M3, amaxes[0:1])
@@ -232,7 +240,8 @@ class _TPGMLPFn(torch.autograd.Function):
         if gathered is not None:
             qdy, ag, done, _ = gathered
             dug, amax_dug = be.gmlp_b2(qdy, qwd, ug, ag=ag)
-            torch.cuda.current_stream().wait_event(done)
+            for ev in done:
+                torch.cuda.current_stream().wait_event(ev)
         else:
             qdy = tp.all_gather_tokens(tp.quant_global(dyb, C.E5M2))
             dug, amax_dug = be.gmlp_b2(qdy, qwd, ug)

@@ -21,7 +21,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, outdir, fused=True):
+def _worker(rank, world, port, outdir, fused=True, ag_engine=1):
     import sys
     import torch.distributed as dist
     sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
@@ -30,8 +30,10 @@ def _worker(rank, world, port, outdir, fused=True):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
     try:
+        from macrogpt_jax_b200 import tp as tp_mod
         from macrogpt_jax_b200.einsum import Rngs, scaled_normal_init
         from macrogpt_jax_b200.tp import TPGMLP
+        tp_mod.AG_ENGINE = ag_engine
         from oracle import path as op
         dev = torch.device("cuda", rank)
         m = TPGMLP(D, H, rngs=Rngs(7), device=dev, fused_init=scaled_normal_init(D ** -0.5),
@@ -64,8 +66,9 @@ def _worker(rank, world, port, outdir, fused=True):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused", [True, False], ids=["p2p_reduce_scatter", "nccl_reduce_scatter"])
-def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused):
+@pytest.mark.parametrize("fused,ag_engine", [(True, 1), (True, 0), (False, 1)],
+                         ids=["p2p_sm_push", "p2p_copy_engine", "nccl"])
+def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused, ag_engine):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -74,7 +77,7 @@ def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused):
     from macrogpt_jax_b200.mlp import GMLP
     from oracle import path as op
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(2, _port(), str(tmp_path), fused), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), fused, ag_engine), nprocs=2, join=True)
     r = [np.load(tmp_path / f"rank{i}.npz") for i in range(2)]
     cpu = torch.device("cpu")
     full = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5), device=cpu),
