@@ -220,44 +220,46 @@ __global__ void __launch_bounds__(32) tp_exchange_max_kernel(const ExchangeArgs 
 }
 
 constexpr int kAgThreads = 256;
-constexpr int kAgCtasPerDst = 16;
+constexpr int kAgCtas = 64;
 constexpr size_t kAgCounterOffset = 128;  // per-destination counters inside the flags area
 
 struct AgPushArgs {
   const uint4* src;
   uint4* dst[kMaxRanks];        // [i-1]: slot [rank] of peer rank-i
   uint32_t* flag[kMaxRanks];    // [i-1]: flag[rank] of peer rank-i
-  unsigned int* counter;        // [i-1]: CTAs of destination i done (own memory, self-resetting)
+  unsigned int* counter;        // [i-1]: CTAs done with destination i (own memory, self-resetting)
   long long n16;
+  int ndst;
   uint32_t epoch;
 };
 
-// Copies this rank's all-gather block to the k-1 peers; CTAs [ (i-1)*C, i*C ) serve peer
-// rank-i, so the earliest destinations are scheduled first.  Each CTA: coalesced 16-byte
-// loads and remote stores, then (thread 0, after __syncthreads) a system-scope fence and a
-// count; the destination's last CTA resets the count and releases the peer's flag.
-__global__ void __launch_bounds__(kAgThreads) tp_ag_push_kernel(const AgPushArgs a) {
-  const int di = blockIdx.x / kAgCtasPerDst;
-  const int cb = blockIdx.x - di * kAgCtasPerDst;
-  uint4* dst = a.dst[di];
-  const long long stride = static_cast<long long>(kAgCtasPerDst) * kAgThreads;
-  long long i = static_cast<long long>(cb) * kAgThreads + threadIdx.x;
-  for (; i + 3 * stride < a.n16; i += 4 * stride) {
-    const uint4 v0 = a.src[i], v1 = a.src[i + stride], v2 = a.src[i + 2 * stride], v3 = a.src[i + 3 * stride];
-    dst[i] = v0;
-    dst[i + stride] = v1;
-    dst[i + 2 * stride] = v2;
-    dst[i + 3 * stride] = v3;
-  }
-  for (; i < a.n16; i += stride) dst[i] = a.src[i];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned int prev = atomicAdd(a.counter + di, 1u);
-    if (prev == kAgCtasPerDst - 1) {
-      a.counter[di] = 0u;
+// Copies this rank's all-gather block to the k-1 peers, one destination after the other so
+// that the blocks arrive staggered in the order the consuming GEMMs use them.  Every CTA
+// copies its share of the block to destination i (coalesced 16-byte loads and remote stores),
+// then thread 0 (after __syncthreads) fences at system scope and counts; the last CTA of a
+// destination resets the count and releases that peer's flag.  No shared memory, at most 32
+// registers a thread: with the maximum shared-memory carveout its CTAs fit beside a persistent
+// GEMM CTA (320 threads x 168 registers, ~225 KiB of shared memory).
+__global__ void __launch_bounds__(kAgThreads, 8) tp_ag_push_kernel(const AgPushArgs a) {
+  const long long stride = static_cast<long long>(gridDim.x) * kAgThreads;
+  for (int di = 0; di < a.ndst; ++di) {
+    uint4* dst = a.dst[di];
+    long long i = static_cast<long long>(blockIdx.x) * kAgThreads + threadIdx.x;
+    for (; i + stride < a.n16; i += 2 * stride) {
+      const uint4 v0 = a.src[i], v1 = a.src[i + stride];
+      dst[i] = v0;
+      dst[i + stride] = v1;
+    }
+    if (i < a.n16) dst[i] = a.src[i];
+    __syncthreads();
+    if (threadIdx.x == 0) {
       __threadfence_system();
-      st_release_sys(a.flag[di], a.epoch);
+      const unsigned int prev = atomicAdd(a.counter + di, 1u);
+      if (prev == gridDim.x - 1) {
+        a.counter[di] = 0u;
+        __threadfence_system();
+        st_release_sys(a.flag[di], a.epoch);
+      }
     }
   }
 }
@@ -472,8 +474,18 @@ int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine,
     }
     a.counter = reinterpret_cast<unsigned int*>(c->base + off + kAgCounterOffset);
     a.n16 = bytes / 16;
+    a.ndst = c->world - 1;
     a.epoch = static_cast<uint32_t>(epoch);
-    tp_ag_push_kernel<<<(c->world - 1) * kAgCtasPerDst, kAgThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+    static thread_local int carveout_device = -1;
+    if (carveout_device != c->device) {
+      // Without this hint the driver may run the push CTAs with a small shared-memory carveout,
+      // and no GEMM CTA (~225 KiB) can join an SM until they leave.
+      cudaError_t e = cudaFuncSetAttribute(tp_ag_push_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                           cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(push carveout)");
+      carveout_device = c->device;
+    }
+    tp_ag_push_kernel<<<kAgCtas, kAgThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? UFP8_OK : cuda_error(e, "all-gather push launch");
   }
