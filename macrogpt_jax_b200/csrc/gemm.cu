@@ -540,31 +540,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
-// Loads 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]);
-// elements at or past `valid` read as zero.
-__device__ __forceinline__ void load_bf16x32_packed(const __nv_bfloat16* p, uint32_t (&w)[16], int valid,
-                                                    bool vec) {
-  if (vec && valid >= 32) {
-    const uint4* q = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 t = q[i];
-      w[4 * i] = t.x;
-      w[4 * i + 1] = t.y;
-      w[4 * i + 2] = t.z;
-      w[4 * i + 3] = t.w;
-    }
-  } else {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t lo = (2 * j < valid) ? q[2 * j] : 0u;
-      const uint32_t hi = (2 * j + 1 < valid) ? q[2 * j + 1] : 0u;
-      w[j] = lo | (hi << 16);
-    }
-  }
-}
-
 // Loads 16 consecutive bf16 values packed two per word; elements at or past `valid` read 0.
 __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint32_t (&w)[8], int valid,
                                                     bool vec) {
@@ -584,9 +559,6 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
   }
 }
 
-__device__ __forceinline__ uint32_t half_of(const uint32_t (&w)[16], int j) {
-  return (j & 1) ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xFFFFu);
-}
 
 template <int NSTAGES, int kVar>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
