@@ -243,6 +243,13 @@ def run_ours(args, cfg, rank, world, local_rank):
         step(x_in, dy_in)
     torch.cuda.synchronize()
     barrier()
+    run = step
+    if args.graph:
+        if world > 1:
+            raise SystemExit("--graph runs on one GPU (the tensor-parallel path is not capturable)")
+        from macrogpt_jax_b200.graphs import GraphedStep
+        run = GraphedStep(step, x_in, dy_in, warmup=args.warmup)
+        torch.cuda.synchronize()
 
     # ---- headline: device-resident inputs, per-launch events on the launching stream
     timer = ops.KernelTimer()
@@ -252,10 +259,11 @@ def run_ours(args, cfg, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ops.set_timer(timer)
+    if not args.graph:
+        ops.set_timer(timer)
     ev0.record()
     for _ in range(args.steps):
-        step(x_in, dy_in)
+        run(x_in, dy_in)
     ev1.record()
     ops.set_timer(None)
     torch.cuda.synchronize()
@@ -263,6 +271,21 @@ def run_ours(args, cfg, rank, world, local_rank):
     launches = _capi.launches - launches0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    eager_ms = ms
+    if args.graph:
+        # Per-kernel CUDA events cannot be recorded inside a graph: the kernel shares and the
+        # roofline come from an eager pass of the same step right after the graph-timed region.
+        launches0 = _capi.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ops.set_timer(timer)
+        e0.record()
+        for _ in range(args.steps):
+            step(x_in, dy_in)
+        e1.record()
+        ops.set_timer(None)
+        torch.cuda.synchronize()
+        launches = _capi.launches - launches0  # the graph replays exactly these kernels
+        eager_ms = e0.elapsed_time(e1)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -280,7 +303,7 @@ def run_ours(args, cfg, rank, world, local_rank):
         for _ in range(2):
             x_dev.copy_(x_host, non_blocking=True)
             dy_dev.copy_(dy_host, non_blocking=True)
-            y_host.copy_(step(x_dev, dy_dev).detach(), non_blocking=True)
+            y_host.copy_(run(x_dev, dy_dev).detach(), non_blocking=True)
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -288,7 +311,7 @@ def run_ours(args, cfg, rank, world, local_rank):
         for _ in range(args.steps):
             x_dev.copy_(x_host, non_blocking=True)
             dy_dev.copy_(dy_host, non_blocking=True)
-            y_host.copy_(step(x_dev, dy_dev).detach(), non_blocking=True)
+            y_host.copy_(run(x_dev, dy_dev).detach(), non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         ems_t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
@@ -333,18 +356,23 @@ def run_ours(args, cfg, rank, world, local_rank):
                      "frac_of_nominal_fp8": (achieved / FP8_NOMINAL_TFLOPS) if achieved else None,
                      "peak_source": f"2 x bf16_tflops_sustained, {peak_src}; tcgen05 runs fp8 at twice "
                                     "its bf16 rate",
-                     "launches": g_n, "time_share": g_ms / ms if ms else None,
+                     "launches": g_n, "time_share": g_ms / eager_ms if eager_ms else None,
                      "traffic": traffic, "traffic_source": traffic_src},
         "roofline_quantize": {"bound": "hbm", "unit": "GB/s",
                               "achieved": (q_b / (q_ms / 1000.0) / 1e9) if q_n else None,
                               "peak": peaks["hbm_gbs"],
                               "frac": (q_b / (q_ms / 1000.0) / 1e9 / peaks["hbm_gbs"]) if q_n else None,
-                              "launches": q_n, "time_share": q_ms / ms if ms else None,
+                              "launches": q_n, "time_share": q_ms / eager_ms if eager_ms else None,
                               "amax_achieved_gbs": (a_b / (a_ms / 1000.0) / 1e9) if a_n else None,
-                              "amax_time_share": a_ms / ms if ms else None},
+                              "amax_time_share": a_ms / eager_ms if eager_ms else None},
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if args.graph:
+        out["config"]["execution"] = "CUDA graph of the whole step (macrogpt_jax_b200.graphs.GraphedStep)"
+        out["roofline"]["source"] = ("per-kernel CUDA events of an eager pass of the same step right after the "
+                                     "graph-timed region (events cannot be recorded inside a graph); time_share "
+                                     f"is of that pass ({eager_ms / args.steps:.3f} ms/step eager)")
     if e2e:
         out["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
@@ -391,21 +419,40 @@ def run_attn(args, cfg, rank, world, local_rank, dev):
     for _ in range(args.warmup):
         step(x, a)
     torch.cuda.synchronize()
+    run = step
+    if args.graph:
+        from macrogpt_jax_b200.graphs import GraphedStep
+        run = GraphedStep(step, x, a, warmup=args.warmup)
+        torch.cuda.synchronize()
     timer = ops.KernelTimer()
     clocks = ClockSampler(local_rank)
     clocks.start()
     launches0 = _capi.launches
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ops.set_timer(timer)
+    if not args.graph:
+        ops.set_timer(timer)
     ev0.record()
     for _ in range(args.steps):
-        step(x, a)
+        run(x, a)
     ev1.record()
     ops.set_timer(None)
     torch.cuda.synchronize()
     launches = _capi.launches - launches0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    eager_ms = ms
+    if args.graph:  # per-kernel events come from an eager pass (none can be recorded in a graph)
+        launches0 = _capi.launches
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ops.set_timer(timer)
+        e0.record()
+        for _ in range(args.steps):
+            step(x, a)
+        e1.record()
+        ops.set_timer(None)
+        torch.cuda.synchronize()
+        launches = _capi.launches - launches0
+        eager_ms = e0.elapsed_time(e1)
     summ = timer.summary()
     peaks, peak_src = load_peaks()
     fl = attn_flops_per_step(T, d)
@@ -413,7 +460,7 @@ def run_attn(args, cfg, rank, world, local_rank, dev):
     g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
     peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
     achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
-    return {
+    out = {
         "metric": "FP8 attention projections fwd+bwd tokens/s (TFLOP/s/GPU)", "value": T * args.steps / (ms / 1000.0),
         "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
@@ -423,9 +470,15 @@ def run_attn(args, cfg, rank, world, local_rank, dev):
         "roofline": {"kernel": "gemm_fp8_pair_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_fp8,
                      "unit": "TFLOP/s", "frac": (achieved / peak_fp8) if achieved else None,
                      "peak_source": f"2 x bf16_tflops_sustained, {peak_src}", "launches": g_n,
-                     "time_share": g_ms / ms if ms else None, "traffic": None},
+                     "time_share": g_ms / eager_ms if eager_ms else None, "traffic": None},
         "gpu_launches": launches, "clocks": clk,
     }
+    if args.graph:
+        out["config"]["execution"] = "CUDA graph of the whole step (macrogpt_jax_b200.graphs.GraphedStep)"
+        out["roofline"]["source"] = ("per-kernel CUDA events of an eager pass of the same step right after the "
+                                     "graph-timed region; time_share is of that pass "
+                                     f"({eager_ms / args.steps:.3f} ms/step eager)")
+    return out
 
 
 def main():
@@ -442,6 +495,9 @@ def main():
     ap.add_argument("--gemm-traffic", type=float, default=None,
                     help="DRAM bytes per GEMM launch to report as roofline.traffic (default: the "
                          "captured figure for gmlp_d4096 on one GPU, else null)")
+    ap.add_argument("--graph", action="store_true",
+                    help="one GPU: capture the whole step in a CUDA graph and time its replays (for the "
+                         "launch-bound small workloads)")
     ap.add_argument("--gemm-variant", type=int, default=0, choices=[0, 1, 2, 3],
                     help="GEMM kernel variant (ufp8_set_gemm_variant): 0 auto, 1 one CTA per tile, "
                          "2 CTA pair, 3 CTA pair with direct epilogue loads/stores")

@@ -52,6 +52,10 @@ def set_timer(t: KernelTimer | None) -> None:
     _timer = t
 
 
+def get_timer() -> KernelTimer | None:
+    return _timer
+
+
 def _launch(kind: str, work: float, fn) -> None:
     if _timer is None:
         fn()
