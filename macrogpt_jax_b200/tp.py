@@ -16,9 +16,12 @@ Every per-tensor scale is the scale of the WHOLE logical tensor (a MAX all-reduc
 local amax values), so each rank quantises exactly as the single-GPU path does; the only
 numerical difference from one GPU is the order of the final bf16 sums.
 
-Collectives go through torch.distributed (NCCL on GPUs).  The compute backend defaults to
-this package's CUDA ops; tests substitute a CPU backend to exercise the host logic over
-gloo.
+With the CUDA backend (default) every collective of the step runs over NVLink peer memory
+through this package's C ABI (see TPContext): the all-gathers are copy-engine pushes consumed
+block by block by the next GEMM, the reduce-scatters are pushed from the GEMM epilogues, and
+the amax MAX all-reduces are single-warp exchanges.  With `fused_reduce_scatter=False`, or a
+substituted backend (the tests use a CPU backend to exercise the host logic over gloo), they
+go through torch.distributed instead (NCCL on GPUs).
 """
 from __future__ import annotations
 
