@@ -26,7 +26,7 @@ def main() -> None:
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--hidden", type=int, default=14336)
-    ap.add_argument("--out", default="gpurun_out")
+    ap.add_argument("--out", default="timelines")
     args = ap.parse_args()
 
     from torch.profiler import ProfilerActivity, profile
