@@ -25,6 +25,7 @@ go through torch.distributed instead (NCCL on GPUs).
 """
 from __future__ import annotations
 
+import warnings
 from typing import Callable, Optional
 
 import torch
@@ -63,7 +64,12 @@ class TPContext:
     owner's staging slot (UFP8_EPI_RS_PUSH) and ufp8_tp_finish sums the slots on the owner,
     so the transfer overlaps the GEMM tile by tile; the MAX all-reduces of the amax values
     are then single-warp P2P exchanges (ufp8_tp_allreduce_max) instead of NCCL calls.
-    Otherwise NCCL's reduce-scatter runs after the GEMM and NCCL all-reduces the amax values."""
+    Otherwise NCCL's reduce-scatter runs after the GEMM and NCCL all-reduces the amax values.
+
+    Construction is collective.  With the P2P path it connects the exchange context right away
+    and the ranks agree (a MIN all-reduce of "connected") on whether peer mappings work; if any
+    rank cannot map its peers (no P2P between these GPUs), every rank uses NCCL instead and a
+    warning says so."""
 
     def __init__(self, group=None, backend=None, fused_reduce_scatter: bool = True):
         self.group = group
@@ -75,6 +81,36 @@ class TPContext:
         self._ex = None  # small-value (amax) exchange context
         self._ag = {}    # all-gather contexts by tensor role ("x", "dy")
         self._side = None
+        if self.fused_rs:
+            self.fused_rs = self._p2p_available()
+
+    def _p2p_available(self) -> bool:
+        """Collective: connects the exchange context; True on every rank iff it worked on all."""
+        if not torch.cuda.is_available():
+            return False
+        ex, err = None, None
+        try:
+            ex = C.TPReduceScatter(self.rank, self.world, 256)
+        except C.UFP8Error as e:
+            err = e
+        handles = [None] * self.world
+        dist.all_gather_object(handles, ex.handle if ex is not None else None, group=self.group)
+        if ex is not None and all(h is not None for h in handles):
+            try:
+                ex.connect(handles)
+            except C.UFP8Error as e:
+                err = e
+        ok = torch.tensor([0 if err is not None or ex is None else 1], dtype=torch.int32,
+                          device=torch.device("cuda", torch.cuda.current_device()))
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 1:
+            self._ex = ex
+            return True
+        if ex is not None:
+            ex.close()
+        warnings.warn(f"TPGMLP: NVLink peer mappings unavailable ({err or 'on another rank'}); "
+                      "using NCCL collectives")
+        return False
 
     def _rs_ctx(self, slot_bytes: int) -> C.TPReduceScatter:
         """Collective: (re)creates the peer-mapped staging when a larger slot is needed."""
@@ -278,10 +314,11 @@ class TPGMLP(torch.nn.Module):
         super().__init__()
         hidden_d = 4 * model_d if hidden_d is None else hidden_d
         group = group if group is not None else mesh
+        if hidden_d % dist.get_world_size(group):
+            raise ValueError(f"hidden {hidden_d} is not divisible by the tensor-parallel size "
+                             f"{dist.get_world_size(group)}")
         self.tp = TPContext(group, backend, fused_reduce_scatter)
         k, r = self.tp.world, self.tp.rank
-        if hidden_d % k:
-            raise ValueError(f"hidden {hidden_d} is not divisible by the tensor-parallel size {k}")
         if activation_fn is not None:
             from .mlp import swish
             if activation_fn is not swish:
