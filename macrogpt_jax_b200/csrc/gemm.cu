@@ -1,8 +1,14 @@
-// Persistent, warp-specialised FP8 GEMM for sm_100a (tcgen05 + TMEM + TMA).
+// Persistent, warp-specialised FP8 GEMMs for sm_100a (tcgen05 + TMEM + TMA).
 //
 //   D[g][m][n] = alpha * sum_k A[m][k] * B[n][k],  alpha = inv_scale_a * inv_scale_b
 //
-// One CTA per SM (192 threads, ~193 KB shared memory, all 512 TMEM columns):
+// Two kernels: gemm_fp8_pair_kernel (the default; further down) computes 256x256 tiles on a
+// cluster of two CTAs with tcgen05.mma.cta_group::2, in three instantiations that differ only
+// in how the epilogue moves data (direct stores; U/G of the dSwiGLU epilogue staged by TMA;
+// reduce-scatter rows pushed to peer GPUs by bulk stores).  gemm_fp8_kernel, described next,
+// is the one-CTA variant (UFP8_GEMM_SINGLE_CTA), kept for comparison and for the tests.
+//
+// One-CTA kernel: one CTA per SM (192 threads, ~193 KB shared memory, all 512 TMEM columns):
 //   warp 0      TMA producer: 4-stage ring of {A 128x128, B 256x128} fp8 tiles in
 //               128-byte-swizzled shared memory (plain per-CTA tiled loads);
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma.cta_group::1.kind::f8f6f4
