@@ -30,6 +30,14 @@
 namespace ufp8 {
 namespace {
 
+// 3-D tiled bulk tensor store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 128;  // bytes of K per stage = one 128-byte swizzle atom row
@@ -466,7 +474,9 @@ constexpr int kPStgBytes = kPEpiWarps * kPStgWarpBytes;
 // epilogue warp streams 32-row x 32-column bf16 boxes of U and G (64-byte swizzle, so the
 // lanes' 16-byte reads of their own rows are bank-conflict free) into a double buffer two
 // chunks ahead of its TMEM reads, including across tiles, so the loads of the next tile run
-// while this tile's MMAs are still in flight.
+// while this tile's MMAs are still in flight.  dU / dG overwrite the U / G granules they were
+// computed from and leave by TMA stores of the same boxes (a tensor map over D [2][M][N]), so
+// the epilogue warps issue no global stores either.
 constexpr int kVarDirect = 0;     // every epilogue, plain stores from registers
 constexpr int kVarRsStaged = 1;   // RS_PUSH rows through shared memory, bulk stores
 constexpr int kVarUgStaged = 2;   // DSWIGLU with U / G staged by TMA
@@ -569,7 +579,8 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 template <int NSTAGES, int kVar>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const __grid_constant__ CUtensorMap tmUG, const GemmArgs args) {
+                         const __grid_constant__ CUtensorMap tmUG, const __grid_constant__ CUtensorMap tmD,
+                         const GemmArgs args) {
   constexpr bool kStaged = kVar == kVarRsStaged;
   constexpr bool kUgStaged = kVar == kVarUgStaged;
   extern __shared__ uint8_t smem_raw[];
@@ -780,7 +791,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kBN);
 
       if (kUgStaged) {
-        // DSWIGLU with U / G from shared memory (TMA-staged two chunks ahead).
+        // DSWIGLU with U / G from shared memory (TMA-staged two chunks ahead); dU / dG written
+        // back into the same boxes and stored by TMA.
         bool ug_ok = true;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -797,45 +809,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
           ug_used = j + 1;
           const int col0 = nb * kBN + chalf * 128 + c * kPUgCols;
-          if (row_ok && col0 < args.N) {
-            const int valid = args.N - col0;
-            const uint8_t* su = ugw + b * kPUgBufBytes + lane * (kPUgCols * 2);
-            const uint8_t* sg = su + kPUgBoxBytes;
-            const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this row's 16-byte granules
-            uint32_t odu[16], odg[16];
-            uint32_t m2 = 0;  // packed 2 x 16-bit max of |dU|, |dG|
+          const int valid = row_ok ? args.N - col0 : 0;
+          uint8_t* box = ugw + b * kPUgBufBytes;
+          uint8_t* su = box + lane * (kPUgCols * 2);
+          uint8_t* sg = su + kPUgBoxBytes;
+          const int sw = (lane >> 1) & 3;  // 64-byte swizzle of this row's 16-byte granules
+          uint32_t m2 = 0;                 // packed 2 x 16-bit max of |dU|, |dG|
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 uq = *reinterpret_cast<const uint4*>(su + ((q ^ sw) << 4));
-              const uint4 gq = *reinterpret_cast<const uint4*>(sg + ((q ^ sw) << 4));
-              const uint32_t cu[4] = {uq.x, uq.y, uq.z, uq.w};
-              const uint32_t cg[4] = {gq.x, gq.y, gq.z, gq.w};
+          for (int q = 0; q < 4; ++q) {
+            uint4* pu = reinterpret_cast<uint4*>(su + ((q ^ sw) << 4));
+            uint4* pg = reinterpret_cast<uint4*>(sg + ((q ^ sw) << 4));
+            const uint4 uq = *pu, gq = *pg;
+            const uint32_t cu[4] = {uq.x, uq.y, uq.z, uq.w};
+            const uint32_t cg[4] = {gq.x, gq.y, gq.z, gq.w};
+            uint32_t du[4], dg[4];
 #pragma unroll
-              for (int w = 0; w < 4; ++w) {
-                const int jj = q * 4 + w;  // output word: columns 2jj, 2jj + 1
-                const uint32_t dhw =
-                    pack_bf16x2(__uint_as_float(r[2 * jj]) * alpha, __uint_as_float(r[2 * jj + 1]) * alpha);
-                const float dh0 = lo_f(dhw), dh1 = hi_f(dhw);
-                const float u0 = lo_f(cu[w]), u1 = hi_f(cu[w]);
-                const float g0 = lo_f(cg[w]), g1 = hi_f(cg[w]);
-                const float s0 = sigmoidf_(g0), s1 = sigmoidf_(g1);
-                odu[jj] = pack_bf16x2(dh0 * (g0 * s0), dh1 * (g1 * s1));
-                odg[jj] = pack_bf16x2((dh0 * u0) * (s0 * (1.0f + g0 * (1.0f - s0))),
-                                      (dh1 * u1) * (s1 * (1.0f + g1 * (1.0f - s1))));
-                const uint32_t keep = (2 * jj + 1 < valid) ? 0x7FFF7FFFu : (2 * jj < valid ? 0x00007FFFu : 0u);
-                m2 = __vmaxu2(m2, __vmaxu2(odu[jj] & keep, odg[jj] & keep));
-              }
+            for (int w = 0; w < 4; ++w) {
+              const int jj = q * 4 + w;  // output word: columns 2jj, 2jj + 1
+              const uint32_t dhw =
+                  pack_bf16x2(__uint_as_float(r[2 * jj]) * alpha, __uint_as_float(r[2 * jj + 1]) * alpha);
+              const float dh0 = lo_f(dhw), dh1 = hi_f(dhw);
+              const float u0 = lo_f(cu[w]), u1 = hi_f(cu[w]);
+              const float g0 = lo_f(cg[w]), g1 = hi_f(cg[w]);
+              const float s0 = sigmoidf_(g0), s1 = sigmoidf_(g1);
+              du[w] = pack_bf16x2(dh0 * (g0 * s0), dh1 * (g1 * s1));
+              dg[w] = pack_bf16x2((dh0 * u0) * (s0 * (1.0f + g0 * (1.0f - s0))),
+                                  (dh1 * u1) * (s1 * (1.0f + g1 * (1.0f - s1))));
+              const uint32_t keep = (2 * jj + 1 < valid) ? 0x7FFF7FFFu : (2 * jj < valid ? 0x00007FFFu : 0u);
+              m2 = __vmaxu2(m2, __vmaxu2(du[w] & keep, dg[w] & keep));
             }
-            amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
-            __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd + col0;
-            store_bf16x32_packed_h(pd, odu, valid, vec, stream);
-            store_bf16x32_packed_h(pd + args.d_bstride, odg, valid, vec, stream);
+            // dU, dG overwrite the U, G granules they came from (same lane, same row).
+            *pu = make_uint4(du[0], du[1], du[2], du[3]);
+            *pg = make_uint4(dg[0], dg[1], dg[2], dg[3]);
           }
-          __syncwarp();  // every lane has read buffer b: it may be refilled
+          amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
+          fence_proxy_async_smem();  // this lane's shared-memory writes -> the TMA store
+          __syncwarp();
           if (lane == 0) {
-            fence_proxy_async_smem();
+            // Rows >= M and columns >= N of the box lie outside the tensor map: not stored.
+            const int y = mb * 2 * kBM + static_cast<int>(rank) * kBM + quad * 32;
+            if (col0 < args.N && y < args.M) {
+              tma_store_3d(&tmD, box, col0, y, 0);
+              tma_store_3d(&tmD, box + kPUgBoxBytes, col0, y, 1);
+              bulk_commit();
+              bulk_wait_read_all();  // the stores have read the box: it may be refilled
+            }
             if (ug_issued == j + 2 && ug_issue(j + 2)) ug_issued = j + 3;
           }
+          __syncwarp();
         }
         if (!ug_ok) break;
       } else if (kStaged) {
@@ -1019,6 +1040,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     if (kUgStaged && lane == 0) {
       volatile int never = 0;
       for (int j = ug_used; j < ug_issued; ++j) mbar_wait(&ugbar[j & 1], (j >> 1) & 1, &never);
+      bulk_wait_all();  // dU / dG stores complete before the CTA exits
     }
     // Peer stores must be complete and visible system-wide before the finish kernel's flag write.
     if (kStaged) bulk_wait_all();
@@ -1109,6 +1131,24 @@ int encode_ug(CUtensorMap* map, const ufp8_gemm_desc& d) {
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(UFP8_ERR_INVALID, "cuTensorMapEncodeTiled failed for U/G (CUresult %d)", static_cast<int>(r));
+  return UFP8_OK;
+}
+
+// 3-D map over a bf16 [2][rows][cols] tensor in 32 x 32 boxes with 64-byte swizzle (the layout
+// of the U/G staging boxes), for TMA stores of dU / dG.
+int encode_bf16_boxes(CUtensorMap* map, void* base, int64_t cols, int64_t rows, int64_t ld, int64_t bstride,
+                      const char* name) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return set_error(UFP8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(bstride) * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(UFP8_ERR_INVALID, "cuTensorMapEncodeTiled failed for %s (CUresult %d)", name, static_cast<int>(r));
   return UFP8_OK;
 }
 
@@ -1294,10 +1334,13 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (rs) var = kVarRsStaged;
     if (d.epilogue == UFP8_EPI_DSWIGLU) var = kVarUgStaged;
   }
-  CUtensorMap tmUG;
+  CUtensorMap tmUG, tmD;
   std::memset(&tmUG, 0, sizeof(tmUG));
+  std::memset(&tmD, 0, sizeof(tmD));
   if (var == kVarUgStaged) {
     rc = encode_ug(&tmUG, d);
+    if (rc) return rc;
+    rc = encode_bf16_boxes(&tmD, d.d, d.N, d.M, d.ldd, d.d_batch_stride, "D");
     if (rc) return rc;
   }
   const void* pair_fn = var == kVarRsStaged   ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>)
@@ -1329,11 +1372,11 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (num_tiles < clusters) clusters = num_tiles;
     const int grid = static_cast<int>(2 * clusters);
     if (var == kVarRsStaged)
-      gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
+      gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
     else if (var == kVarUgStaged)
-      gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
+      gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
     else
-      gemm_fp8_pair_kernel<kPStages, kVarDirect><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, a);
+      gemm_fp8_pair_kernel<kPStages, kVarDirect><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
   } else {
     if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
     gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);
