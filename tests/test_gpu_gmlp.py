@@ -2,7 +2,6 @@
 import numpy as np
 import pytest
 
-from oracle import fp8 as ofp8
 from oracle import path as op
 
 from helpers import bf16_bits_to_f64, bits_to_torch_bf16, compare, torch_bf16_to_bits, torch_fp8_to_codes
