@@ -173,3 +173,11 @@ def test_promote_fp8():
     assert [t.dtype for t in promote_fp8(a, a)] == [torch.float8_e4m3fn] * 2
     assert torch.float8_e5m2 in LOW_PRECISION
     assert torch.allclose(swish(torch.tensor([0.0, 1.0])), torch.tensor([0.0, 1 / (1 + math.exp(-1))]))
+
+
+def test_graphed_step_needs_cuda_inputs():
+    from macrogpt_jax_b200.graphs import GraphedStep
+    with pytest.raises(ValueError, match="CUDA"):
+        GraphedStep(lambda t: t, torch.zeros(2))
+    with pytest.raises(ValueError, match="CUDA"):
+        GraphedStep(lambda: None)
