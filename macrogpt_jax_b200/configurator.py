@@ -2,14 +2,19 @@
 layers a module builds (ueaj/utils/configurator.py:69-161).  It is how the FP8 Einsum is
 plugged in, e.g. ``GMLP.override(fused_proj=Einsum, down_proj=Einsum)``.
 
-Behaviour kept from the reference:
+Behaviour kept from the reference (pinned by tests/test_reference_golden.py against the
+reference's own configurator):
   * ``@config`` on a class or function adds ``.override(**kw)``, which returns a new
-    configurable factory; ``.override`` chains, later keys winning;
-  * an override replaces the argument whatever the caller passes at call time;
-  * ``override(**kw)`` as a value overrides the arguments of the current value of that
-    parameter (``.override`` when it has one, ``functools.partial`` otherwise);
-  * an unknown key raises TypeError unless the target takes ``**kwargs``, where it is
-    forwarded through them.
+    configurable factory function; ``.override`` chains, later keys winning;
+  * functions: an override replaces the argument whatever the caller passes at call time;
+    ``override(**kw)`` as a value overrides the arguments of the current value of that
+    parameter (``.override`` when it has one, ``functools.partial`` otherwise); an unknown key
+    raises TypeError unless the function takes ``**kwargs``, where it is forwarded through them;
+  * classes: the factory is ``lambda *args, **kwargs: Class(*args, **kwargs)``, so every
+    override is forwarded as a constructor keyword (winning over a call-site keyword of the
+    same name; a positional argument for the same parameter is an error of the constructor
+    call), nothing is validated before construction, and a nested ``override(**kw)`` value is
+    forwarded as it is.
 """
 from __future__ import annotations
 
@@ -84,15 +89,12 @@ def _make_overridden(target: Callable, sig: inspect.Signature, name: str, overri
 def config(obj):
     """Adds ``.override(**kw)`` to a class or function (see module docstring)."""
     if inspect.isclass(obj):
-        sig = inspect.signature(obj.__init__)
-        params = list(sig.parameters.values())[1:]  # drop self
-        sig = sig.replace(parameters=params)
-
         def construct(*args, **kwargs):
             return obj(*args, **kwargs)
 
+        sig = inspect.signature(construct)  # (*args, **kwargs): every override is a keyword
+
         def cls_override(**kw):
-            _check_keys(obj.__name__, sig, kw)
             return _make_overridden(construct, sig, obj.__name__, kw)
 
         obj.override = staticmethod(cls_override)

@@ -39,11 +39,29 @@ def test_override_validates_keys():
         _make.override(zz=1)
 
 
-def test_class_override_forwards_extra_kwargs_and_nests():
-    t = _Thing.override(x=4, extra=1)(0)
+class _Plain:
+    def __init__(self, x, y=1):
+        self.x, self.y = x, y
+
+
+_Plain = config(_Plain)
+
+
+def test_class_override_forwards_keywords():
+    """Class overrides are constructor keywords (ueaj/utils/configurator.py:152-160)."""
+    t = _Thing.override(x=4, extra=1)()
     assert isinstance(t, _Thing) and t.x == 4 and t.kw == {"extra": 1}
-    t2 = _Thing.override(inner=override(b=11))(1)
+    assert _Thing.override(extra=2)(0, extra=3).kw == {"extra": 2}  # the override wins
+    with pytest.raises(TypeError):
+        _Thing.override(x=4)(0)  # x given twice: positionally and by the override
+    t2 = _Thing.override(inner=_make.override(b=11))(1)
     assert t2.inner(0) == (0, 11, 3)
+    marker = override(b=11)
+    assert _Thing.override(inner=marker)(1).inner == marker  # forwarded as it is
+    factory = _Plain.override(zz=1)  # not validated until the constructor runs
+    with pytest.raises(TypeError):
+        factory(0)
+    assert _Plain.override(y=5).override(y=6)(0).y == 6
 
 
 # ----------------------------------------------------------------------------- Einsum
