@@ -7,8 +7,9 @@ package imports JAX at the top of ueaj/utils/__init__.py and ueaj/model/einsum.p
 installed here, so this script loads only pure-Python code from it, unchanged:
 ueaj/utils/configurator.py as a standalone module, and the EinsumMetadata dataclass plus the
 parse_einsum_expr / compute_weight_metadata functions of ueaj/model/einsum.py (their source,
-extracted with ast and executed with the standard-library names they use).  Writes
-reference_behaviour.json next to this script; the reference is not read at test time.
+extracted with ast and executed with the standard-library names they use); and the
+constructor signatures of Einsum, GMLP, MLP and SoftmaxAttention (parsed, not executed).
+Writes reference_behaviour.json next to this script; the reference is not read at test time.
 """
 from __future__ import annotations
 
@@ -47,12 +48,30 @@ def load_einsum_metadata(root: Path):
     return ns["parse_einsum_expr"], ns["compute_weight_metadata"]
 
 
+def constructor_signatures(root: Path) -> dict:
+    """Positional parameters with their default expressions (source text) and keyword-only
+    parameters of the layer constructors on the path, read from the reference's source."""
+    out = {}
+    for rel, cls in (("ueaj/model/einsum.py", "Einsum"), ("ueaj/model/mlp.py", "GMLP"), ("ueaj/model/mlp.py", "MLP"),
+                     ("ueaj/model/soft_attn.py", "SoftmaxAttention")):
+        tree = ast.parse((root / rel).read_text())
+        init = next(f for n in tree.body if isinstance(n, ast.ClassDef) and n.name == cls
+                    for f in n.body if isinstance(f, ast.FunctionDef) and f.name == "__init__")
+        a = init.args
+        pos = [x.arg for x in a.args][1:]
+        defaults = [None] * (len(pos) - len(a.defaults)) + [ast.unparse(d) for d in a.defaults]
+        out[cls] = {"positional": [[n, d] for n, d in zip(pos, defaults)],
+                    "keyword_only": [x.arg for x in a.kwonlyargs]}
+    return out
+
+
 def main() -> None:
     root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
     cfg = load_configurator(root)
     parse, meta = load_einsum_metadata(root)
     out = {"configurator": sc.configurator_results(cfg.config, cfg.override),
-           "einsum": sc.metadata_results(parse, meta)}
+           "einsum": sc.metadata_results(parse, meta),
+           "constructors": constructor_signatures(root)}
     (HERE / "reference_behaviour.json").write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
     print("wrote", HERE / "reference_behaviour.json")
 

@@ -38,3 +38,33 @@ def test_einsum_metadata_matches_reference():
     assert len(ours["metadata"]) == len(ref["metadata"])
     for case, got, want in zip(sc.METADATA_CASES, ours["metadata"], ref["metadata"]):
         assert got == want, case
+
+
+def test_layer_constructors_match_reference_signatures():
+    """Same positional parameters in the same order with the same defaults (a JAX default
+    maps to its PyTorch counterpart), and the reference's keyword-only parameters first;
+    additions are keyword-only and come after them."""
+    import inspect
+
+    import torch
+
+    from macrogpt_jax_b200.einsum import Einsum, lecun_normal_init
+    from macrogpt_jax_b200.mlp import GMLP, MLP, swish
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+
+    same_as = {"jnp.bfloat16": torch.bfloat16, "nnx.swish": swish, "Einsum": Einsum,
+               "lecun_normal_init": lecun_normal_init, "None": None, "''": "", "64": 64, "1": 1,
+               "10000.0": 10000.0, "'sp'": "sp"}
+    ref = _reference()["constructors"]
+    for cls in (Einsum, GMLP, MLP, SoftmaxAttention):
+        want = ref[cls.__name__]
+        params = list(inspect.signature(cls.__init__).parameters.values())[1:]
+        pos = [p for p in params if p.kind is inspect.Parameter.POSITIONAL_OR_KEYWORD]
+        kwo = [p.name for p in params if p.kind is inspect.Parameter.KEYWORD_ONLY]
+        assert [p.name for p in pos] == [n for n, _ in want["positional"]], cls.__name__
+        for p, (name, default) in zip(pos, want["positional"]):
+            if default is None:
+                assert p.default is inspect.Parameter.empty, (cls.__name__, name)
+            else:
+                assert p.default == same_as[default], (cls.__name__, name)
+        assert kwo[:len(want["keyword_only"])] == want["keyword_only"], cls.__name__
