@@ -120,8 +120,10 @@ def cpu_oracle_step(d, h, T, seed=0):
     quantisation (and dequantisation) of the weights, both contractions forward, the four
     backward, gating and the activation/gradient quantisations."""
     import numpy as np
+    from oracle import fp8 as ofp8
     from oracle import path as op
     op.FAST_CAST = True
+    ofp8.THREADED = True
     rng = np.random.default_rng(seed)
     wf = op.bf16_normal(rng, (2, d, h), d ** -0.5)
     wd = op.bf16_normal(rng, (h, d), h ** -0.5)
@@ -133,28 +135,29 @@ def cpu_oracle_step(d, h, T, seed=0):
     return time.perf_counter() - t0
 
 
-def extrapolate(samples, T_full, h_scale):
-    """Least-squares fit t(T) = a + b T over (T, seconds) samples taken at a hidden slice,
-    evaluated at T_full and scaled by h_scale = hidden / slice (every cost of the block, the
-    weights included, is linear in the hidden width)."""
+def fit_hidden(samples, h_full):
+    """Least-squares fit t(h) = a + b h over (hidden slice, seconds) samples taken at the full
+    token count and d_model, evaluated at h_full.  The activation-side work (x and dY
+    quantisation, dx rounding) is the intercept a; every weight-side cost is linear in the
+    hidden width.  Returns (seconds at h_full, a, b)."""
     import numpy as np
-    Ts = np.array([s[0] for s in samples], dtype=np.float64)
+    hs = np.array([s[0] for s in samples], dtype=np.float64)
     ts = np.array([s[1] for s in samples], dtype=np.float64)
-    b, a = np.polyfit(Ts, ts, 1) if len(set(Ts)) > 1 else (ts.mean() / Ts.mean(), 0.0)
-    return float((max(a, 0.0) + max(b, 0.0) * T_full) * h_scale)
+    if len(set(hs.tolist())) > 1:
+        b, a = np.polyfit(hs, ts, 1)
+    else:
+        a, b = 0.0, ts.mean() / hs.mean()
+    a, b = max(float(a), 0.0), max(float(b), 0.0)
+    return a + b * h_full, a, b
 
 
-def cpu_plan(T, h, ref_tokens, ref_hidden):
-    T_lo = max(16, min(T, ref_tokens))
-    T_hi = min(T, 3 * T_lo)
-    h_s = max(128, min(h, ref_hidden))
-    return T_lo, T_hi, h_s
+CPU_SLICES = (128, 768)  # hidden widths the CPU port executes (alternating), full tokens and d_model
 
 
-def cpu_sample_desc(T_lo, T_hi, h_s, T_full, h):
-    return (f"oracle GMLP fwd+bwd steps of {T_lo} and {T_hi} tokens at d_model full and hidden {h_s} of {h} "
-            f"(weights quantised each step), fitted as a + b*T, evaluated at {T_full} tokens and scaled by "
-            f"{h}/{h_s} (all costs are linear in hidden); numpy fp32 BLAS matmuls on all host threads, "
+def cpu_sample_desc(T, d, h, n_steps):
+    return (f"{n_steps} oracle GMLP fwd+bwd steps at the full {T} tokens and d_model {d} on hidden slices "
+            f"{CPU_SLICES[0]} and {CPU_SLICES[1]} (alternating) of {h}, weights quantised each step; fitted as "
+            f"t(h) = a + b*h and evaluated at hidden {h}; numpy fp32 BLAS contractions on all host threads, "
             "ml_dtypes casts, single-threaded elementwise")
 
 
@@ -165,32 +168,57 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def gpu_arm_config(args, cfg, world):
+    """The `config` dict both arms print for this workload and GPU count."""
+    d, h, T = cfg["d"], cfg["h"], cfg["B"] * cfg["S"]
+    if world > 1:
+        parallelism = (f"tp{world} (all-gather + reduce-scatter: NVLink P2P fused with the GEMMs, all-gather by "
+                       f"{'SM push kernel' if args.tp_ag == 'sm' else 'copy engines'})" if args.tp_rs == "p2p"
+                       else f"tp{world} (NCCL all-gather / reduce-scatter / all-reduce)")
+    else:
+        parallelism = "tp1"
+    return {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h, "parallelism": parallelism,
+            "l2": ("inputs larger than L2" if T * (6 * h + 3 * d) * 2 > 2 * 126e6 else
+                   "working set below 2x L2: no flush between steps (secondary workload)")}
+
+
 # ----------------------------------------------------------------------------- arms
 def run_reference(args, cfg, rank, world):
+    """The CPU port of the path (oracle/), rank 0 only.  Every step runs the full token count
+    on a hidden slice; the printed ms_per_step is the measured time of those executed steps,
+    and `value` is the full-config throughput from the fit t(h) = a + b h (fields `executed`
+    and `extrapolation` give both)."""
     if rank != 0:
         return None
     d, h, T = cfg["d"], cfg["h"], cfg["B"] * cfg["S"]
-    T_lo, T_hi, h_s = cpu_plan(T, h, args.ref_tokens, args.ref_hidden)
     samples = []
     for i in range(args.warmup + args.steps):
-        Ti = T_lo if i % 2 == 0 else T_hi
-        t = cpu_oracle_step(d, h_s, Ti, seed=i)
+        hs = CPU_SLICES[i % 2]
+        t = cpu_oracle_step(d, hs, T, seed=i)
         if i >= args.warmup:
-            samples.append((Ti, t))
-    step_s = extrapolate(samples, T, h / h_s)
-    step_times = [step_s] * args.steps
-    sample = cpu_sample_desc(T_lo, T_hi, h_s, T, h)
-    total = sum(step_times)
-    value = T * args.steps / total
+            samples.append((hs, t))
+    full_s, a, b = fit_hidden(samples, h)
+    exec_ms = 1000.0 * sum(s[1] for s in samples) / len(samples)
+    value = T / full_s
+    by_h = {str(hs): 1000.0 * sum(s[1] for s in samples if s[0] == hs) / max(1, sum(1 for s in samples if s[0] == hs))
+            for hs in CPU_SLICES}
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": exec_ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8",
         "data": "synthetic (seeded)",
-        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h},
-        "tflops_per_gpu": flops_per_step(T, d, h) * value / T / 1e12,
+        "config": gpu_arm_config(args, cfg, world),
+        "tflops_per_gpu": flops_per_step(T, d, h) / full_s / 1e12,
+        "executed": {"steps": args.steps, "warmup_steps": args.warmup, "tokens": T, "d_model": d,
+                     "hidden_slices": list(CPU_SLICES), "ms_per_step": exec_ms, "ms_per_step_by_hidden": by_h,
+                     "note": "ms_per_step is the mean measured time of these executed steps"},
+        "extrapolation": {"model": "t(h) = a + b*h, least squares over the executed steps",
+                          "a_ms": 1000.0 * a, "b_ms_per_hidden": 1000.0 * b, "to_hidden": h,
+                          "est_ms_per_step_full": 1000.0 * full_s, "factor": 1000.0 * full_s / exec_ms,
+                          "note": "value (tokens/s) = tokens / est_ms_per_step_full: an estimate for the full "
+                                  "config, not a measurement of it"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": sample},
+                         "sample": cpu_sample_desc(T, d, h, args.steps)},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return out
@@ -217,15 +245,11 @@ def run_ours(args, cfg, rank, world, local_rank):
         mlp = TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
                      fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5),
                      fused_reduce_scatter=args.tp_rs == "p2p")
-        parallelism = (f"tp{world} (all-gather + reduce-scatter: NVLink P2P fused with the GEMMs, all-gather by "
-                       f"{'SM push kernel' if args.tp_ag == 'sm' else 'copy engines'})" if args.tp_rs == "p2p"
-                       else f"tp{world} (NCCL all-gather / reduce-scatter / all-reduce)")
     else:
         mlp = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(d ** -0.5)),
                             down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
             model_d=d, hidden_d=h, rngs=Rngs(0))
         assert mlp.fused()
-        parallelism = "tp1"
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)  # identical activations on every rank (TP replicates x and dY)
     x_full = torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
@@ -350,10 +374,7 @@ def run_ours(args, cfg, rank, world, local_rank):
         "metric": METRIC, "value": tokens_s, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
-        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h,
-                   "parallelism": parallelism,
-                   "l2": ("inputs larger than L2" if T * (6 * h + 3 * d) * 2 > 2 * 126e6 else
-                          "working set below 2x L2: no flush between steps (secondary workload)")},
+        "config": gpu_arm_config(args, cfg, world),
         "tflops_per_gpu": tflops_gpu,
         "frac_of_fp8_peak": {"nominal_4500": tflops_gpu / FP8_NOMINAL_TFLOPS,
                              "measured_2x_bf16_sustained": tflops_gpu / peak_fp8},
@@ -382,11 +403,11 @@ def run_ours(args, cfg, rank, world, local_rank):
     if e2e:
         out["e2e"] = e2e
     if world == 1 and not args.no_cpu_baseline:
-        T_lo, T_hi, h_s = cpu_plan(T, h, args.ref_tokens, args.ref_hidden)
-        samples = [(Ti, cpu_oracle_step(d, h_s, Ti, seed=k)) for k, Ti in enumerate((T_lo, T_hi, T_lo, T_hi))]
-        step_s = extrapolate(samples, T, h / h_s)
+        samples = [(hs, cpu_oracle_step(d, hs, T, seed=k)) for k, hs in enumerate(CPU_SLICES)]
+        step_s, a, b = fit_hidden(samples, h)
         out["cpu_baseline"] = {"value": T / step_s, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
-                               "sample": cpu_sample_desc(T_lo, T_hi, h_s, T, h), "est_ms_per_step": step_s * 1000.0,
+                               "sample": cpu_sample_desc(T, d, h, len(samples)), "est_ms_per_step": step_s * 1000.0,
+                               "executed_ms": {str(hs): 1000.0 * s for hs, s in samples},
                                "tflops": flops_per_step(T, d, h) / step_s / 1e12}
     return out
 
@@ -496,8 +517,6 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gmlp_d4096")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ref-tokens", type=int, default=256)
-    ap.add_argument("--ref-hidden", type=int, default=1792)
     ap.add_argument("--gemm-traffic", type=float, default=None,
                     help="DRAM bytes per GEMM launch to report as roofline.traffic (default: the "
                          "captured figure for gmlp_d4096 on one GPU, else null)")

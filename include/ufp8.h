@@ -100,8 +100,9 @@ int ufp8_amax_quant(const void* x_bf16, int64_t n, int fmt, void* q, float* amax
  * may not allocate device memory nor hold a spare device word, e.g. an XLA FFI handler whose
  * buffers all come from XLA.  This entry point has no counterpart in the reference (XLA's cast
  * needs no scratch).  Overlapping calls on one device race on the shared scratch: calls must be
- * ordered (one stream, or synchronised).  The first call on a device looks up the scratch
- * address (cudaGetSymbolAddress, with that device current); make it outside any stream capture. */
+ * ordered (one stream, or synchronised).  The first call in a device's CUDA context looks up the
+ * scratch address (cudaGetSymbolAddress, with that device current; again after the context
+ * changes, e.g. after cudaDeviceReset); make that first call outside any stream capture. */
 int ufp8_amax_quant_noalloc(const void* x_bf16, int64_t n, int fmt, void* q, float* inv_scale,
                             ufp8_stream_t stream);
 
@@ -230,16 +231,19 @@ int ufp8_device_status(int* status, int clear);
 /* Number of CTAs the persistent GEMM launches (0 = one per SM, the default). */
 int ufp8_set_gemm_ctas(int ctas);
 
-/* GEMM kernel variant for this process: UFP8_GEMM_AUTO (default: the CTA-pair kernel),
+/* GEMM kernel variant for this process: UFP8_GEMM_AUTO (default: the CTA-pair kernel, with
+ * the ring stages of UFP8_GEMM_CTA_PAIR_WIDE for the epilogues that store directly),
  * UFP8_GEMM_SINGLE_CTA (128 x 256 tiles, one CTA each), UFP8_GEMM_CTA_PAIR (256 x 256
- * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2; RS_PUSH rows leave through
- * shared memory as bulk async stores and DSWIGLU reads the saved U / G through TMA) or
- * UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with plain 16-byte loads and stores in every
- * epilogue). */
+ * tiles on a cluster of two CTAs with tcgen05.mma.cta_group::2, ring stages of one 128-byte K
+ * chunk, 7 deep; RS_PUSH rows leave through shared memory as bulk async stores and DSWIGLU
+ * reads the saved U / G through TMA), UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with plain
+ * 16-byte loads and stores in every epilogue) or UFP8_GEMM_CTA_PAIR_WIDE (UFP8_GEMM_CTA_PAIR
+ * with ring stages of two 128-byte K chunks, 3 deep, for the epilogues that store directly). */
 #define UFP8_GEMM_AUTO 0
 #define UFP8_GEMM_SINGLE_CTA 1
 #define UFP8_GEMM_CTA_PAIR 2
 #define UFP8_GEMM_CTA_PAIR_DIRECT 3
+#define UFP8_GEMM_CTA_PAIR_WIDE 4
 int ufp8_set_gemm_variant(int variant);
 
 /* Tile raster of the persistent GEMM: how many M tiles form a group that is swept along N

@@ -460,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // at link rate), and the warp moves on as soon as the row has been read out of shared memory.
 constexpr int kPStages = 7;
 constexpr int kPStagesStaged = 5;
+constexpr int kPStagesWide = 3;                   // ring depth with two 128-byte K chunks per stage
 constexpr int kPHalfBytes = 128 * kBK;            // 16 KiB: 128 rows x 128 B
-constexpr int kPStageBytes = 2 * kPHalfBytes;     // A half + B half
+constexpr int kPStageBytes = 2 * kPHalfBytes;     // A half + B half (one 128-byte K chunk)
 constexpr int kPEpiWarps = 8;
 constexpr int kPThreads = 64 + 32 * kPEpiWarps;   // 320
 constexpr int kPStgCols = 64;                     // columns per staged row segment
@@ -488,15 +489,17 @@ constexpr int kPUgBytes = kPEpiWarps * kPUgWarpBytes + 256;  // + the warps' mba
 __host__ __device__ constexpr int pair_extra_bytes(int var) {
   return var == kVarRsStaged ? kPStgBytes : (var == kVarUgStaged ? kPUgBytes : 0);
 }
-__host__ __device__ constexpr int pair_smem_bytes(int stages, int var) {
-  return stages * kPStageBytes + pair_extra_bytes(var) + kBarrierBytes + 1024;
+__host__ __device__ constexpr int pair_smem_bytes(int stages, int var, int kch = 1) {
+  return stages * kch * kPStageBytes + pair_extra_bytes(var) + kBarrierBytes + 1024;
 }
 constexpr int kPSmemBytes = pair_smem_bytes(kPStages, kVarDirect);
+constexpr int kPSmemBytesWide = pair_smem_bytes(kPStagesWide, kVarDirect, 2);
 constexpr int kPSmemBytesStaged = pair_smem_bytes(kPStagesStaged, kVarRsStaged);
 constexpr int kPSmemBytesUg = pair_smem_bytes(kPStagesStaged, kVarUgStaged);
 static_assert(kPSmemBytesStaged <= 232448, "staged CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytesUg <= 232448, "U/G-staged CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytes <= 232448, "CTA-pair kernel exceeds shared memory");
+static_assert(kPSmemBytesWide <= 232448, "wide-stage CTA-pair kernel exceeds shared memory");
 
 // Stores 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]).
 __device__ __forceinline__ void store_bf16x32_packed(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
@@ -576,7 +579,10 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 }
 
 
-template <int NSTAGES, int kVar>
+// KCH = 128-byte K chunks per ring stage (1 or 2): a stage holds KCH A sub-tiles followed by KCH
+// B sub-tiles of 16 KiB each, and the MMA thread issues 4 * KCH MMAs per stage, so the per-stage
+// barrier hand-offs (full -> MMA issue -> commit -> empty -> next load) occur half as often.
+template <int NSTAGES, int kVar, int KCH = 1>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmUG, const __grid_constant__ CUtensorMap tmD,
@@ -585,7 +591,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   constexpr bool kUgStaged = kVar == kVarUgStaged;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging = smem + NSTAGES * kPStageBytes;  // staged variants only
+  constexpr int kStageBytes = KCH * kPStageBytes;
+  uint8_t* staging = smem + NSTAGES * kStageBytes;  // staged variants only
   uint64_t* ugbar_all = reinterpret_cast<uint64_t*>(staging + kPEpiWarps * kPUgWarpBytes);  // kUgStaged only
   uint64_t* full = reinterpret_cast<uint64_t*>(staging + pair_extra_bytes(kVar));
   uint64_t* empty = full + NSTAGES;
@@ -657,20 +664,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (int ks = 0; ks < total_k; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
           const int kb = ks / args.ksteps;
-          const int k0 = (ks - kb * args.ksteps) * kBK;
-          uint8_t* sa = smem + stage * kPStageBytes;
-          uint8_t* sb = sa + kPHalfBytes;
+          const int k0 = (ks - kb * args.ksteps) * (KCH * kBK);
+          uint8_t* sa = smem + stage * kStageBytes;
+          uint8_t* sb = sa + KCH * kPHalfBytes;
           if (leader) {
-            mbar_arrive_expect_tx(&full[stage], 2 * kPStageBytes);
+            mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
             armed |= 1u << stage;
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
           const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
-          if (args.a_major == UFP8_K_MAJOR)
-            tma_load_3d_pair(sa, &tmA, bar, k0, row0, az);
-          else
-            tma_load_3d_pair(sa, &tmA, bar, row0, k0, az);
           int n0, bz;
           if (swiglu) {
             n0 = nb * 128;
@@ -679,10 +682,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             n0 = nb * kBN + static_cast<int>(rank) * 128;
             bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
           }
-          if (args.b_major == UFP8_K_MAJOR)
-            tma_load_3d_pair(sb, &tmB, bar, k0, n0, bz);
-          else
-            tma_load_3d_pair(sb, &tmB, bar, n0, k0, bz);
+#pragma unroll
+          for (int j = 0; j < KCH; ++j) {
+            // K chunks past K (or past this slice's K for k_batches) read as zeros.
+            const int kj = k0 + j * kBK;
+            if (args.a_major == UFP8_K_MAJOR)
+              tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, kj, row0, az);
+            else
+              tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, row0, kj, az);
+            if (args.b_major == UFP8_K_MAJOR)
+              tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, kj, n0, bz);
+            else
+              tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, n0, kj, bz);
+          }
           if (++stage == NSTAGES) {
             stage = 0;
             phase ^= 1u;
@@ -717,15 +729,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * kPStageBytes);
-          const uint32_t sb = sa + kPHalfBytes;
+          const uint32_t sa0 = smem_u32(smem + stage * kStageBytes);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk) {
-            const uint64_t adesc = args.a_major == UFP8_K_MAJOR ? make_sdesc_sw128(sa + kk * 32, 16, 1024)
-                                                                : make_sdesc_sw128(sa + kk * 32 * 128, kPHalfBytes, 1024);
-            const uint64_t bdesc = args.b_major == UFP8_K_MAJOR ? make_sdesc_sw128(sb + kk * 32, 16, 1024)
-                                                                : make_sdesc_sw128(sb + kk * 32 * 128, kPHalfBytes, 1024);
-            umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | kk) != 0 ? 1u : 0u);
+          for (int j = 0; j < KCH; ++j) {
+            const uint32_t sa = sa0 + j * kPHalfBytes;
+            const uint32_t sb = sa0 + (KCH + j) * kPHalfBytes;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 32; ++kk) {
+              const uint64_t adesc = args.a_major == UFP8_K_MAJOR ? make_sdesc_sw128(sa + kk * 32, 16, 1024)
+                                                                  : make_sdesc_sw128(sa + kk * 32 * 128, kPHalfBytes, 1024);
+              const uint64_t bdesc = args.b_major == UFP8_K_MAJOR ? make_sdesc_sw128(sb + kk * 32, 16, 1024)
+                                                                  : make_sdesc_sw128(sb + kk * 32 * 128, kPHalfBytes, 1024);
+              umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | j | kk) != 0 ? 1u : 0u);
+            }
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == NSTAGES) {
@@ -1322,6 +1338,9 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesUg);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWide);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
@@ -1334,6 +1353,14 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (rs) var = kVarRsStaged;
     if (d.epilogue == UFP8_EPI_DSWIGLU) var = kVarUgStaged;
   }
+  // Direct epilogues on the pair kernel (the default, UFP8_GEMM_AUTO, and UFP8_GEMM_CTA_PAIR_WIDE):
+  // ring stages of two 128-byte K chunks, 3 deep.  Half as many full/empty hand-offs per FLOP as
+  // the 7-deep ring of single chunks (UFP8_GEMM_CTA_PAIR), which measured 8-9 % slower on the
+  // long-K GMLP contractions (F2 754 vs 694 us, B4 1484 vs 1355 us at 16384 x 4096 x 14336 / 28672).
+  const bool wide = pair && var == kVarDirect &&
+                    (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE);
+  const int kch = wide ? 2 : 1;
+  a.ksteps = static_cast<int>((d.K + kch * kBK - 1) / (kch * kBK));
   CUtensorMap tmUG, tmD;
   std::memset(&tmUG, 0, sizeof(tmUG));
   std::memset(&tmD, 0, sizeof(tmD));
@@ -1345,14 +1372,18 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   }
   const void* pair_fn = var == kVarRsStaged   ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>)
                         : var == kVarUgStaged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>)
+                        : wide                ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2>)
                                               : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, kVarDirect>);
-  const int pair_smem = var == kVarRsStaged ? kPSmemBytesStaged : (var == kVarUgStaged ? kPSmemBytesUg : kPSmemBytes);
+  const int pair_smem = var == kVarRsStaged ? kPSmemBytesStaged
+                        : var == kVarUgStaged ? kPSmemBytesUg
+                        : wide ? kPSmemBytesWide : kPSmemBytes;
+  const int occ_slot = wide ? 3 : var;
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device[3] = {-1, -1, -1}, occ_clusters[3] = {0, 0, 0};
-    if (occ_device[var] != dev.device) {
+    static thread_local int occ_device[4] = {-1, -1, -1, -1}, occ_clusters[4] = {0, 0, 0, 0};
+    if (occ_device[occ_slot] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
       cfg.blockDim = dim3(kPThreads, 1, 1);
@@ -1361,10 +1392,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
       e = cudaOccupancyMaxActiveClusters(&n, pair_fn, &cfg);
       if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveClusters");
       if (n < 1) return set_error(UFP8_ERR_DEVICE, "no CTA pair of the GEMM kernel fits on this device");
-      occ_clusters[var] = n;
-      occ_device[var] = dev.device;
+      occ_clusters[occ_slot] = n;
+      occ_device[occ_slot] = dev.device;
     }
-    const int max_clusters = occ_clusters[var];
+    const int max_clusters = occ_clusters[occ_slot];
     // Persistent grid: no more clusters than can be resident at once.
     if (ctas_override <= 0 || ctas > 2 * max_clusters) ctas = 2 * max_clusters;
     long long clusters = ctas / 2;
@@ -1375,6 +1406,8 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
       gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
     else if (var == kVarUgStaged)
       gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
+    else if (wide)
+      gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
     else
       gemm_fp8_pair_kernel<kPStages, kVarDirect><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
   } else {

@@ -11,9 +11,11 @@
 // Launches, in stream order: na_partial_kernel (one CTA per block of x) -> na_reduce_kernel
 // (one CTA) -> the library's quantize kernel with amax = &g_na_amax[0] (the launch
 // ufp8_quantize uses).  The result is bit-identical to ufp8_amax_quant.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "internal.h"
 
@@ -81,18 +83,48 @@ __global__ void __launch_bounds__(kNaThreads) na_reduce_kernel(int parts) {
   }
 }
 
-// Device address of g_na_amax, looked up once per device (with that device current).
+// Device address of g_na_amax for the current device.  The lookup (cudaGetSymbolAddress, with
+// the device current) runs on the first call in each CUDA context and again whenever the
+// device's current context changes (after cudaDeviceReset the module is loaded anew and may sit
+// at another address).  A mutex serialises the cache, so first calls from several host threads
+// do not race.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
 int na_amax_address(int device, float** out) {
-  static float* addr[kNaMaxDevices] = {};
+  struct Entry {
+    CUcontext ctx;
+    float* addr;
+  };
+  static Entry cache[kNaMaxDevices] = {};
+  static std::mutex mu;
   if (device < 0 || device >= kNaMaxDevices)
     return set_error(UFP8_ERR_UNSUPPORTED, "ufp8_amax_quant_noalloc: device %d >= %d", device, kNaMaxDevices);
-  if (!addr[device]) {
+  CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+  CUcontext ctx = nullptr;
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS || !ctx)
+    return set_error(UFP8_ERR_CUDA, "ufp8_amax_quant_noalloc: no current CUDA context");
+  std::lock_guard<std::mutex> lock(mu);
+  Entry& e = cache[device];
+  if (!e.addr || e.ctx != ctx) {
     void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_na_amax);
-    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(no-alloc amax scratch)");
-    addr[device] = static_cast<float*>(p);
+    cudaError_t err = cudaGetSymbolAddress(&p, g_na_amax);
+    if (err != cudaSuccess) return cuda_error(err, "cudaGetSymbolAddress(no-alloc amax scratch)");
+    e.addr = static_cast<float*>(p);
+    e.ctx = ctx;
   }
-  *out = addr[device];
+  *out = e.addr;
   return UFP8_OK;
 }
 

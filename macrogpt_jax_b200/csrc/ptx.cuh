@@ -40,14 +40,20 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Suspend-time hint of mbar_try_wait: a waiting thread sleeps until the phase completes or this
+// many nanoseconds pass, instead of returning at once and spinning.  Waiting roles then take no
+// issue slots from the MMA and producer threads (measured: F2 GEMM 758 -> 710 us with 128-byte
+// stages).  The timeout and abort checks of mbar_wait run each time the hint expires.
+constexpr uint32_t kTryWaitHintNs = 1000000u;  // 1 ms
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kTryWaitHintNs)
       : "memory");
   return ok != 0;
 }

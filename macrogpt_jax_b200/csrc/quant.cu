@@ -4,8 +4,8 @@
 // ueaj/utils/gradutils.py:15-54):
 //   amax      = max |x|, taken as an unsigned max over the sign-cleared bf16 bit patterns,
 //               so it is exact and NaN-propagating (a NaN pattern is above +inf);
-//   s         = FMAX / amax in IEEE fp32 (FMAX = 448 for e4m3fn, 57344 for e5m2), s = 1
-//               when amax == 0;
+//   s         = min(FMAX / amax, FLT_MAX) in IEEE fp32 (FMAX = 448 for e4m3fn, 57344 for
+//               e5m2), s = 1 when amax == 0, NaN when amax is NaN;
 //   q         = cast(f32(x) * s) with round-to-nearest-even and the ml_dtypes 0.5.4
 //               overflow rules (e4m3fn: |p| > 464 or inf -> NaN 0x7F|sign;
 //               e5m2: |p| >= 61440 or inf -> inf 0x7C|sign); a NaN product becomes the
@@ -95,8 +95,15 @@ __global__ void __launch_bounds__(kThreads) amax_scalar_kernel(const uint16_t* _
 
 __device__ __forceinline__ float fp8_fmax(int fmt) { return fmt == UFP8_E4M3 ? 448.0f : 57344.0f; }
 
+// s = FMAX / amax, capped at the largest finite f32: for amax below FMAX / FLT_MAX (about
+// 1.3e-36 for e4m3fn, 1.7e-34 for e5m2; still normal bf16 values) the quotient would be +inf,
+// and inf * x would turn every element into a non-finite code (0 * inf into NaN).  With the cap,
+// x * s stays finite and below FMAX, and inv_scale = 1 / FLT_MAX = 2^-128 (an f32 subnormal).
+// NaN amax keeps s = NaN (NaN propagates into every code, as the unscaled cast would).
 __device__ __forceinline__ float scale_from_amax(float amax, int fmt) {
-  return amax == 0.0f ? 1.0f : __fdiv_rn(fp8_fmax(fmt), amax);
+  if (amax == 0.0f) return 1.0f;
+  const float s = __fdiv_rn(fp8_fmax(fmt), amax);
+  return s > 3.402823466e38f ? 3.402823466e38f : s;  // a NaN s fails the compare and stays NaN
 }
 
 // True where the satfinite hardware conversion differs from the non-saturating cast:

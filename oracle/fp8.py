@@ -91,8 +91,45 @@ def f32_to_fp8_fast(x: np.ndarray, fmt: int) -> np.ndarray:
     return codes
 
 
+# ----------------------------------------------------------------------------- threaded passes
+# THREADED = True routes the element-wise passes of the oracle through torch's multi-threaded
+# CPU kernels (exact conversions: bf16 <-> f32, fp8 -> f32, and the RNE f32 -> bf16 rounding),
+# for the CPU baseline, which times the oracle on all host cores.  Tensors holding a NaN take
+# the numpy path, whose NaN handling is the specified one.  tests/test_oracle.py checks both
+# paths give identical bits.
+THREADED = False
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _bf16_bits_to_f32_threaded(bits: np.ndarray) -> np.ndarray:
+    torch = _torch()
+    b = np.ascontiguousarray(bits, dtype=np.uint16)
+    return torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).float().numpy()
+
+
+def _f32_to_bf16_bits_threaded(x: np.ndarray):
+    torch = _torch()
+    t = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32))
+    if bool(torch.isnan(t).any()):
+        return None
+    return t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def fp8_to_f32_threaded(codes: np.ndarray, fmt: int) -> np.ndarray:
+    """float32 values of fp8 codes (exact) through torch's fp8 decode."""
+    torch = _torch()
+    c = torch.from_numpy(np.ascontiguousarray(codes, dtype=np.uint8))
+    return c.view(torch.float8_e4m3fn if fmt == E4M3 else torch.float8_e5m2).float().numpy()
+
+
 # ----------------------------------------------------------------------------- bf16
 def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    if THREADED:
+        return _bf16_bits_to_f32_threaded(bits)
     return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
@@ -101,6 +138,10 @@ def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
 
     For every non-NaN pattern b (at most 0xFF800000), b + 0x7FFF + 1 stays below 2**32,
     so the rounding add is done in uint32."""
+    if THREADED:
+        out = _f32_to_bf16_bits_threaded(x)
+        if out is not None:
+            return out
     x = np.ascontiguousarray(x, dtype=np.float32)
     b = x.view(np.uint32)
     r = (b >> 16) & np.uint32(1)
@@ -128,11 +169,19 @@ def amax_bits(x_bits: np.ndarray) -> np.float32:
     return np.array([m], dtype=np.uint32).view(np.float32)[0]
 
 
+F32_MAX = np.float32(np.finfo(np.float32).max)
+
+
 def scale_from_amax(amax: np.float32, fmt: int) -> np.float32:
+    """s = min(FMAX / amax, FLT_MAX); 1 for amax == 0; NaN for a NaN amax.
+
+    The cap keeps s finite for amax below FMAX / FLT_MAX (still normal bf16 values), where the
+    quotient overflows to inf and would turn every code non-finite (0 * inf = NaN)."""
     with np.errstate(over="ignore", divide="ignore", invalid="ignore"):
         if amax == 0:
             return np.float32(1.0)
-        return np.float32(FMAX[fmt]) / np.float32(amax)
+        s = np.float32(FMAX[fmt]) / np.float32(amax)
+        return s if np.isnan(s) else np.minimum(s, F32_MAX)
 
 
 def quantize_bits(x_bits: np.ndarray, fmt: int, amax: np.float32 | None = None, fast: bool = False):

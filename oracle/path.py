@@ -12,6 +12,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
+from . import fp8 as fp8mod
 from .fp8 import (E4M3, E5M2, amax_bits, bf16_bits_to_f32, f32_to_bf16_bits, fp8_to_f64, quantize_bits,
                   round_bf16)
 
@@ -29,7 +30,10 @@ class Q:
         cache = self.__dict__.setdefault("_deq", {})
         key = np.dtype(dtype).str
         if key not in cache:
-            cache[key] = fp8_to_f64(self.codes, self.fmt).astype(dtype, copy=False)
+            if fp8mod.THREADED and np.dtype(dtype) == np.float32:
+                cache[key] = fp8mod.fp8_to_f32_threaded(self.codes, self.fmt)
+            else:
+                cache[key] = fp8_to_f64(self.codes, self.fmt).astype(dtype, copy=False)
         return cache[key]
 
 

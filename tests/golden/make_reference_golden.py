@@ -1,8 +1,8 @@
 """Records the reference's own behaviour for tests/golden/reference_scenarios.py.
 
-    python tests/golden/make_reference_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_reference_golden.py REFERENCE_ROOT
 
-REFERENCE_ROOT defaults to /root/reference (the macrogpt-jax checkout).  The reference's
+REFERENCE_ROOT is the macrogpt-jax checkout (or set MACROGPT_JAX_REFERENCE).  The reference's
 package imports JAX at the top of ueaj/utils/__init__.py and ueaj/model/einsum.py, which is not
 installed here, so this script loads only pure-Python code from it, unchanged:
 ueaj/utils/configurator.py as a standalone module, and the EinsumMetadata dataclass plus the
@@ -17,6 +17,7 @@ import ast
 import importlib.util
 import json
 import operator
+import os
 import sys
 from dataclasses import dataclass
 from functools import reduce
@@ -49,8 +50,9 @@ def load_einsum_metadata(root: Path):
 
 
 def constructor_signatures(root: Path) -> dict:
-    """Positional parameters with their default expressions (source text) and keyword-only
-    parameters of the layer constructors on the path, read from the reference's source."""
+    """Positional and keyword-only parameters with their default expressions (source text;
+    None where there is no default) of the layer constructors on the path, read from the
+    reference's source."""
     out = {}
     for rel, cls in (("ueaj/model/einsum.py", "Einsum"), ("ueaj/model/mlp.py", "GMLP"), ("ueaj/model/mlp.py", "MLP"),
                      ("ueaj/model/soft_attn.py", "SoftmaxAttention")):
@@ -60,13 +62,17 @@ def constructor_signatures(root: Path) -> dict:
         a = init.args
         pos = [x.arg for x in a.args][1:]
         defaults = [None] * (len(pos) - len(a.defaults)) + [ast.unparse(d) for d in a.defaults]
+        kw_defaults = [None if d is None else ast.unparse(d) for d in a.kw_defaults]
         out[cls] = {"positional": [[n, d] for n, d in zip(pos, defaults)],
-                    "keyword_only": [x.arg for x in a.kwonlyargs]}
+                    "keyword_only": [[x.arg, d] for x, d in zip(a.kwonlyargs, kw_defaults)]}
     return out
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MACROGPT_JAX_REFERENCE")
+    if not arg:
+        raise SystemExit("usage: make_reference_golden.py REFERENCE_ROOT (or set MACROGPT_JAX_REFERENCE)")
+    root = Path(arg)
     cfg = load_configurator(root)
     parse, meta = load_einsum_metadata(root)
     out = {"configurator": sc.configurator_results(cfg.config, cfg.override),

@@ -69,7 +69,7 @@ def test_quant_edges(cuda, fmt, case):
     x = bf16_normal(rng, (4099,))
     if case == "zeros":
         x[:] = 0
-    elif case == "tiny":       # denormal amax: s = FMAX/amax overflows to inf
+    elif case == "tiny":       # denormal amax: FMAX/amax overflows; s is capped at FLT_MAX
         x = (rng.integers(0, 3, 4099).astype(np.uint16)) | (rng.integers(0, 2, 4099).astype(np.uint16) << 15)
     elif case == "nan":
         x[17] = 0x7FC0
@@ -98,3 +98,22 @@ def test_quant_ops_wrapper(cuda):
     rc2, _, rinv2 = ofp8.quantize_bits(xb.reshape(-1), ofp8.E4M3, np.float32(float(ramax) / 2))
     assert (torch_fp8_to_codes(qt2.q).reshape(-1) == rc2).all()
     assert qt2.inv_scale.item() == float(rinv2)
+
+
+@pytest.mark.parametrize("fmt", [ofp8.E4M3, ofp8.E5M2])
+@pytest.mark.parametrize("amax", [1e-37, 3e-36, 1e-34])
+def test_quant_tiny_amax_stays_finite(cuda, fmt, amax):
+    """Normal bf16 tensors whose amax is below FMAX / FLT_MAX: the scale is capped at FLT_MAX,
+    so no code is NaN/inf (an uncapped scale would be +inf and turn 0 into NaN), the codes
+    match the oracle bit for bit, and code * inv_scale is close to x."""
+    rng = np.random.default_rng(5)
+    x = bf16_normal(rng, (70001,), std=amax / 4.0)
+    x[0] = 0
+    _check(x, fmt, cuda)
+    codes, _, inv_u = _run(x, fmt, cuda)
+    inv = np.array([inv_u], np.uint32).view(np.float32)[0]
+    vals = ofp8.fp8_to_f64(codes, fmt)
+    assert np.isfinite(vals).all()
+    xf = ofp8.bf16_bits_to_f32(x).astype(np.float64)
+    deq = vals * np.float64(inv)
+    assert np.abs(deq - xf).max() <= 0.13 * np.abs(xf).max()

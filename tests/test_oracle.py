@@ -68,12 +68,22 @@ def test_quantize_recipe_edges():
     x = fp8.f32_to_bf16_bits(np.array([0.5, -3.0, 1.25], np.float32))
     q, a, inv = fp8.quantize_bits(x, fp8.E4M3)
     assert a == np.float32(3.0) and q[1] == 0xFE  # -448
-    # denormal amax: s overflows to inf; x*inf -> inf (NaN code in e4m3fn), 0*inf -> NaN
+    # denormal amax: FMAX/amax overflows, s is capped at FLT_MAX, so the products stay finite:
+    # x = 2^-133 (bf16 0x0001): 2^-133 * FLT_MAX = 2^-6 * (2 - 2^-23) rounds to 2^-5 in both
+    # formats, 0 stays 0, and code * inv_scale (2^-128) gives x back exactly
     x = np.array([0x0001, 0x0000, 0x8001], np.uint16)
     q, a, inv = fp8.quantize_bits(x, fp8.E4M3)
-    assert inv == 0 and list(q) == [0x7F, 0x7F, 0xFF]
+    assert inv == np.float32(2.0 ** -128) and list(q) == [0x10, 0x00, 0x90]
     q, _, _ = fp8.quantize_bits(x, fp8.E5M2)
-    assert list(q) == [0x7C, 0x7E, 0xFC]
+    assert list(q) == [0x28, 0x00, 0xA8]
+    # amax around 1e-37 (normal bf16): no NaN, dequantised values close to x
+    for fmt in (fp8.E4M3, fp8.E5M2):
+        xb = fp8.f32_to_bf16_bits(np.array([1e-37, -3e-38, 5e-38, 0.0], np.float32))
+        q, a, inv = fp8.quantize_bits(xb, fmt)
+        deq = fp8.fp8_to_f64(q, fmt) * np.float64(inv)
+        ref = fp8.bf16_bits_to_f32(xb).astype(np.float64)
+        assert np.isfinite(deq).all()
+        assert np.abs(deq - ref).max() <= 0.13 * np.abs(ref).max()
     # a NaN element makes amax NaN and every code NaN
     x = fp8.f32_to_bf16_bits(np.array([1.0, np.nan], np.float32))
     q, a, inv = fp8.quantize_bits(x, fp8.E4M3)
@@ -134,3 +144,40 @@ def test_golden_fixtures_reproduce():
             assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), k
         else:
             assert np.array_equal(a, b), k
+
+
+def test_threaded_passes_equal_numpy():
+    """The CPU baseline's threaded element-wise passes (fp8.THREADED) give the numpy bits:
+    bf16 -> f32 and the RNE f32 -> bf16 rounding on every bf16 pattern and on random f32 values
+    (ties included), fp8 -> f32 on all 256 codes of both formats, and a whole oracle GMLP step."""
+    allb = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    rng = np.random.default_rng(4)
+    f = rng.standard_normal(200_000).astype(np.float32) * np.float32(3e3)
+    ties = (fp8.bf16_bits_to_f32(allb[:30000]).view(np.uint32) | np.uint32(0x8000)).view(np.float32)
+    f = np.concatenate([f, ties[np.isfinite(ties)], np.array([0.0, -0.0, 3.4e38, -1e-40], np.float32)])
+    ref_up = fp8.bf16_bits_to_f32(allb)
+    ref_down = fp8.f32_to_bf16_bits(f)
+    ref_codes = {fmt: fp8.fp8_to_f64(np.arange(256, dtype=np.uint8), fmt).astype(np.float32) for fmt in (0, 1)}
+    x = path.bf16_normal(rng, (64, 48))
+    wf = path.bf16_normal(rng, (2, 48, 80), 48 ** -0.5)
+    wd = path.bf16_normal(rng, (80, 48), 80 ** -0.5)
+    dy = path.bf16_normal(rng, (64, 48), 1e-3)
+    y_ref, saved = path.gmlp_forward(x, wf, wd, acc=np.float32)
+    g_ref = path.gmlp_backward(dy, saved, acc=np.float32)
+    fp8.THREADED = True
+    try:
+        up = fp8.bf16_bits_to_f32(allb)
+        assert np.array_equal(up.view(np.uint32), ref_up.view(np.uint32))
+        assert np.array_equal(fp8.f32_to_bf16_bits(f), ref_down)
+        for fmt in (0, 1):
+            got = fp8.fp8_to_f32_threaded(np.arange(256, dtype=np.uint8), fmt)
+            assert np.array_equal(np.isnan(got), np.isnan(ref_codes[fmt]))
+            fin = ~np.isnan(got)
+            assert np.array_equal(got[fin].view(np.uint32), ref_codes[fmt][fin].view(np.uint32))
+        y, saved2 = path.gmlp_forward(x, wf, wd, acc=np.float32)
+        g = path.gmlp_backward(dy, saved2, acc=np.float32)
+    finally:
+        fp8.THREADED = False
+    assert np.array_equal(y, y_ref)
+    for k in ("dx", "dwf", "dwd"):
+        assert np.array_equal(g[k], g_ref[k]), k

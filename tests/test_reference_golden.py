@@ -42,8 +42,8 @@ def test_einsum_metadata_matches_reference():
 
 def test_layer_constructors_match_reference_signatures():
     """Same positional parameters in the same order with the same defaults (a JAX default
-    maps to its PyTorch counterpart), and the reference's keyword-only parameters first;
-    additions are keyword-only and come after them."""
+    maps to its PyTorch counterpart), and the reference's keyword-only parameters first, with
+    the same defaults; additions are keyword-only and come after them."""
     import inspect
 
     import torch
@@ -67,4 +67,10 @@ def test_layer_constructors_match_reference_signatures():
                 assert p.default is inspect.Parameter.empty, (cls.__name__, name)
             else:
                 assert p.default == same_as[default], (cls.__name__, name)
-        assert kwo[:len(want["keyword_only"])] == want["keyword_only"], cls.__name__
+        kw = {p.name: p for p in params if p.kind is inspect.Parameter.KEYWORD_ONLY}
+        assert kwo[:len(want["keyword_only"])] == [n for n, _ in want["keyword_only"]], cls.__name__
+        for name, default in want["keyword_only"]:
+            if default is None:
+                assert kw[name].default is inspect.Parameter.empty, (cls.__name__, name)
+            else:
+                assert kw[name].default == same_as[default], (cls.__name__, name)
