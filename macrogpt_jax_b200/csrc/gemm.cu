@@ -494,12 +494,17 @@ __host__ __device__ constexpr int pair_smem_bytes(int stages, int var, int kch =
 }
 constexpr int kPSmemBytes = pair_smem_bytes(kPStages, kVarDirect);
 constexpr int kPSmemBytesWide = pair_smem_bytes(kPStagesWide, kVarDirect, 2);
+constexpr int kPStagesWideStaged = 2;  // beside the RS rows (36 KiB) or U/G boxes (64 KiB)
+constexpr int kPSmemBytesWideStaged = pair_smem_bytes(kPStagesWideStaged, kVarRsStaged, 2);
+constexpr int kPSmemBytesWideUg = pair_smem_bytes(kPStagesWideStaged, kVarUgStaged, 2);
 constexpr int kPSmemBytesStaged = pair_smem_bytes(kPStagesStaged, kVarRsStaged);
 constexpr int kPSmemBytesUg = pair_smem_bytes(kPStagesStaged, kVarUgStaged);
 static_assert(kPSmemBytesStaged <= 232448, "staged CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytesUg <= 232448, "U/G-staged CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytes <= 232448, "CTA-pair kernel exceeds shared memory");
 static_assert(kPSmemBytesWide <= 232448, "wide-stage CTA-pair kernel exceeds shared memory");
+static_assert(kPSmemBytesWideStaged <= 232448, "wide-stage RS kernel exceeds shared memory");
+static_assert(kPSmemBytesWideUg <= 232448, "wide-stage U/G kernel exceeds shared memory");
 
 // Stores 32 consecutive bf16 values packed two per word (element 2j in the low half of w[j]).
 __device__ __forceinline__ void store_bf16x32_packed(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
@@ -1341,6 +1346,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWide);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWideStaged, kVarRsStaged, 2>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWideStaged);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWideStaged, kVarUgStaged, 2>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWideUg);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
@@ -1357,8 +1368,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   // ring stages of two 128-byte K chunks, 3 deep.  Half as many full/empty hand-offs per FLOP as
   // the 7-deep ring of single chunks (UFP8_GEMM_CTA_PAIR), which measured 8-9 % slower on the
   // long-K GMLP contractions (F2 754 vs 694 us, B4 1484 vs 1355 us at 16384 x 4096 x 14336 / 28672).
-  const bool wide = pair && var == kVarDirect &&
-                    (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE);
+  // The staged epilogues keep the single-chunk ring unless UFP8_GEMM_CTA_PAIR_WIDE asks for two
+  // chunks there too (2 stages beside the RS rows or the U/G boxes).
+  const bool wide = pair && ((var == kVarDirect && (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE)) ||
+                             (var != kVarDirect && variant == UFP8_GEMM_CTA_PAIR_WIDE));
   const int kch = wide ? 2 : 1;
   a.ksteps = static_cast<int>((d.K + kch * kBK - 1) / (kch * kBK));
   CUtensorMap tmUG, tmD;
@@ -1370,19 +1383,26 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     rc = encode_bf16_boxes(&tmD, d.d, d.N, d.M, d.ldd, d.d_batch_stride, "D");
     if (rc) return rc;
   }
-  const void* pair_fn = var == kVarRsStaged   ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>)
-                        : var == kVarUgStaged ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>)
-                        : wide                ? reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2>)
-                                              : reinterpret_cast<const void*>(gemm_fp8_pair_kernel<kPStages, kVarDirect>);
-  const int pair_smem = var == kVarRsStaged ? kPSmemBytesStaged
-                        : var == kVarUgStaged ? kPSmemBytesUg
-                        : wide ? kPSmemBytesWide : kPSmemBytes;
-  const int occ_slot = wide ? 3 : var;
+  using PairFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmArgs);
+  PairFn pair_kernel;
+  int pair_smem;
+  if (var == kVarRsStaged) {
+    pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWideStaged, kVarRsStaged, 2> : gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged>;
+    pair_smem = wide ? kPSmemBytesWideStaged : kPSmemBytesStaged;
+  } else if (var == kVarUgStaged) {
+    pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWideStaged, kVarUgStaged, 2> : gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>;
+    pair_smem = wide ? kPSmemBytesWideUg : kPSmemBytesUg;
+  } else {
+    pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2> : gemm_fp8_pair_kernel<kPStages, kVarDirect>;
+    pair_smem = wide ? kPSmemBytesWide : kPSmemBytes;
+  }
+  const void* pair_fn = reinterpret_cast<const void*>(pair_kernel);
+  const int occ_slot = var + (wide ? 3 : 0);
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device[4] = {-1, -1, -1, -1}, occ_clusters[4] = {0, 0, 0, 0};
+    static thread_local int occ_device[6] = {-1, -1, -1, -1, -1, -1}, occ_clusters[6] = {0, 0, 0, 0, 0, 0};
     if (occ_device[occ_slot] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
@@ -1402,14 +1422,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (clusters < 1) clusters = 1;
     if (num_tiles < clusters) clusters = num_tiles;
     const int grid = static_cast<int>(2 * clusters);
-    if (var == kVarRsStaged)
-      gemm_fp8_pair_kernel<kPStagesStaged, kVarRsStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
-    else if (var == kVarUgStaged)
-      gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
-    else if (wide)
-      gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
-    else
-      gemm_fp8_pair_kernel<kPStages, kVarDirect><<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
+    pair_kernel<<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
   } else {
     if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
     gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);

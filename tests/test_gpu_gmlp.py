@@ -36,3 +36,21 @@ def test_gmlp_fwd_bwd(cuda, T, d, h):
     compare(bf16_bits_to_f64(torch_bf16_to_bits(dx)), bf16_bits_to_f64(rb["dx"]))
     compare(bf16_bits_to_f64(torch_bf16_to_bits(dwf)), bf16_bits_to_f64(rb["dwf"]))
     compare(bf16_bits_to_f64(torch_bf16_to_bits(dwd)), bf16_bits_to_f64(rb["dwd"]))
+
+
+def test_gmlp_fwd_bwd_small_workload_full_size(cuda):
+    """The small GMLP workload at its own size (8192 tokens, d_model 768, hidden 3072) against
+    the oracle; the oracle accumulates in fp32 here (numpy BLAS) to finish in seconds."""
+    from macrogpt_jax_b200 import ops
+    T, d, h = 8192, 768, 3072
+    x, wf, wd, dy = _inputs(T, d, h, seed=3)
+    y, saved = ops.gmlp_forward(bits_to_torch_bf16(x, cuda), bits_to_torch_bf16(wf, cuda),
+                                bits_to_torch_bf16(wd, cuda))
+    dx, dwf, dwd = ops.gmlp_backward(bits_to_torch_bf16(dy, cuda), saved)
+    ry, rs = op.gmlp_forward(x, wf, wd, acc=np.float32)
+    rb = op.gmlp_backward(dy, rs, acc=np.float32)
+    assert (torch_fp8_to_codes(saved[0].q) == rs["qx"].codes).all()
+    assert (torch_fp8_to_codes(saved[1].q) == rs["qwf"].codes).all()
+    assert (torch_fp8_to_codes(saved[4].q) == rs["qwd"].codes).all()
+    for got, ref in ((y, ry), (dx, rb["dx"]), (dwf, rb["dwf"]), (dwd, rb["dwd"])):
+        compare(bf16_bits_to_f64(torch_bf16_to_bits(got)), bf16_bits_to_f64(ref))

@@ -167,3 +167,60 @@ def test_attention_projections(cuda, fused):
     compare(bf16_bits_to_f64(torch_bf16_to_bits(y)), bf16_bits_to_f64(ry))
     y.backward(bits_to_torch_bf16(op.bf16_normal(rng, (2, 96, d), 1e-2), cuda))
     assert x.grad is not None and x.grad.shape == x.shape and torch.isfinite(x.grad.float()).all()
+
+
+def _attention_backward_case(cuda, fused, b, n, d, H, K, acc, seed):
+    """Q/K/V/O projections forward and backward with independent seeded upstream gradients
+    (dq, dk, dv for the projections, dy for O, whose input `a` is an independent leaf), against
+    the oracle: the outputs, dx (the sum of the projections' input gradients), dW of every
+    projection weight and da."""
+    import torch
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+    init = Einsum.override(initializer=scaled_normal_init(d ** -0.5))
+    kw = dict(qkv=init, o=init) if fused else dict(q=init, k=init, v=init, o=init)
+    m = SoftmaxAttention(d, kq_d=K, kv_heads=H, rngs=Rngs(seed), fused_qkv=fused, **kw)
+    rng = np.random.default_rng(seed)
+    xb = op.bf16_normal(rng, (b, n, d))
+    ab = op.bf16_normal(rng, (b, n, H, 1, K))
+    dqkv = op.bf16_normal(rng, (3, b, n, H, K), 1e-3)
+    dyb = op.bf16_normal(rng, (b, n, d), 1e-3)
+    x = bits_to_torch_bf16(xb, cuda).requires_grad_(True)
+    a = bits_to_torch_bf16(ab, cuda).requires_grad_(True)
+    q, k, v = m.project_qkv(x)
+    y = m.project_out(a)
+    g = bits_to_torch_bf16(dqkv, cuda)
+    torch.autograd.backward([q, k, v, y], [g[0].reshape(q.shape), g[1], g[2], bits_to_torch_bf16(dyb, cuda)])
+    if fused:
+        w = torch_bf16_to_bits(m.qkv.w)
+        ref, qx, qw = op.einsum_fp8("bnd,fdhk->fbnhk", xb, w, acc=acc)
+        got = torch.stack([q.reshape(b, n, H, K), k, v])
+        compare(bf16_bits_to_f64(torch_bf16_to_bits(got)), bf16_bits_to_f64(ref))
+        rdx, rdw = op.einsum_fp8_backward("bnd,fdhk->fbnhk", qx, qw, dqkv, acc=acc)
+        compare(bf16_bits_to_f64(torch_bf16_to_bits(m.qkv.w.grad)), bf16_bits_to_f64(rdw))
+        ref_dx = bf16_bits_to_f64(rdx)
+    else:
+        ref_dx = 0.0
+        for t, e, gi in ((q, m.q, dqkv[0].reshape(b, n, H, 1, K)), (k, m.k, dqkv[1]), (v, m.v, dqkv[2])):
+            ref, qx, qw = op.einsum_fp8(e.einsum_expr, xb, torch_bf16_to_bits(e.w), acc=acc)
+            compare(bf16_bits_to_f64(torch_bf16_to_bits(t)), bf16_bits_to_f64(ref))
+            rdx, rdw = op.einsum_fp8_backward(e.einsum_expr, qx, qw, gi, acc=acc)
+            compare(bf16_bits_to_f64(torch_bf16_to_bits(e.w.grad)), bf16_bits_to_f64(rdw))
+            ref_dx = ref_dx + bf16_bits_to_f64(rdx)  # autograd sums the three input gradients
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(x.grad)), ref_dx)
+    ry, qa, qo = op.einsum_fp8("bnhiv,hivd->bnd", ab, torch_bf16_to_bits(m.o.w), acc=acc)
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(y)), bf16_bits_to_f64(ry))
+    rda, rdo = op.einsum_fp8_backward("bnhiv,hivd->bnd", qa, qo, dyb, acc=acc)
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(a.grad)), bf16_bits_to_f64(rda))
+    compare(bf16_bits_to_f64(torch_bf16_to_bits(m.o.w.grad)), bf16_bits_to_f64(rdo))
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_attention_projections_backward(cuda, fused):
+    _attention_backward_case(cuda, fused, 2, 96, 256, 4, 64, np.float64, 5)
+
+
+def test_attention_projections_full_size(cuda):
+    """The attention-projection workload at its own size: 16384 tokens (B16 x S1024), d_model
+    2048, 16 heads x 128, fused QKV; the oracle accumulates in fp32 to finish in seconds."""
+    _attention_backward_case(cuda, True, 16, 1024, 2048, 16, 128, np.float32, 6)
