@@ -238,12 +238,15 @@ int ufp8_set_gemm_ctas(int ctas);
  * chunk, 7 deep; RS_PUSH rows leave through shared memory as bulk async stores and DSWIGLU
  * reads the saved U / G through TMA), UFP8_GEMM_CTA_PAIR_DIRECT (the same tiles with plain
  * 16-byte loads and stores in every epilogue) or UFP8_GEMM_CTA_PAIR_WIDE (UFP8_GEMM_CTA_PAIR
- * with ring stages of two 128-byte K chunks, 3 deep, for the epilogues that store directly). */
+ * with ring stages of two 128-byte K chunks, 3 deep, for the epilogues that store directly) or
+ * UFP8_GEMM_CTA_PAIR_N512 (256 x 512 tiles on a CTA pair, for bf16 STORE and SWIGLU outputs;
+ * the others as UFP8_GEMM_CTA_PAIR). */
 #define UFP8_GEMM_AUTO 0
 #define UFP8_GEMM_SINGLE_CTA 1
 #define UFP8_GEMM_CTA_PAIR 2
 #define UFP8_GEMM_CTA_PAIR_DIRECT 3
 #define UFP8_GEMM_CTA_PAIR_WIDE 4
+#define UFP8_GEMM_CTA_PAIR_N512 5
 int ufp8_set_gemm_variant(int variant);
 
 /* Tile raster of the persistent GEMM: how many M tiles form a group that is swept along N

@@ -19,7 +19,8 @@ E4M3, E5M2 = 0, 1
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH = 0, 1, 2, 3
-GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE = 0, 1, 2, 3, 4
+GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE, GEMM_CTA_PAIR_N512 = (
+    0, 1, 2, 3, 4, 5)
 
 EXPORTED_SYMBOLS = (
     "ufp8_last_error",

@@ -141,7 +141,8 @@ int ufp8_device_status(int* status, int clear) {
 
 int ufp8_set_gemm_variant(int variant) {
   if (variant != UFP8_GEMM_AUTO && variant != UFP8_GEMM_SINGLE_CTA && variant != UFP8_GEMM_CTA_PAIR &&
-      variant != UFP8_GEMM_CTA_PAIR_DIRECT && variant != UFP8_GEMM_CTA_PAIR_WIDE)
+      variant != UFP8_GEMM_CTA_PAIR_DIRECT && variant != UFP8_GEMM_CTA_PAIR_WIDE &&
+      variant != UFP8_GEMM_CTA_PAIR_N512)
     return set_error(UFP8_ERR_INVALID, "ufp8_set_gemm_variant: unknown variant %d", variant);
   g_gemm_variant = variant;
   return UFP8_OK;

@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
     const int row_in_tile = quad * 32 + lane;
     const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
-    const bool vec = args.vec_ok != 0;
+    const int vec = args.vec_ok;
     uint32_t amax = 0;  // max |value| over bf16 bit patterns written by this thread
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -536,9 +536,13 @@ __device__ __forceinline__ void store_bf16x16_packed(__nv_bfloat16* p, const uin
   }
 }
 
+// vec: 0 = element stores, 1 = 16-byte stores (16-byte aligned rows), 2 = 32-byte stores
+// (32-byte aligned rows).
 __device__ __forceinline__ void store_bf16x16_packed_h(__nv_bfloat16* p, const uint32_t (&w)[8], int valid,
-                                                       bool vec, uint64_t pol) {
-  if (vec && valid >= 16) {
+                                                       int vec, uint64_t pol) {
+  if (vec >= 2 && valid >= 16) {
+    st_global_v8_hint(p, make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]), pol);
+  } else if (vec && valid >= 16) {
     st_global_v4_hint(p, make_uint4(w[0], w[1], w[2], w[3]), pol);
     st_global_v4_hint(p + 8, make_uint4(w[4], w[5], w[6], w[7]), pol);
   } else {
@@ -547,8 +551,11 @@ __device__ __forceinline__ void store_bf16x16_packed_h(__nv_bfloat16* p, const u
 }
 
 __device__ __forceinline__ void store_bf16x32_packed_h(__nv_bfloat16* p, const uint32_t (&w)[16], int valid,
-                                                       bool vec, uint64_t pol) {
-  if (vec && valid >= 32) {
+                                                       int vec, uint64_t pol) {
+  if (vec >= 2 && valid >= 32) {
+    st_global_v8_hint(p, make_uint4(w[0], w[1], w[2], w[3]), make_uint4(w[4], w[5], w[6], w[7]), pol);
+    st_global_v8_hint(p + 16, make_uint4(w[8], w[9], w[10], w[11]), make_uint4(w[12], w[13], w[14], w[15]), pol);
+  } else if (vec && valid >= 32) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) st_global_v4_hint(p + 8 * i, make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]), pol);
   } else {
@@ -769,7 +776,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const int chalf = e >> 2;    // which half of the tile's columns this warp handles
     const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
     const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
-    const bool vec = args.vec_ok != 0;
+    const int vec = args.vec_ok;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint64_t stream = l2_policy_evict_first();  // outputs are not re-read by this kernel
     uint32_t amax = 0;
@@ -1078,6 +1085,337 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicOr(args.status, UFP8_STATUS_WAIT_TIMEOUT);
 }
 
+// ============================================================================= 256 x 512 pair tiles
+// The same contraction on a cluster of two CTAs computing 256 x 512 tiles.  Every 128-byte K
+// step issues two tcgen05.mma.cta_group::2 (M = 256, N = 256) with the same A sub-tiles, into
+// TMEM columns [0, 256) ("half 0") and [256, 512) ("half 1"), so a CTA streams 48 KiB (A: 128
+// rows; B: two sub-tiles of 128 rows) for twice the MMAs of a 256 x 256 tile: 25 % fewer operand
+// bytes per FLOP cross from L2 into shared memory, which is what limits the 256 x 256 kernel on
+// long-K contractions (no TMA multicast is used).
+//
+// The accumulator fills all 512 TMEM columns, so it is handed over per half.  When a tile's
+// MMAs complete, the epilogue warps copy half 0 into registers (packed bf16, 64 registers a
+// thread), release it (tempty[0]), store it, then do the same with half 1 (tempty[1]).  The MMA
+// thread starts the next tile with the half-0 MMAs of its first kWStages K steps as soon as
+// tempty[0] completes, then issues their half-1 MMAs once tempty[1] completes (only then are
+// those ring stages released), and continues with both halves per K step.
+//
+// Epilogues: STORE (bf16; half j = tile columns [256 j, 256 j + 256)) and SWIGLU (half j holds
+// 128 hidden units: up in its first 128 columns, gate in the next 128, loaded by the even and
+// the odd CTA respectively; U and G are rounded to bf16 before H = U * swish(G), as in the other
+// kernels, so the results are the same bits).
+constexpr int kWStages = 4;
+constexpr int kWStageBytes = 3 * kPHalfBytes;  // A + two B sub-tiles: 48 KiB
+constexpr int kWSmemBytes = kWStages * kWStageBytes + kBarrierBytes + 1024;
+static_assert(kWSmemBytes <= 232448, "256 x 512 CTA-pair kernel exceeds shared memory");
+
+// The three shared-memory descriptors (A, B half 0, B half 1) of MMA K step kk of the ring
+// stage at shared address sa.
+__device__ __forceinline__ void n512_descs(uint32_t sa, int kk, bool a_k, bool b_k, uint64_t& ad, uint64_t& b0,
+                                           uint64_t& b1) {
+  const uint32_t sb0 = sa + kPHalfBytes, sb1 = sa + 2 * kPHalfBytes;
+  ad = a_k ? make_sdesc_sw128(sa + kk * 32, 16, 1024) : make_sdesc_sw128(sa + kk * 32 * 128, kPHalfBytes, 1024);
+  b0 = b_k ? make_sdesc_sw128(sb0 + kk * 32, 16, 1024) : make_sdesc_sw128(sb0 + kk * 32 * 128, kPHalfBytes, 1024);
+  b1 = b_k ? make_sdesc_sw128(sb1 + kk * 32, 16, 1024) : make_sdesc_sw128(sb1 + kk * 32 * 128, kPHalfBytes, 1024);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
+    gemm_fp8_n512_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWStages * kWStageBytes);
+  uint64_t* empty = full + kWStages;
+  uint64_t* tfull = empty + kWStages;
+  uint64_t* tempty = tfull + 1;  // [2]: one per accumulator half
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(&tempty[0], 2 * kPEpiWarps);
+    mbar_init(&tempty[1], 2 * kPEpiWarps);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = args.tiles_m * args.tiles_n * args.batch;
+  const int total_k = args.ksteps * args.k_batches;
+  const bool swiglu = args.mode == UFP8_EPI_SWIGLU;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_parity = 0;
+      uint32_t arrived = 0;  // all-gather blocks seen complete (bit per source rank)
+      for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters) {
+        int g, mb, nb;
+        map_tile(tile, args, g, mb, nb);
+        const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        if (args.ag_flags != nullptr && row0 < args.M) {
+          const int src = static_cast<int>(row0 / args.ag_rows);
+          if (src != args.ag_rank && !((arrived >> src) & 1u)) {
+            if (!ag_wait(args, src, abort_flag)) break;
+            arrived |= 1u << src;
+          }
+        }
+        for (int ks = 0; ks < total_k; ++ks) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+          const int kb = ks / args.ksteps;
+          const int k0 = (ks - kb * args.ksteps) * kBK;
+          uint8_t* sa = smem + stage * kWStageBytes;
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage], 2 * kWStageBytes);
+            armed |= 1u << stage;
+            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          if (args.a_major == UFP8_K_MAJOR)
+            tma_load_3d_pair(sa, &tmA, bar, k0, row0, az);
+          else
+            tma_load_3d_pair(sa, &tmA, bar, row0, k0, az);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            int n0, bz;
+            if (swiglu) {  // half j: hidden units nb*256 + 128 j; even CTA up, odd CTA gate
+              n0 = nb * kBN + j * 128;
+              bz = static_cast<int>(rank);
+            } else {
+              n0 = nb * 2 * kBN + j * kBN + static_cast<int>(rank) * 128;
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+            }
+            uint8_t* sb = sa + (1 + j) * kPHalfBytes;
+            if (args.b_major == UFP8_K_MAJOR)
+              tma_load_3d_pair(sb, &tmB, bar, k0, n0, bz);
+            else
+              tma_load_3d_pair(sb, &tmB, bar, n0, k0, bz);
+          }
+          if (++stage == kWStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag && leader) {
+        volatile int never = 0;
+        for (int s = 0; s < kWStages; ++s)
+          if (armed & (1u << s)) mbar_wait(&full[s], (armed_parity >> s) & 1u, &never);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      const int pre = total_k < kWStages ? total_k : kWStages;  // K steps issued half 0 first
+      const bool a_k = args.a_major == UFP8_K_MAJOR, b_k = args.b_major == UFP8_K_MAJOR;
+      bool ok = true;
+      for (int tile = cluster_id; tile < num_tiles && ok && !*abort_flag; tile += num_clusters, ++local) {
+        const uint32_t tpar = (local & 1) ^ 1u;  // tile `local` needs the epilogue of local - 1
+        // Half 0 of the first `pre` K steps, as soon as the epilogue has released half 0.
+        if (!mbar_wait(&tempty[0], tpar, abort_flag)) break;
+        tc_fence_after();
+        int st = stage;
+        uint32_t ph = phase;
+        for (int ks = 0; ks < pre; ++ks) {
+          if (!mbar_wait(&full[st], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + st * kWStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            uint64_t ad, b0, b1;
+            n512_descs(sa, kk, a_k, b_k, ad, b0, b1);
+            umma_f8f6f4_pair(tmem_base, ad, b0, args.idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          if (++st == kWStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        // Half 1 of the same K steps once half 1 is free; their ring stages are released here.
+        if (!mbar_wait(&tempty[1], tpar, abort_flag)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < pre; ++ks) {
+          const uint32_t sa = smem_u32(smem + stage * kWStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            uint64_t ad, b0, b1;
+            n512_descs(sa, kk, a_k, b_k, ad, b0, b1);
+            umma_f8f6f4_pair(tmem_base + kBN, ad, b1, args.idesc, (ks | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kWStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        // The remaining K steps: both halves per stage.
+        for (int ks = pre; ks < total_k; ++ks) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kWStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk) {
+            uint64_t ad, b0, b1;
+            n512_descs(sa, kk, a_k, b_k, ad, b0, b1);
+            umma_f8f6f4_pair(tmem_base, ad, b0, args.idesc, 1u);
+            umma_f8f6f4_pair(tmem_base + kBN, ad, b1, args.idesc, 1u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kWStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull, 0x3);
+      }
+      umma_commit_pair(drain, 0x1);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (both CTAs)
+    const int e = warp - 2;
+    const int quad = warp & 3;  // TMEM lanes this warp may read: [32*quad, 32*quad+32)
+    const int chalf = e >> 2;   // which half of each accumulator half this warp drains
+    const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
+    const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
+    const int vec = args.vec_ok;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    const uint64_t stream = l2_policy_evict_first();
+    uint32_t amax = 0;
+    int local = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
+      bool ok = mbar_wait(tfull, local & 1, abort_flag);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      int g, mb, nb;
+      map_tile(tile, args, g, mb, nb);
+      const int row = mb * 2 * kBM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t hbase = tbase + static_cast<uint32_t>(half * kBN);
+        uint32_t pk[64];  // 128 accumulator columns of this row, packed bf16
+        // Four 32-column chunks: STORE columns [128 chalf, +128); SWIGLU 64 hidden units, up in
+        // columns [64 chalf, +64) -> pk[0, 32), gate in [128 + 64 chalf, +64) -> pk[32, 64).
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t col = swiglu ? static_cast<uint32_t>((c >> 1) * 128 + chalf * 64 + (c & 1) * 32)
+                                      : static_cast<uint32_t>(chalf * 128 + c * 32);
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(hbase + col, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            pk[16 * c + j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
+        }
+        // This half is in registers: hand it back to the MMA thread before storing.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(half * sizeof(uint64_t)));
+        if (row_ok) {
+          if (swiglu) {
+            const int unit0 = nb * kBN + half * 128 + chalf * 64;
+            __nv_bfloat16* pu = static_cast<__nv_bfloat16*>(args.d) + row * args.ldd;
+            __nv_bfloat16* ph = args.h + row * args.ldh;
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const int col0 = unit0 + 32 * q;
+              if (col0 < args.N) {
+                const int valid = args.N - col0;
+                uint32_t uw[16], gw[16], hw[16];
+                uint32_t m2 = 0;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  uw[j] = pk[16 * q + j];
+                  gw[j] = pk[32 + 16 * q + j];
+                  const float g0 = lo_f(gw[j]), g1 = hi_f(gw[j]);
+                  hw[j] = pack_bf16x2(lo_f(uw[j]) * (g0 * sigmoidf_(g0)), hi_f(uw[j]) * (g1 * sigmoidf_(g1)));
+                  const uint32_t keep = (2 * j + 1 < valid) ? 0x7FFF7FFFu : (2 * j < valid ? 0x00007FFFu : 0u);
+                  m2 = __vmaxu2(m2, hw[j] & keep);
+                }
+                amax = max(amax, max(m2 & 0xFFFFu, m2 >> 16));
+                store_bf16x32_packed_h(pu + col0, uw, valid, vec, stream);
+                store_bf16x32_packed_h(pu + args.d_bstride + col0, gw, valid, vec, stream);
+                store_bf16x32_packed_h(ph + col0, hw, valid, vec, stream);
+              }
+            }
+          } else {
+            const int colbase = nb * 2 * kBN + half * kBN + chalf * 128;
+            __nv_bfloat16* pd = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int col0 = colbase + 32 * q;
+              if (col0 < args.N) {
+                uint32_t w[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w[j] = pk[16 * q + j];
+                store_bf16x32_packed_h(pd + col0, w, args.N - col0, vec, stream);
+              }
+            }
+          }
+        }
+      }
+    }
+    if (args.amax_bits != nullptr) {
+      amax = __reduce_max_sync(0xFFFFFFFFu, amax);
+      if (lane == 0 && amax != 0u) atomicMax(args.amax_bits, amax << 16);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicOr(args.status, UFP8_STATUS_WAIT_TIMEOUT);
+}
+
 // Writes zeros to every output of an empty-K contraction (K == 0).
 __global__ void zero_outputs_kernel(GemmArgs a) {
   const long long total = static_cast<long long>(a.batch) * a.M * a.N;
@@ -1323,7 +1661,11 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   bool vec = (rs || aligned16(d.d)) && (d.ldd * esz) % 16 == 0 && (d.d_batch_stride * esz) % 16 == 0;
   if (swiglu) vec = vec && aligned16(d.h) && (d.ldh * 2) % 16 == 0;
   if (d.epilogue == UFP8_EPI_DSWIGLU) vec = vec && aligned16(d.ug) && (d.ldug * 2) % 16 == 0 && (d.ug_batch_stride * 2) % 16 == 0;
-  a.vec_ok = vec ? 1 : 0;
+  // 32-byte stores where every row start is 32-byte aligned (the direct epilogues' bf16 rows).
+  auto aligned32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31u) == 0; };
+  bool vec32 = vec && !a.d_f32 && !rs && aligned32(d.d) && (d.ldd * esz) % 32 == 0 && (d.d_batch_stride * esz) % 32 == 0;
+  if (swiglu) vec32 = vec32 && aligned32(d.h) && (d.ldh * 2) % 32 == 0;
+  a.vec_ok = vec ? (vec32 ? 2 : 1) : 0;
 
   CUtensorMap tmA, tmB;
   rc = encode_operand(&tmA, d.a, d.M, d.K, "A");
@@ -1352,6 +1694,8 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWideStaged, kVarUgStaged, 2>,
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWideUg);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_n512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWSmemBytes);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
@@ -1370,8 +1714,23 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   // long-K GMLP contractions (F2 754 vs 694 us, B4 1484 vs 1355 us at 16384 x 4096 x 14336 / 28672).
   // The staged epilogues keep the single-chunk ring unless UFP8_GEMM_CTA_PAIR_WIDE asks for two
   // chunks there too (2 stages beside the RS rows or the U/G boxes).
-  const bool wide = pair && ((var == kVarDirect && (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE)) ||
-                             (var != kVarDirect && variant == UFP8_GEMM_CTA_PAIR_WIDE));
+  // 256 x 512 tiles (gemm_fp8_n512_kernel) for bf16 STORE / SWIGLU outputs: always with
+  // UFP8_GEMM_CTA_PAIR_N512; by default (UFP8_GEMM_AUTO) for bf16 STORE outputs when the tile
+  // rounds favour it.  A 256 x 512 tile runs in ~0.92x the time of two 256 x 256 tiles on the
+  // long-K GMLP contractions (F2 650 vs 680 us, B4 1250 vs 1311 us, B3 1305 vs 1333 us), but
+  // half as many tiles quantise worse onto the persistent grid and a ragged N wastes more.
+  bool n512 = pair && var == kVarDirect && !a.d_f32 && (d.epilogue == UFP8_EPI_STORE || swiglu) &&
+              variant == UFP8_GEMM_CTA_PAIR_N512;
+  if (pair && var == kVarDirect && !a.d_f32 && d.epilogue == UFP8_EPI_STORE && variant == UFP8_GEMM_AUTO) {
+    const int64_t nc = dev.sm_count / 2;
+    const int64_t t256 = static_cast<int64_t>(a.tiles_m) * ((d.N + 255) / 256) * d.batch;
+    const int64_t t512 = static_cast<int64_t>(a.tiles_m) * ((d.N + 511) / 512) * d.batch;
+    n512 = 1.84 * static_cast<double>((t512 + nc - 1) / nc) <= static_cast<double>((t256 + nc - 1) / nc);
+  }
+  const bool wide = !n512 && pair &&
+                    ((var == kVarDirect && (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE)) ||
+                     (var != kVarDirect && variant == UFP8_GEMM_CTA_PAIR_WIDE));
+  if (n512) a.tiles_n = static_cast<int>((d.N + 2 * bn - 1) / (2 * bn));
   const int kch = wide ? 2 : 1;
   a.ksteps = static_cast<int>((d.K + kch * kBK - 1) / (kch * kBK));
   CUtensorMap tmUG, tmD;
@@ -1396,13 +1755,15 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2> : gemm_fp8_pair_kernel<kPStages, kVarDirect>;
     pair_smem = wide ? kPSmemBytesWide : kPSmemBytes;
   }
-  const void* pair_fn = reinterpret_cast<const void*>(pair_kernel);
-  const int occ_slot = var + (wide ? 3 : 0);
+  if (n512) pair_smem = kWSmemBytes;
+  const void* pair_fn = n512 ? reinterpret_cast<const void*>(gemm_fp8_n512_kernel)
+                             : reinterpret_cast<const void*>(pair_kernel);
+  const int occ_slot = n512 ? 6 : var + (wide ? 3 : 0);
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device[6] = {-1, -1, -1, -1, -1, -1}, occ_clusters[6] = {0, 0, 0, 0, 0, 0};
+    static thread_local int occ_device[7] = {-1, -1, -1, -1, -1, -1, -1}, occ_clusters[7] = {0, 0, 0, 0, 0, 0, 0};
     if (occ_device[occ_slot] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);
@@ -1422,7 +1783,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (clusters < 1) clusters = 1;
     if (num_tiles < clusters) clusters = num_tiles;
     const int grid = static_cast<int>(2 * clusters);
-    pair_kernel<<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
+    if (n512)
+      gemm_fp8_n512_kernel<<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, a);
+    else
+      pair_kernel<<<grid, kPThreads, pair_smem, stream>>>(tmA, tmB, tmUG, tmD, a);
   } else {
     if (num_tiles < ctas) ctas = static_cast<int>(num_tiles);
     gemm_fp8_kernel<<<ctas, kThreads, kSmemBytes, stream>>>(tmA, tmB, a);

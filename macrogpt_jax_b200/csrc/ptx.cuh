@@ -209,6 +209,12 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+// 32-byte store (address 32-byte aligned) with an L2 cache hint: one full sector per request.
+__device__ __forceinline__ void st_global_v8_hint(void* ptr, uint4 lo, uint4 hi, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8}, %9;" ::"l"(ptr), "r"(lo.x),
+               "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void st_global_v4_hint(void* ptr, uint4 v, uint64_t policy) {
   asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w), "l"(policy)

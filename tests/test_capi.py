@@ -92,7 +92,7 @@ def test_host_validation_errors(call, code, msg):
 
 def test_python_wrapper_raises():
     with pytest.raises(C.UFP8Error) as e:
-        C.set_gemm_variant(5)
+        C.set_gemm_variant(6)
     assert e.value.code == C.ERR_INVALID
     C.set_gemm_variant(0)
 

@@ -14,12 +14,12 @@ from helpers import bf16_bits_to_f64, compare, torch_bf16_to_bits, bits_to_torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[1, 2, 3, 4], ids=["single_cta", "cta_pair", "cta_pair_direct", "cta_pair_wide"],
-                autouse=True)
+@pytest.fixture(params=[1, 2, 3, 4, 5], ids=["single_cta", "cta_pair", "cta_pair_direct", "cta_pair_wide",
+                                             "cta_pair_n512"], autouse=True)
 def variant(request, cuda):
     """Runs every test with the one-CTA kernel and with the CTA-pair kernel, the latter with
-    its staged epilogues (U / G of DSWIGLU through TMA), with the direct ones, and with ring
-    stages of two 128-byte K chunks (the default for the direct epilogues)."""
+    its staged epilogues (U / G of DSWIGLU through TMA), with the direct ones, with ring
+    stages of two 128-byte K chunks, and with 256 x 512 tiles (bf16 STORE and SWIGLU)."""
     from macrogpt_jax_b200 import _capi
     _capi.set_gemm_variant(request.param)
     yield request.param
