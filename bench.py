@@ -34,6 +34,9 @@ CONFIGS = {
     # attention projections (fused QKV d -> 3d plus O d -> d, 16 heads x 128)
     "gmlp_d4096": dict(kind="gmlp", d=4096, h=14336, B=4, S=4096),
     "gmlp_d768": dict(kind="gmlp", d=768, h=3072, B=8, S=1024),
+    # the MLP half of a transformer layer at the headline sizes: RMSNorm (fused with the fp8
+    # quantisation of its output) -> GMLP, forward and backward
+    "norm_gmlp_d4096": dict(kind="gmlp", d=4096, h=14336, B=4, S=4096, norm=True),
     "attn_d2048": dict(kind="attn", d=2048, heads=16, head_d=128, B=16, S=1024),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
@@ -285,6 +288,48 @@ def e2e_pipelined(step_fn, x_in, dy_in, steps, barrier, graph=False):
     return e0.elapsed_time(e1)
 
 
+def tp_parity_check(mlp, x_full, dy_full, x_in, dy_in, d, h, rank, world, dev):
+    """One tensor-parallel step (outside any timed region) against the single-GPU GMLP with the
+    same weights and inputs on rank 0: y and dx gathered over tokens, dWf and dWd gathered over
+    the hidden axis.  Returns {tensor: {max_rel, cos}} on rank 0 (None elsewhere).  The two
+    differ only in the order of the final bf16 sums (every per-tensor scale is global)."""
+    import torch
+    import torch.distributed as dist
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.mlp import GMLP
+    xl = x_in.detach().requires_grad_(True)
+    y = mlp(xl)
+    y.backward(dy_in)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    def gather(t, dim):
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        return torch.cat(parts, dim=dim)
+
+    got = {"y": gather(y.detach(), 0), "dx": gather(xl.grad, 0),
+           "dWf": gather(mlp.fused_proj.w.grad, 2), "dWd": gather(mlp.down_proj.w.grad, 0)}
+    for p in mlp.parameters():
+        p.grad = None
+    if rank != 0:
+        return None
+    ref_mlp = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(d ** -0.5)),
+                            down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
+        model_d=d, hidden_d=h, rngs=Rngs(0))
+    xr = x_full.reshape(-1, d).detach().requires_grad_(True)
+    yr = ref_mlp(xr)
+    yr.backward(dy_full.reshape(-1, d))
+    ref = {"y": yr.detach(), "dx": xr.grad, "dWf": ref_mlp.fused_proj.w.grad, "dWd": ref_mlp.down_proj.w.grad}
+    out = {"vs": "single-GPU GMLP on rank 0, same weights and inputs"}
+    for k in ("y", "dx", "dWf", "dWd"):
+        a, b = got[k].double().reshape(-1), ref[k].double().reshape(-1)
+        out[k] = {"max_rel": float((a - b).abs().max() / b.abs().max()),
+                  "cos": float(torch.dot(a, b) / (a.norm() * b.norm()))}
+    del ref_mlp
+    return out
+
+
 def run_ours(args, cfg, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -299,6 +344,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         return run_attn(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
+    if world > 1 and cfg.get("norm"):
+        raise SystemExit("the RMSNorm -> GMLP workload runs on one GPU")
     if world > 1:
         from macrogpt_jax_b200 import tp as tp_mod
         from macrogpt_jax_b200.tp import TPGMLP
@@ -311,16 +358,26 @@ def run_ours(args, cfg, rank, world, local_rank):
                             down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))(
             model_d=d, hidden_d=h, rngs=Rngs(0))
         assert mlp.fused()
+    block = mlp
+    if cfg.get("norm"):
+        from macrogpt_jax_b200.layer import norm_fusable, norm_mlp
+        from macrogpt_jax_b200.rmsnorm import RMSNorm
+        norm = RMSNorm(d, rngs=Rngs(1), device=dev)
+        assert norm_fusable(norm, mlp)
+        if args.norm_unfused:
+            block = lambda t: mlp(norm(t))  # noqa: E731
+        else:
+            block = lambda t: norm_mlp(norm, mlp, t)  # noqa: E731
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)  # identical activations on every rank (TP replicates x and dY)
     x_full = torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     dy_full = (torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32) * 1e-3).to(torch.bfloat16)
     x_in, dy_in = (mlp.shard_tokens(x_full), mlp.shard_tokens(dy_full)) if world > 1 else (x_full, dy_full)
-    params = list(mlp.parameters())
+    params = list(mlp.parameters()) + (list(norm.parameters()) if cfg.get("norm") else [])
 
     def step(xb, dyb):
         xl = xb.detach().requires_grad_(True)
-        y = mlp(xl)
+        y = block(xl)
         y.backward(dyb)
         for p in params:
             p.grad = None
@@ -394,7 +451,7 @@ def run_ours(args, cfg, rank, world, local_rank):
                 # y can leave for the host as soon as the forward has produced it, while the
                 # backward of the same step runs.
                 xl = xb.detach().requires_grad_(True)
-                y = mlp(xl)
+                y = block(xl)
                 y_ev = torch.cuda.Event()
                 y_ev.record()
                 y.backward(dyb)
@@ -412,6 +469,10 @@ def run_ours(args, cfg, rank, world, local_rank):
                "path": "GMLP module forward+backward; every step copies its x and dY from pinned host memory "
                        "(side stream, double-buffered: step i+1's inputs arrive while step i computes) and "
                        "reads its y back (side stream, overlapping the backward)"}
+
+    tp_parity = None
+    if world > 1 and not args.no_tp_parity:
+        tp_parity = tp_parity_check(mlp, x_full, dy_full, x_in, dy_in, d, h, rank, world, dev)
 
     if rank != 0:
         return None
@@ -454,6 +515,15 @@ def run_ours(args, cfg, rank, world, local_rank):
         "gpu_launches": launches,
         "clocks": clk,
     }
+    norm_parts = {k: summ[k] for k in ("norm_quant", "norm", "norm_bwd") if k in summ}
+    if norm_parts:
+        # algorithmic bytes: norm_quant 5 B/element (x twice, fp8 out), norm 4 B (x, bf16 y),
+        # norm_bwd 6 B (x, dy, dx)
+        out["roofline_norm"] = {k: {"bound": "hbm", "unit": "GB/s", "launches": n,
+                                    "achieved": b / (ms / 1000.0) / 1e9, "peak": peaks["hbm_gbs"],
+                                    "frac": b / (ms / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                                    "time_share": ms / eager_ms if eager_ms else None}
+                                for k, (n, ms, b) in norm_parts.items()}
     if args.graph:
         out["config"]["execution"] = "CUDA graph of the whole step (macrogpt_jax_b200.graphs.GraphedStep)"
         out["roofline"]["source"] = ("per-kernel CUDA events of an eager pass of the same step right after the "
@@ -461,6 +531,8 @@ def run_ours(args, cfg, rank, world, local_rank):
                                      f"is of that pass ({eager_ms / args.steps:.3f} ms/step eager)")
     if e2e:
         out["e2e"] = e2e
+    if tp_parity:
+        out["tp_parity"] = tp_parity
     if world == 1 and not args.no_cpu_baseline:
         samples = [(hs, cpu_oracle_step(d, hs, T, seed=k)) for k, hs in enumerate(CPU_SLICES)]
         step_s, a, b = fit_hidden(samples, h)
@@ -576,6 +648,10 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gmlp_d4096")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--norm-unfused", action="store_true",
+                    help="norm_gmlp_d4096: run RMSNorm and GMLP as separate modules (for comparison)")
+    ap.add_argument("--no-tp-parity", action="store_true",
+                    help="N > 1: skip the tensor-parallel vs single-GPU comparison printed as tp_parity")
     ap.add_argument("--gemm-traffic", type=float, default=None,
                     help="DRAM bytes per GEMM launch to report as roofline.traffic (default: the "
                          "captured figure for gmlp_d4096 on one GPU, else null)")
@@ -602,6 +678,12 @@ def main():
     else:
         args.config_desc = (f"GMLP fwd+bwd, {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
                             f"d_model {cfg['d']}, hidden {cfg['h']}, FP8 e4m3/e5m2")
+        if cfg.get("norm"):
+            args.config_desc = ("RMSNorm (uncentered) -> " + args.config_desc +
+                                ("; norm and GMLP as separate modules" if args.norm_unfused else
+                                 "; norm fused with the fp8 quantisation of its output"))
+            if args.impl == "reference":
+                raise SystemExit("the CPU arm covers the GMLP workloads")
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -111,6 +111,32 @@ int ufp8_amax_quant_noalloc(const void* x_bf16, int64_t n, int fmt, void* q, flo
  * float8_e5m2, round to nearest even with the ml_dtypes overflow rules. */
 int ufp8_cast(const void* x_bf16, int64_t n, int fmt, void* q, ufp8_stream_t stream);
 
+/* ---- RMSNorm fused with the fp8 quantisation of its output -------------------------------
+ * Replaces RMSNorm.__call__ (ueaj/model/rmsnorm.py:68-84) followed by the per-tensor cast of its
+ * output that the next FP8 Einsum makes (ueaj/model/layer.py:54,56: attn(attn_norm(x)),
+ * mlp(mlp_norm(x))).  x: [rows, d] bf16 with row pitch ldx.  scale: bf16, scale_len 1 or d
+ * (NULL: scale_mode 'none'); centered != 0 multiplies by 1 + scale ('centered' modes).
+ * Per row: r = 1 / sqrt(mean(x^2) + eps) in f32 (fixed summation order, see csrc/norm.cu),
+ * y = bf16((x * r) * w); rstd[row] = r (f32, kept for the backward).  If y_bf16 is not NULL, y
+ * is stored (pitch ldy).  If inv_scale is not NULL, amax = max|y| and q = fp8(y * FMAX/amax)
+ * ([rows, d] contiguous; q may be NULL only when rows == 0) with *inv_scale as ufp8_quantize
+ * writes it; amax alone may be asked for with inv_scale = NULL.  Two passes over x: 5 bytes of
+ * HBM traffic per element with the fp8 output. */
+int ufp8_rmsnorm_quant(const void* x_bf16, int64_t rows, int64_t d, int64_t ldx, const void* scale_bf16,
+                       int64_t scale_len, int centered, float eps, int fmt, void* q, float* amax, float* inv_scale,
+                       float* rstd, void* y_bf16, int64_t ldy, ufp8_stream_t stream);
+
+/* Backward of the RMSNorm above (the derivative JAX takes of ueaj/model/rmsnorm.py:68-84):
+ * dx = bf16(r * w * dy - x * r^3 * sum(dy * w * x) / d) per row, from the forward's rstd, and,
+ * when dscale (f32, scale_len entries) is not NULL, dscale = sum over rows of dy * x * r (summed
+ * over the row too for a one-element scale), deterministic: per-CTA partials in `workspace`
+ * (ufp8_rmsnorm_backward_workspace bytes), summed in CTA order.  d <= 8192. */
+int ufp8_rmsnorm_backward_workspace(int64_t rows, int64_t d, int64_t* bytes);
+int ufp8_rmsnorm_backward(const void* x_bf16, int64_t rows, int64_t d, int64_t ldx, const void* scale_bf16,
+                          int64_t scale_len, int centered, const float* rstd, const void* dy_bf16, int64_t lddy,
+                          void* dx_bf16, int64_t lddx, float* dscale, float* workspace, int64_t workspace_bytes,
+                          ufp8_stream_t stream);
+
 /* One fp8 operand of a GEMM.  Logical shape [rows, K] for A (rows = M) and for B
  * (rows = N); `major` says which index is contiguous in memory.  `ld` is the pitch in
  * elements between consecutive stored rows (K-major: >= K; MN-major: >= rows) and

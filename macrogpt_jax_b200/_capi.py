@@ -46,6 +46,9 @@ EXPORTED_SYMBOLS = (
     "ufp8_tp_local",
     "ufp8_tp_ag_push",
     "ufp8_amax_quant_noalloc",
+    "ufp8_rmsnorm_quant",
+    "ufp8_rmsnorm_backward_workspace",
+    "ufp8_rmsnorm_backward",
 )
 
 
@@ -138,11 +141,16 @@ def load() -> ctypes.CDLL:
     lib.ufp8_tp_allreduce_max.argtypes = [vp, vp, vp, i32, vp]
     lib.ufp8_tp_local.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
     lib.ufp8_tp_ag_push.argtypes = [vp, ctypes.c_uint64, i64, i32, vp]
+    f32 = ctypes.c_float
+    lib.ufp8_rmsnorm_quant.argtypes = [vp, i64, i64, i64, vp, i64, i32, f32, i32, vp, vp, vp, vp, vp, i64, vp]
+    lib.ufp8_rmsnorm_backward_workspace.argtypes = [i64, i64, ctypes.POINTER(i64)]
+    lib.ufp8_rmsnorm_backward.argtypes = [vp, i64, i64, i64, vp, i64, i32, vp, vp, i64, vp, i64, vp, vp, i64, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
                  "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
-                 "ufp8_tp_local", "ufp8_tp_ag_push"):
+                 "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
+                 "ufp8_rmsnorm_backward"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -182,6 +190,27 @@ def amax_quant_noalloc(x_ptr: int, n: int, fmt: int, q_ptr: int, inv_ptr: int, s
 def cast(x_ptr: int, n: int, fmt: int, q_ptr: int, stream: int) -> None:
     check(load().ufp8_cast(x_ptr, n, fmt, q_ptr, stream))
     _count(1 if n > 0 else 0)
+
+
+def rmsnorm_quant(x_ptr, rows, d, ldx, scale_ptr, scale_len, centered, eps, fmt, q_ptr, amax_ptr, inv_ptr,
+                  rstd_ptr, y_ptr, ldy, stream) -> None:
+    """ufp8_rmsnorm_quant: RMSNorm rows of x (rstd out), optional bf16 y, optional fp8 q."""
+    check(load().ufp8_rmsnorm_quant(x_ptr, rows, d, ldx, scale_ptr, scale_len, 1 if centered else 0, eps, fmt,
+                                    q_ptr, amax_ptr, inv_ptr, rstd_ptr, y_ptr, ldy, stream))
+    _count((1 if rows > 0 else 0) + (1 if inv_ptr else 0))
+
+
+def rmsnorm_backward_workspace(rows: int, d: int) -> int:
+    out = ctypes.c_int64(0)
+    check(load().ufp8_rmsnorm_backward_workspace(rows, d, ctypes.byref(out)))
+    return out.value
+
+
+def rmsnorm_backward(x_ptr, rows, d, ldx, scale_ptr, scale_len, centered, rstd_ptr, dy_ptr, lddy, dx_ptr, lddx,
+                     dscale_ptr, ws_ptr, ws_bytes, stream) -> None:
+    check(load().ufp8_rmsnorm_backward(x_ptr, rows, d, ldx, scale_ptr, scale_len, 1 if centered else 0, rstd_ptr,
+                                       dy_ptr, lddy, dx_ptr, lddx, dscale_ptr, ws_ptr, ws_bytes, stream))
+    _count((1 if (rows > 0 or dscale_ptr) else 0) + (1 if dscale_ptr else 0))
 
 
 def gemm(desc: GemmDesc, stream: int) -> None:

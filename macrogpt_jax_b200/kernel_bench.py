@@ -3,7 +3,7 @@
     python -m macrogpt_jax_b200.kernel_bench [--tokens T] [--d D] [--hidden H]
                                              [--gemms F1,F2,B2,B1,B4,B3] [--reps R] [--warmup W]
                                              [--variant V] [--seconds S] [--cublas]
-                                             [--quant | --rs-push]
+                                             [--quant | --norm | --rs-push]
 
 Each named GEMM of the GMLP step runs R times after W warm-up launches on seeded fp8
 operands; the script prints one line per GEMM with its mean duration and TFLOP/s.  With
@@ -193,6 +193,26 @@ def quant_bench(args, dev):
         del x
 
 
+def norm_bench(args, dev):
+    """RMSNorm on [tokens, d]: fused with the e4m3 quantisation (5 B/element), bf16 output
+    (4 B/element) and the backward with a vector scale (6 B/element); algorithmic GB/s."""
+    T, d = args.tokens, args.d
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    x = (torch.randn((T, d), generator=gen, device=dev) * 2).to(torch.bfloat16)
+    dy = (torch.randn((T, d), generator=gen, device=dev) * 1e-2).to(torch.bfloat16)
+    scale = (1 + 0.1 * torch.randn(d, generator=gen, device=dev)).to(torch.bfloat16)
+    _, rstd = ops.rmsnorm(x, scale, False, 1e-6)
+    n = T * d
+    res = {}
+    for kind, fn, nbytes in (("norm_quant", lambda: ops.rmsnorm_quant(x, scale, False, 1e-6, C.E4M3), 5 * n),
+                             ("norm", lambda: ops.rmsnorm(x, scale, False, 1e-6), 4 * n),
+                             ("norm_bwd", lambda: ops.rmsnorm_backward(x, scale, False, rstd, dy), 6 * n)):
+        us = _time_us(fn, args.reps, args.warmup)
+        res[kind] = {"us": us, "gbs": nbytes / us / 1e3}
+    print(json.dumps({"tokens": T, "d": d, **res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
@@ -206,6 +226,7 @@ def main():
     ap.add_argument("--cublas", action="store_true", help="also time cuBLAS fp8 GEMMs of the same shapes")
     ap.add_argument("--group-m", type=int, default=0, help="tile raster group (0 = library default)")
     ap.add_argument("--quant", action="store_true", help="time amax and quantize on the GMLP tensor sizes instead")
+    ap.add_argument("--norm", action="store_true", help="time the RMSNorm kernels on [tokens, d] instead")
     ap.add_argument("--rs-push", action="store_true",
                     help="time the TP-2/4/8 F2 and B4 GEMMs storing locally vs pushing rows to a peer GPU")
     args = ap.parse_args()
@@ -216,6 +237,8 @@ def main():
     torch.cuda.set_device(dev)
     if args.quant:
         return quant_bench(args, dev)
+    if args.norm:
+        return norm_bench(args, dev)
     if args.rs_push:
         return rs_push_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)

@@ -282,9 +282,16 @@ def gmlp_forward(x: torch.Tensor, wf: torch.Tensor, wd: torch.Tensor):
     Returns y [T, d] bf16 and the tensors the backward needs.
     """
     x = _check_bf16_cuda(x, "x")
+    return gmlp_forward_q(quantize(x, C.E4M3), wf, wd)
+
+
+def gmlp_forward_q(qx: Fp8Tensor, wf: torch.Tensor, wd: torch.Tensor):
+    """gmlp_forward from an already quantised input (e4m3 [T, d]), e.g. the fp8 output of
+    rmsnorm_quant."""
+    if qx.fmt != C.E4M3:
+        raise ValueError("gmlp_forward_q: the input must be float8_e4m3fn")
     wf = _check_bf16_cuda(wf, "wf")
     wd = _check_bf16_cuda(wd, "wd")
-    qx = quantize(x, C.E4M3)
     qwf = quantize(wf, C.E4M3)
     ug, hid, amax_h = gmlp_f1(qx, qwf)
     qh = quantize(hid, C.E4M3, amax_h)
@@ -309,3 +316,63 @@ def gmlp_backward(dy: torch.Tensor, saved, need_dx: bool = True, need_dw: bool =
 
 def device_status(clear: bool = True) -> int:
     return C.device_status(clear)
+
+
+# ----------------------------------------------------------------------------- RMSNorm
+# RMSNorm (ueaj/model/rmsnorm.py:68-84) on [rows, d] bf16 activations, alone (bf16 out) or fused
+# with the per-tensor fp8 quantisation of its output for the FP8 Einsum that consumes it.
+def _norm_scale(scale: torch.Tensor | None):
+    if scale is None:
+        return None, 0
+    s = _check_bf16_cuda(scale.reshape(-1), "rmsnorm scale")
+    return s, s.numel()
+
+
+def rmsnorm(x2d: torch.Tensor, scale: torch.Tensor | None, centered: bool, eps: float):
+    """(y bf16 [rows, d], rstd f32 [rows])."""
+    x2d = _check_bf16_cuda(x2d, "rmsnorm x")
+    rows, d = x2d.shape
+    s, slen = _norm_scale(scale)
+    y = torch.empty_like(x2d)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x2d.device)
+    _launch("norm", 4.0 * rows * d, lambda: C.rmsnorm_quant(
+        x2d.data_ptr(), rows, d, d, s.data_ptr() if s is not None else None, slen, centered, eps, 0, None, None,
+        None, rstd.data_ptr(), y.data_ptr(), d, _stream()))
+    return y, rstd
+
+
+def rmsnorm_quant(x2d: torch.Tensor, scale: torch.Tensor | None, centered: bool, eps: float, fmt: int):
+    """RMSNorm fused with the fp8 quantisation of its output: (Fp8Tensor of y, rstd).  The
+    algorithmic traffic is 5 B per element (x read twice, fp8 written)."""
+    x2d = _check_bf16_cuda(x2d, "rmsnorm x")
+    rows, d = x2d.shape
+    s, slen = _norm_scale(scale)
+    q = torch.empty((rows, d), dtype=FP8_DTYPE[fmt], device=x2d.device)
+    amax_t = torch.empty(1, dtype=torch.float32, device=x2d.device)
+    inv = torch.empty(1, dtype=torch.float32, device=x2d.device)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x2d.device)
+    _launch("norm_quant", 5.0 * rows * d, lambda: C.rmsnorm_quant(
+        x2d.data_ptr(), rows, d, d, s.data_ptr() if s is not None else None, slen, centered, eps, fmt,
+        q.data_ptr(), amax_t.data_ptr(), inv.data_ptr(), rstd.data_ptr(), None, 0, _stream()))
+    return Fp8Tensor(q, inv, amax_t), rstd
+
+
+def rmsnorm_backward(x2d: torch.Tensor, scale: torch.Tensor | None, centered: bool, rstd: torch.Tensor,
+                     dy2d: torch.Tensor, need_dscale: bool = True):
+    """(dx bf16 [rows, d], dscale f32 [scale elements] or None)."""
+    x2d = _check_bf16_cuda(x2d, "rmsnorm x")
+    dy2d = _check_bf16_cuda(dy2d, "rmsnorm dy")
+    rows, d = x2d.shape
+    s, slen = _norm_scale(scale)
+    dx = torch.empty_like(x2d)
+    dscale = ws = None
+    nbytes = 0
+    if s is not None and need_dscale:
+        dscale = torch.empty(slen, dtype=torch.float32, device=x2d.device)
+        nbytes = C.rmsnorm_backward_workspace(rows, d)
+        ws = torch.empty(nbytes // 4, dtype=torch.float32, device=x2d.device)
+    _launch("norm_bwd", 6.0 * rows * d, lambda: C.rmsnorm_backward(
+        x2d.data_ptr(), rows, d, d, s.data_ptr() if s is not None else None, slen, centered, rstd.data_ptr(),
+        dy2d.data_ptr(), d, dx.data_ptr(), d, dscale.data_ptr() if dscale is not None else None,
+        ws.data_ptr() if ws is not None else None, nbytes, _stream()))
+    return dx, dscale

@@ -13,7 +13,9 @@ What it restates (reference file:line, relative to the macrogpt-jax repository):
     ml_dtypes 0.5.4 (requirements.txt:38);
   * the per-tensor current-scaling recipe (amax -> s = FMAX/amax -> RNE(x*s), fp32
     accumulate, bf16 out), which the reference does not contain: it is the recipe the
-    FP8 mode is specified with, composed here from the primitives above.
+    FP8 mode is specified with, composed here from the primitives above;
+  * RMSNorm.__call__  ueaj/model/rmsnorm.py:68-84 (norm.py), with the summation order and
+    the rsqrt the CUDA kernel uses.
 
 Parity pinning:
   * fp8 cast bytes: pinned.  fp8.py's own round-to-nearest-even cast is checked against
@@ -22,4 +24,4 @@ Parity pinning:
     here (jax, flax, optax absent, no network) and the reference ships no golden vectors;
     these functions are restatements, checked against an independent einsum (torch) only.
 """
-from . import fp8, path  # noqa: F401
+from . import fp8, norm, path  # noqa: F401

@@ -76,6 +76,14 @@ def test_struct_layout_matches_header(tmp_path):
 
 @pytest.mark.parametrize("call,code,msg", [
     (lambda L: L.ufp8_gemm(None, None), C.ERR_INVALID, "null descriptor"),
+    (lambda L: L.ufp8_rmsnorm_quant(None, 4, 0, 0, None, 0, 0, 1e-6, 0, None, None, None, None, None, 0, None),
+     C.ERR_INVALID, "d > 0"),
+    (lambda L: L.ufp8_rmsnorm_quant(None, 0, 8, 8, None, 0, 0, 1e-6, 0, None, None, None, None, None, 0, None),
+     C.ERR_INVALID, "no output requested"),
+    (lambda L: L.ufp8_rmsnorm_backward(None, 1, 8, 8, None, 0, 0, None, None, 8, None, 8, None, None, 0, None),
+     C.ERR_INVALID, "null x"),
+    (lambda L: L.ufp8_rmsnorm_backward(ctypes.c_void_p(16), 1, 9000, 9000, None, 0, 0, None, None, 9000, None, 9000,
+                                       None, None, 0, None), C.ERR_UNSUPPORTED, "d 9000"),
     (lambda L: L.ufp8_amax(None, -1, None, None), C.ERR_INVALID, "n < 0"),
     (lambda L: L.ufp8_quantize(None, 4, 7, None, None, None, None), C.ERR_INVALID, "fmt 7"),
     (lambda L: L.ufp8_amax_quant(None, 4, 3, None, None, None, None), C.ERR_INVALID, "fmt 3"),

@@ -181,3 +181,69 @@ def test_threaded_passes_equal_numpy():
     assert np.array_equal(y, y_ref)
     for k in ("dx", "dwf", "dwd"):
         assert np.array_equal(g[k], g_ref[k]), k
+
+
+def test_norm_oracle_against_float64():
+    """The restated RMSNorm (fixed summation order, 1 / sqrt) is within one bf16 rounding of a
+    float64 evaluation of the reference formula, for every scale mode."""
+    from oracle import norm
+    rng = np.random.default_rng(9)
+    x = path.bf16_normal(rng, (37, 1000), 3.0)
+    xs = fp8.bf16_bits_to_f32(x).astype(np.float64)
+    r64 = 1.0 / np.sqrt((xs ** 2).mean(-1, keepdims=True) + 1e-6)
+    for scale, centered in ((None, False), (path.bf16_normal(rng, (1000,), 0.5), False),
+                            (path.bf16_normal(rng, (1000,), 0.5), True), (path.bf16_normal(rng, (1,)), False),
+                            (path.bf16_normal(rng, (1,)), True)):
+        y, r = norm.rmsnorm(x, scale, centered, 1e-6)
+        w = 1.0 if scale is None else fp8.bf16_bits_to_f32(scale).astype(np.float64)
+        w = 1.0 + w if centered else w
+        ref = xs * r64 * w
+        got = fp8.bf16_bits_to_f32(y).astype(np.float64)
+        assert np.allclose(r, r64[:, 0], rtol=1e-6)
+        assert np.all(np.abs(got - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-30)
+
+
+def test_norm_oracle_summation_order():
+    """row_sumsq follows the kernel's order exactly: equal to a per-lane loop written out."""
+    from oracle import norm
+    rng = np.random.default_rng(10)
+    x = (rng.standard_normal((3, 300)) * 10).astype(np.float32)
+    got = norm.row_sumsq(x)
+    for r in range(3):
+        lanes = []
+        for lane in range(32):
+            acc = np.float32(0)
+            for c in range(lane, 38, 32):
+                for j in range(8):
+                    e = 8 * c + j
+                    v = x[r, e] if e < 300 else np.float32(0)
+                    acc = np.float32(acc + np.float32(v * v))
+            lanes.append(acc)
+        for o in (16, 8, 4, 2, 1):
+            lanes = [np.float32(lanes[i] + lanes[i ^ o]) for i in range(32)]
+        assert got[r] == lanes[0]
+
+
+def test_norm_backward_oracle_matches_autograd():
+    """The float64 RMSNorm derivative against torch autograd of the same formula."""
+    from oracle import norm
+    rng = np.random.default_rng(11)
+    x = path.bf16_normal(rng, (5, 64))
+    g = path.bf16_normal(rng, (5, 64))
+    for scale, centered in ((path.bf16_normal(rng, (64,), 0.5), False), (path.bf16_normal(rng, (64,), 0.5), True),
+                            (path.bf16_normal(rng, (1,)), False), (None, False)):
+        _, r = norm.rmsnorm(x, scale, centered)
+        dx, dw = norm.rmsnorm_backward(x, scale, centered, r, g)
+        xt = torch.tensor(fp8.bf16_bits_to_f32(x), dtype=torch.float64, requires_grad=True)
+        st = None
+        if scale is not None:
+            st = torch.tensor(fp8.bf16_bits_to_f32(scale), dtype=torch.float64, requires_grad=True)
+        rr = torch.rsqrt((xt ** 2).mean(-1, keepdim=True) + 1e-6)
+        w = 1.0 if st is None else (1.0 + st if centered else st)
+        (xt * rr * w).backward(torch.tensor(fp8.bf16_bits_to_f32(g), dtype=torch.float64))
+        # the oracle takes r from the f32 forward; the bound allows for that rounding
+        ref_dx = xt.grad.numpy()
+        assert np.allclose(dx, ref_dx, rtol=1e-5, atol=1e-5 * np.abs(ref_dx).max())
+        if scale is not None:
+            ref_dw = st.grad.numpy().reshape(-1)
+            assert np.allclose(dw, ref_dw, rtol=1e-5, atol=1e-5 * np.abs(ref_dw).max())
