@@ -54,5 +54,40 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return LIB_PATH
 
 
+XLA_LIB_PATH = LIB_DIR / "libufp8_xla.so"
+
+
+def jax_ffi_include_dir() -> str | None:
+    """jaxlib's XLA FFI header directory, or None when JAX is not installed."""
+    try:
+        import jax.ffi  # noqa: F401
+        return jax.ffi.include_dir()
+    except Exception:  # noqa: BLE001  (absent or too old a jax: no XLA binding)
+        return None
+
+
+def build_xla_ffi(force: bool = False) -> Path | None:
+    """Compiles csrc/xla_ffi.cc (the XLA custom-call handlers) into lib/libufp8_xla.so, linked
+    to libufp8.so, when jaxlib's headers are available; returns None (and builds nothing)
+    otherwise.  The reference registers the handlers with jax.ffi.register_ffi_target."""
+    inc = jax_ffi_include_dir()
+    if inc is None:
+        return None
+    lib = build()
+    src = CSRC / "xla_ffi.cc"
+    if not force and XLA_LIB_PATH.exists() and XLA_LIB_PATH.stat().st_mtime > max(src.stat().st_mtime,
+                                                                                   lib.stat().st_mtime):
+        return XLA_LIB_PATH
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-I{inc}", f"-I{INCLUDE}", f"-I{cuda_home}/include",
+           "-o", str(XLA_LIB_PATH), str(src), f"-L{LIB_DIR}", "-lufp8", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed ({res.returncode}):\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return XLA_LIB_PATH
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    xla = build_xla_ffi(force="--force" in sys.argv)
+    print(xla if xla is not None else "libufp8_xla.so skipped: jaxlib headers (jax.ffi.include_dir) not found")

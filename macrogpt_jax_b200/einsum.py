@@ -208,6 +208,7 @@ class Einsum(torch.nn.Module):
         self.static_scale = static_scale
         self.sharding = sharding
         self.mesh = mesh
+        self.shard = None  # (canonical dim, rank, ranks) once reshard() has sliced the weight
         if fwd_dtype not in ops.FMT_OF_DTYPE or bwd_dtype not in ops.FMT_OF_DTYPE:
             raise ValueError("fwd_dtype / bwd_dtype must be float8_e4m3fn or float8_e5m2")
         self.fwd_dtype, self.bwd_dtype = fwd_dtype, bwd_dtype
@@ -241,12 +242,40 @@ class Einsum(torch.nn.Module):
         return {"w": self.metadata}
 
     def reshard(self, mesh) -> None:
-        """Records the mesh; the weight keeps its layout (sharded layers live in tp.py)."""
+        """Applies the layer's sharding spec on `mesh` (ueaj/model/einsum.py:257-278).
+
+        The reference places the weight under a NamedSharding; here the weight itself becomes
+        this rank's shard: along the canonical dimension the spec marks 'tensor', the rank of
+        the mesh's tensor axis keeps its contiguous 1/k slice, and `size_dict` and `metadata`
+        describe the local shard.  The layer then computes its local part of the contraction:
+        a split output dimension gives this rank's output columns, a split reducing dimension
+        a partial sum over this rank's slice of the input (the block that owns the layer
+        gathers or reduces, as tp.py does for GMLP).  Without a tensor axis of more than one
+        rank, or without 'tensor' in the spec, only the mesh is recorded."""
+        from .tp import tensor_group
+        import torch.distributed as dist
         sharding = self.sharding if self.sharding is not None else (None,) * len(self.metadata.canonical_shape)
         if len(sharding) != len(self.metadata.canonical_shape):
             raise ValueError(f"Sharding spec length {len(sharding)} doesn't match "
                              f"weight dimensions {len(self.metadata.canonical_shape)}")
         self.mesh = mesh
+        group = tensor_group(mesh)
+        if group is None or "tensor" not in sharding:
+            return
+        if getattr(self, "shard", None) is not None:
+            raise ValueError("reshard: the weight is already sharded")
+        dim = sharding.index("tensor")
+        k, r = dist.get_world_size(group), dist.get_rank(group)
+        size = self.w.shape[dim]
+        if size % k:
+            raise ValueError(f"reshard: dimension {dim} of size {size} is not divisible by the tensor axis ({k})")
+        local = size // k
+        letter = self.weight_expr[dim]  # the weight is stored in weight_expr order
+        with torch.no_grad():
+            self.w = torch.nn.Parameter(self.w.detach().narrow(dim, r * local, local).contiguous())
+        self.size_dict = {**self.size_dict, letter: local}
+        self.metadata = compute_weight_metadata(self.weight_expr, self.output_expr, self.batch_dims, self.size_dict)
+        self.shard = (dim, r, k)
 
 
 FP8Einsum = Einsum

@@ -71,22 +71,50 @@ class GMLP(torch.nn.Module):
 
     def __init__(self, model_d: int, hidden_d: Optional[int] = None, activation_fn: Callable = swish,
                  param_dtype: torch.dtype = torch.bfloat16, fused_proj: Callable = Einsum,
-                 down_proj: Callable = Einsum, *, rngs: Rngs, mesh=None):
+                 down_proj: Callable = Einsum, *, rngs: Rngs, mesh=None, tp_backend=None):
+        """With a `mesh` whose 'tensor' axis has k > 1 ranks (a DeviceMesh with a 'tensor'
+        dimension, or a ProcessGroup), the block is tensor-parallel exactly as the reference's
+        sharding annotations declare it (mlp.py:85,96: gate/up split over hidden, down over its
+        input): the projection factories build the full weights, every rank keeps its slice,
+        `fused_proj` / `down_proj` are the local shards, and forward takes and returns this
+        rank's token shard (ueaj/model/layer.py:57), running tp.TPGMLP's NVLink schedule.
+        `tp_backend` replaces the CUDA ops there (tests run the host logic on CPU ranks)."""
         super().__init__()
         hidden_d = 4 * model_d if hidden_d is None else hidden_d
-        self.fused_proj = fused_proj("bnd,idh->ibnh", size_dict={"d": model_d, "h": hidden_d, "i": 2},
-                                     batch_dims="i", rngs=rngs, dtype=param_dtype, mesh=mesh,
-                                     sharding=(None, None, "tensor"))
-        self.down_proj = down_proj("bnh,hd->bnd", initializer=zeros_init, size_dict={"d": model_d, "h": hidden_d},
-                                   rngs=rngs, dtype=param_dtype, mesh=mesh, sharding=("tensor", None))
         self.activation_fn = activation_fn
         self.model_d, self.hidden_d = model_d, hidden_d
+        self._tp = None
+        from .tp import TPGMLP, tensor_group
+        group = tensor_group(mesh)
+        make_kw = {"device": torch.device("cpu")} if group is not None else {}
+        fused = fused_proj("bnd,idh->ibnh", size_dict={"d": model_d, "h": hidden_d, "i": 2},
+                           batch_dims="i", rngs=rngs, dtype=param_dtype, mesh=mesh,
+                           sharding=(None, None, "tensor"), **make_kw)
+        down = down_proj("bnh,hd->bnd", initializer=zeros_init, size_dict={"d": model_d, "h": hidden_d},
+                         rngs=rngs, dtype=param_dtype, mesh=mesh, sharding=("tensor", None), **make_kw)
+        if group is None:
+            self.fused_proj, self.down_proj = fused, down
+            return
+        if not (_is_fp8_einsum(fused) and _is_fp8_einsum(down)) or activation_fn is not swish:
+            raise NotImplementedError("the tensor-parallel GMLP runs the fused FP8 block: FP8 Einsum "
+                                      "projections with swish gating")
+        self._tp = TPGMLP(model_d, hidden_d, swish, param_dtype, rngs=Rngs(0), group=group, backend=tp_backend,
+                          full_weights=(fused.w.detach(), down.w.detach()))
+        self.fused_proj, self.down_proj = self._tp.fused_proj, self._tp.down_proj
+
+    def shard_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's token block of a full activation (tensor-parallel blocks only)."""
+        if self._tp is None:
+            raise ValueError("shard_tokens: this GMLP is not tensor-parallel")
+        return self._tp.shard_tokens(x)
 
     def fused(self) -> bool:
         """True when forward runs as the single fused FP8 GMLP (see module docstring)."""
         return self.activation_fn is swish and _is_fp8_einsum(self.fused_proj) and _is_fp8_einsum(self.down_proj)
 
     def forward(self, x):
+        if self._tp is not None:
+            return self._tp(x)
         if self.fused() and x.dtype not in LOW_PRECISION:
             lead = x.shape[:-1]
             wf = self.fused_proj.w

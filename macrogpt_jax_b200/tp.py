@@ -44,6 +44,26 @@ from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 AG_ENGINE = C.AG_COPY_ENGINE
 
 
+def tensor_group(mesh):
+    """The process group of the 'tensor' axis of `mesh` (ueaj/model/mlp.py:85,96 and
+    ueaj/model/einsum.py:218-220 shard weights over that axis), or None when there is no such
+    axis or it has a single rank.  `mesh` may be a torch DeviceMesh with a dimension named
+    'tensor' or a ProcessGroup (taken as the tensor axis); anything else (None, or a mesh
+    description this package does not run on, which layers only record) has no tensor axis."""
+    if mesh is None or not dist.is_available() or not dist.is_initialized():
+        return None
+    if hasattr(mesh, "mesh_dim_names") and hasattr(mesh, "get_group"):
+        names = tuple(mesh.mesh_dim_names or ())
+        if "tensor" not in names:
+            return None
+        group = mesh.get_group("tensor")
+    elif isinstance(mesh, dist.ProcessGroup):
+        group = mesh
+    else:
+        return None
+    return group if dist.get_world_size(group) > 1 else None
+
+
 class _DeviceBytes:
     """A raw device allocation seen through __cuda_array_interface__ (no ownership)."""
 
@@ -310,10 +330,14 @@ class TPGMLP(torch.nn.Module):
 
     def __init__(self, model_d: int, hidden_d: Optional[int] = None, activation_fn: Callable = None,
                  param_dtype: torch.dtype = torch.bfloat16, *, rngs: Rngs, mesh=None, group=None, device=None,
-                 fused_init=lecun_normal_init, down_init=zeros_init, backend=None, fused_reduce_scatter: bool = True):
+                 fused_init=lecun_normal_init, down_init=zeros_init, backend=None, fused_reduce_scatter: bool = True,
+                 full_weights=None):
+        """`full_weights` = (wf [2, d, h], wd [h, d]) replaces the construction of the full weights
+        from `rngs` (GMLP passes the weights its own projection factories built)."""
         super().__init__()
         hidden_d = 4 * model_d if hidden_d is None else hidden_d
-        group = group if group is not None else mesh
+        if group is None and mesh is not None:
+            group = tensor_group(mesh) or (mesh if isinstance(mesh, dist.ProcessGroup) else None)
         if hidden_d % dist.get_world_size(group):
             raise ValueError(f"hidden {hidden_d} is not divisible by the tensor-parallel size "
                              f"{dist.get_world_size(group)}")
@@ -326,10 +350,14 @@ class TPGMLP(torch.nn.Module):
         hl = hidden_d // k
         self.model_d, self.hidden_d, self.hidden_local = model_d, hidden_d, hl
         cpu = torch.device("cpu")
-        full_f = Einsum("bnd,idh->ibnh", initializer=fused_init, size_dict={"d": model_d, "h": hidden_d, "i": 2},
-                        batch_dims="i", rngs=rngs, dtype=param_dtype, sharding=(None, None, "tensor"), device=cpu)
-        full_d = Einsum("bnh,hd->bnd", initializer=down_init, size_dict={"d": model_d, "h": hidden_d}, rngs=rngs,
-                        dtype=param_dtype, sharding=("tensor", None), device=cpu)
+        if full_weights is None:
+            full_wf = Einsum("bnd,idh->ibnh", initializer=fused_init, size_dict={"d": model_d, "h": hidden_d, "i": 2},
+                             batch_dims="i", rngs=rngs, dtype=param_dtype, sharding=(None, None, "tensor"),
+                             device=cpu).w
+            full_wd = Einsum("bnh,hd->bnd", initializer=down_init, size_dict={"d": model_d, "h": hidden_d},
+                             rngs=rngs, dtype=param_dtype, sharding=("tensor", None), device=cpu).w
+        else:
+            full_wf, full_wd = full_weights
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else cpu
         # Local shards as Einsum layers over the local hidden width, so optimisers that read
@@ -340,8 +368,8 @@ class TPGMLP(torch.nn.Module):
         self.down_proj = Einsum("bnh,hd->bnd", initializer=zeros_init, size_dict={"d": model_d, "h": hl},
                                 rngs=Rngs(0), dtype=param_dtype, sharding=("tensor", None), device=device)
         with torch.no_grad():
-            self.fused_proj.w.copy_(full_f.w[:, :, r * hl:(r + 1) * hl])
-            self.down_proj.w.copy_(full_d.w[r * hl:(r + 1) * hl, :])
+            self.fused_proj.w.copy_(full_wf[:, :, r * hl:(r + 1) * hl])
+            self.down_proj.w.copy_(full_wd[r * hl:(r + 1) * hl, :])
 
     def shard_tokens(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's contiguous token block of a full [..., d] activation, as [T/k, d]."""

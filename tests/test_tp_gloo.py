@@ -110,3 +110,66 @@ def test_missing_rank_fails_fast():
     p.join(60)
     assert not p.is_alive()
     assert q.get(timeout=5) != "joined"
+
+
+def _mesh_worker(rank, world, port, outdir):
+    """The reference's own drop-in: GMLP.override(...)(..., mesh=<tensor group>) builds the
+    tensor-parallel block; and Einsum.reshard(mesh) slices a weight along its 'tensor' axis."""
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from cpu_backend import CpuBackend
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.mlp import GMLP
+    from oracle import path as op
+    group = dist.new_group(list(range(world)))
+    m = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5)),
+                      down_proj=Einsum.override(initializer=scaled_normal_init(H ** -0.5)))(
+        D, H, rngs=Rngs(5), mesh=group, tp_backend=CpuBackend())
+    assert tuple(m.fused_proj.w.shape) == (2, D, H // world) and tuple(m.down_proj.w.shape) == (H // world, D)
+    rng = np.random.default_rng(0)
+    xb = op.bf16_normal(rng, (T, D))
+    dyb = op.bf16_normal(rng, (T, D), 1e-3)
+    to_t = lambda b: torch.from_numpy(b.view(np.int16)).view(torch.bfloat16)  # noqa: E731
+    x = m.shard_tokens(to_t(xb)).requires_grad_(True)
+    y = m(x)
+    y.backward(m.shard_tokens(to_t(dyb)))
+    bits = lambda t: t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    e = Einsum("bnd,dh->bnh", initializer=scaled_normal_init(0.1), size_dict={"d": D, "h": H}, rngs=Rngs(9),
+               sharding=(None, "tensor"), device=torch.device("cpu"))
+    full_e = bits(e.w)
+    e.reshard(group)
+    assert e.shard == (1, rank, world) and e.size_dict["h"] == H // world
+    assert e.metadata.canonical_shape == (D, H // world)
+    np.savez(os.path.join(outdir, f"mesh{rank}.npz"), y=bits(y), dx=bits(x.grad), dwf=bits(m.fused_proj.w.grad),
+             dwd=bits(m.down_proj.w.grad), e_full=full_e, e_local=bits(e.w))
+    dist.destroy_process_group()
+
+
+def test_gmlp_with_mesh_is_tensor_parallel(tmp_path):
+    from helpers import bf16_bits_to_f64, compare
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.mlp import GMLP
+    from oracle import path as op
+    mp.spawn(_mesh_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    r = [np.load(tmp_path / f"mesh{i}.npz") for i in range(2)]
+    full = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5)),
+                         down_proj=Einsum.override(initializer=scaled_normal_init(H ** -0.5)))(
+        D, H, rngs=Rngs(5))
+    bits = lambda t: t.detach().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    wf, wd = bits(full.fused_proj.w), bits(full.down_proj.w)
+    rng = np.random.default_rng(0)
+    xb = op.bf16_normal(rng, (T, D))
+    dyb = op.bf16_normal(rng, (T, D), 1e-3)
+    y, saved = op.gmlp_forward(xb, wf, wd)
+    g = op.gmlp_backward(dyb, saved)
+    f = bf16_bits_to_f64
+    compare(f(np.concatenate([r[0]["y"], r[1]["y"]])), f(y))
+    compare(f(np.concatenate([r[0]["dx"], r[1]["dx"]])), f(g["dx"]))
+    compare(f(np.concatenate([r[0]["dwf"], r[1]["dwf"]], axis=2)), f(g["dwf"]))
+    compare(f(np.concatenate([r[0]["dwd"], r[1]["dwd"]], axis=0)), f(g["dwd"]))
+    # reshard: each rank holds its contiguous column block of the same full weight
+    assert (r[0]["e_full"] == r[1]["e_full"]).all()
+    assert (np.concatenate([r[0]["e_local"], r[1]["e_local"]], axis=1) == r[0]["e_full"]).all()
