@@ -40,7 +40,8 @@ CONFIGS = {
     "attn_d2048": dict(kind="attn", d=2048, heads=16, head_d=128, B=16, S=1024),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
-GMLP_D4096_GEMM_TRAFFIC = 1.999e9  # DRAM bytes per GEMM launch, T 16384 / d 4096 / h 14336, ncu
+GMLP_D4096_GEMM_TRAFFIC = 1.651e9  # DRAM bytes per GEMM launch, T 16384 / d 4096 / h 14336, from one ncu
+# capture of kernel_bench with this build's kernels (profiles/gemm_dram_traffic_d4096_t16384.md)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -482,7 +483,9 @@ def run_ours(args, cfg, rank, world, local_rank):
     if traffic is None and args.config == "gmlp_d4096" and world == 1:
         # Mean dram__bytes_read.sum + dram__bytes_write.sum per GEMM launch over the six
         # contractions of this workload, from one ncu capture of kernel_bench at these sizes.
-        traffic, traffic_src = GMLP_D4096_GEMM_TRAFFIC, "ncu capture, mean of the six GEMMs of this workload"
+        traffic, traffic_src = GMLP_D4096_GEMM_TRAFFIC, ("past ncu capture (not measured by this run): mean "
+                                                         "dram__bytes_read + write of the six GEMMs of this workload, "
+                                                         "kernel_bench at these sizes")
     tokens_s = T * args.steps / (ms / 1000.0)
     tflops_gpu = fl * args.steps / (ms / 1000.0) / world / 1e12
     g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
