@@ -41,7 +41,7 @@ extern "C" {
 
 typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 
-#define UFP8_ABI_VERSION 3
+#define UFP8_ABI_VERSION 4
 
 /* return codes */
 #define UFP8_OK 0
@@ -58,6 +58,7 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 /* fp8 formats (values match the MMA instruction-descriptor encoding) */
 #define UFP8_E4M3 0 /* float8_e4m3fn: forward operands, max 448   */
 #define UFP8_E5M2 1 /* float8_e5m2:   gradients,        max 57344 */
+#define UFP8_BF16 2 /* unquantised bf16 (output format of ufp8_xent_backward only) */
 
 /* operand storage order */
 #define UFP8_K_MAJOR 0  /* stored [rows = M or N][K], K contiguous   */
@@ -72,6 +73,7 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_EPI_SWIGLU 1  /* D[0]=U, D[1]=G, H = U * silu(G), amax_out = max|H|          */
 #define UFP8_EPI_DSWIGLU 2 /* dH = acc*sa*sb; D[0]=dU, D[1]=dG from saved U,G; amax |dUG| */
 #define UFP8_EPI_RS_PUSH 3 /* D rows stored into their owner rank's reduce-scatter staging slot */
+#define UFP8_EPI_XENT 4    /* D = logits (bf16, optionally soft-capped) + per-row softmax partials  */
 
 const char* ufp8_last_error(void);
 int ufp8_abi_version(void);
@@ -192,9 +194,51 @@ typedef struct ufp8_gemm_desc {
   uint32_t ag_epoch;
   int32_t ag_rank;
   int64_t ag_rows_per_rank;
+  /* XENT (CTA-pair kernel, bf16 D, batch 1): D receives the logits l = bf16(acc * sa * sb), or,
+   * with xent_cap > 0, c = bf16(cap * bf16(tanh(bf16(l / cap)))) (the soft cap of
+   * ueaj/model/model.py:162-163 with bf16 rounding after each operation).  For every row and
+   * every group of 128 columns [128 j, 128 j + 128) that holds a column < N, the pair
+   * (m, s) = (max c, sum exp(c - m)) over the group's columns < N is written as two f32 at
+   * xent_stats + 2 * (row * xent_ld_stats + j); xent_ld_stats >= ceil(N / 128). */
+  float* xent_stats;
+  int64_t xent_ld_stats;
+  float xent_cap;
+  int32_t xent_reserved;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);
+
+/* ---- next-token cross-entropy on the lm_head logits ---------------------------------------
+ * Replaces the loss of chunked_softmax_cross_entropy (ueaj/opt/next_token_loss.py:99-174):
+ * optax.softmax_cross_entropy_with_integer_labels on each chunk's logits, times the loss mask.
+ * Logits: [rows, V] bf16 with row pitch ldl (the capped values when the model soft-caps them).
+ * labels: int32 [rows]; a negative label counts from the end (as jnp.take_along_axis normalises
+ * it) and a label outside [-V, V) has no column.  mask: uint8 [rows] multiplied into the loss
+ * (NULL = all ones).  Per row, in f32: M = max_j c_j, lse = M + log(sum_j exp(c_j - M)),
+ * loss = (lse - c[label]) * mask (NaN for a label without a column, as the reference's fill-mode
+ * gather gives), qrow = 1 - exp(c[label] - lse) (1 without a column): the largest
+ * |softmax_j - onehot_j| of the row, which the backward's fp8 scale uses. */
+int ufp8_xent_forward(const void* logits_bf16, int64_t rows, int64_t V, int64_t ldl, const int32_t* labels,
+                      const uint8_t* mask, float* lse, float* loss, float* qrow, ufp8_stream_t stream);
+
+/* The same per-row results from the partials of a UFP8_EPI_XENT GEMM (stats, pitch ld_stats in
+ * pairs, ceil(V / 128) groups per row): the logits are read only at the labels. */
+int ufp8_xent_combine(const float* stats, int64_t ld_stats, const void* logits_bf16, int64_t rows, int64_t V,
+                      int64_t ldl, const int32_t* labels, const uint8_t* mask, float* lse, float* loss, float* qrow,
+                      ufp8_stream_t stream);
+
+/* Backward of the loss above (JAX's derivative of the per-token loss, with the soft cap's):
+ * g_r = dloss[r] * mask[r] (dloss NULL = all ones), dl_rj = g_r * (exp(c_rj - lse_r) - [j == label_r]),
+ * times (1 - (c_rj * (1 / cap))^2) when cap > 0 (tanh' from the stored capped value).
+ * fmt UFP8_BF16: dl stored as bf16 [rows, V] (pitch ldo); amax / inv_scale unused.
+ * fmt UFP8_E4M3 / UFP8_E5M2: amax = max_r |g_r| * qrow_r, which equals max |dl| when cap == 0 (the
+ * label column holds each row's largest |softmax - onehot|, computed with the same operations) and
+ * bounds it otherwise; then s = FMAX / amax as ufp8_quantize derives it, q = fp8(dl * s), and
+ * *amax, *inv_scale as ufp8_quantize writes them.  Two launches, 3 bytes of HBM traffic per
+ * element with the fp8 output. */
+int ufp8_xent_backward(const void* logits_bf16, int64_t rows, int64_t V, int64_t ldl, const int32_t* labels,
+                       const uint8_t* mask, const float* lse, const float* qrow, const float* dloss, float cap,
+                       int fmt, void* dlogits, int64_t ldo, float* amax, float* inv_scale, ufp8_stream_t stream);
 
 /* ---- tensor-parallel reduce-scatter over NVLink peer memory ------------------------------
  * Replaces the reduce-scatter XLA/GSPMD would insert after the row-split down projection of

@@ -16,9 +16,10 @@ STATUS_WAIT_TIMEOUT, STATUS_PEER_TIMEOUT = 1, 2
 IPC_HANDLE_BYTES = 64
 AG_COPY_ENGINE, AG_SM = 0, 1
 E4M3, E5M2 = 0, 1
+BF16 = 2  # unquantised output of ufp8_xent_backward
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
-EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH = 0, 1, 2, 3
+EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH, EPI_XENT = 0, 1, 2, 3, 4
 GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE, GEMM_CTA_PAIR_N512 = (
     0, 1, 2, 3, 4, 5)
 
@@ -49,6 +50,9 @@ EXPORTED_SYMBOLS = (
     "ufp8_rmsnorm_quant",
     "ufp8_rmsnorm_backward_workspace",
     "ufp8_rmsnorm_backward",
+    "ufp8_xent_forward",
+    "ufp8_xent_combine",
+    "ufp8_xent_backward",
 )
 
 
@@ -93,6 +97,10 @@ class GemmDesc(ctypes.Structure):
         ("ag_epoch", ctypes.c_uint32),
         ("ag_rank", ctypes.c_int32),
         ("ag_rows_per_rank", ctypes.c_int64),
+        ("xent_stats", ctypes.c_void_p),
+        ("xent_ld_stats", ctypes.c_int64),
+        ("xent_cap", ctypes.c_float),
+        ("xent_reserved", ctypes.c_int32),
     ]
 
 
@@ -145,12 +153,15 @@ def load() -> ctypes.CDLL:
     lib.ufp8_rmsnorm_quant.argtypes = [vp, i64, i64, i64, vp, i64, i32, f32, i32, vp, vp, vp, vp, vp, i64, vp]
     lib.ufp8_rmsnorm_backward_workspace.argtypes = [i64, i64, ctypes.POINTER(i64)]
     lib.ufp8_rmsnorm_backward.argtypes = [vp, i64, i64, i64, vp, i64, i32, vp, vp, i64, vp, i64, vp, vp, i64, vp]
+    lib.ufp8_xent_forward.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, vp]
+    lib.ufp8_xent_combine.argtypes = [vp, i64, vp, i64, i64, i64, vp, vp, vp, vp, vp, vp]
+    lib.ufp8_xent_backward.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, f32, i32, vp, i64, vp, vp, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
                  "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
                  "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
-                 "ufp8_rmsnorm_backward"):
+                 "ufp8_rmsnorm_backward", "ufp8_xent_forward", "ufp8_xent_combine", "ufp8_xent_backward"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -211,6 +222,29 @@ def rmsnorm_backward(x_ptr, rows, d, ldx, scale_ptr, scale_len, centered, rstd_p
     check(load().ufp8_rmsnorm_backward(x_ptr, rows, d, ldx, scale_ptr, scale_len, 1 if centered else 0, rstd_ptr,
                                        dy_ptr, lddy, dx_ptr, lddx, dscale_ptr, ws_ptr, ws_bytes, stream))
     _count((1 if (rows > 0 or dscale_ptr) else 0) + (1 if dscale_ptr else 0))
+
+
+def xent_forward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, loss_ptr, qrow_ptr, stream) -> None:
+    """ufp8_xent_forward: per-row lse, masked loss and qrow from bf16 logits."""
+    check(load().ufp8_xent_forward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, loss_ptr, qrow_ptr,
+                                   stream))
+    _count(1 if rows > 0 else 0)
+
+
+def xent_combine(stats_ptr, ld_stats, logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, loss_ptr, qrow_ptr,
+                 stream) -> None:
+    """ufp8_xent_combine: the per-row results from the partials of a UFP8_EPI_XENT GEMM."""
+    check(load().ufp8_xent_combine(stats_ptr, ld_stats, logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr,
+                                   loss_ptr, qrow_ptr, stream))
+    _count(1 if rows > 0 else 0)
+
+
+def xent_backward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, qrow_ptr, dloss_ptr, cap, fmt, out_ptr,
+                  ldo, amax_ptr, inv_ptr, stream) -> None:
+    """ufp8_xent_backward: dlogits (fp8 with its per-tensor scale, or bf16)."""
+    check(load().ufp8_xent_backward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, qrow_ptr, dloss_ptr,
+                                    cap, fmt, out_ptr, ldo, amax_ptr, inv_ptr, stream))
+    _count((1 if fmt != BF16 else 0) + (1 if rows > 0 else 0))
 
 
 def gemm(desc: GemmDesc, stream: int) -> None:

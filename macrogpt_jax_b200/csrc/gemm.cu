@@ -22,6 +22,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 
 #include "internal.h"
@@ -77,6 +78,9 @@ struct GemmArgs {
   uint32_t ag_epoch;
   int ag_rank;
   long long ag_rows;
+  float* xent_stats;  // XENT: per-row (max, sum exp) of each 128-column group
+  long long xent_ld;
+  float xent_cap;     // XENT: soft cap (0 = none)
 };
 
 // Waits until the all-gather block of rank s has arrived (flag == epoch), bounded like the
@@ -571,6 +575,40 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 __device__ __forceinline__ float lo_f(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_f(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+// XENT epilogue, one 32-column chunk of a row (bf16 logits packed in o[]): applies the soft cap
+// c = bf16(cap * bf16(tanh(bf16(l / cap)))) when cap > 0 (bf16 rounding after each operation, as
+// the reference's bf16 expression 15 * jnp.tanh(logits / 15) computes it), then folds the chunk's
+// columns below `valid` into the running softmax partials (m = max c, s = sum exp(c - m)),
+// rescaling s when the maximum grows.  exp is the MUFU approximation (a few ulp).  A NaN logit
+// leaves m alone and makes s NaN, so the row's loss becomes NaN.
+__device__ __forceinline__ void xent_chunk(uint32_t (&o)[16], int valid, float cap, float& m, float& s) {
+  if (cap > 0.0f) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float t0 = bf16_round(tanhf(bf16_round(__fdiv_rn(lo_f(o[j]), cap))));
+      const float t1 = bf16_round(tanhf(bf16_round(__fdiv_rn(hi_f(o[j]), cap))));
+      o[j] = pack_bf16x2(cap * t0, cap * t1);
+    }
+  }
+  float cm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (2 * j < valid) cm = fmaxf(cm, lo_f(o[j]));
+    if (2 * j + 1 < valid) cm = fmaxf(cm, hi_f(o[j]));
+  }
+  if (cm > m) {
+    s = s * __expf(m - cm);  // m = -inf on the first chunk: s = 0 * 0
+    m = cm;
+  }
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (2 * j < valid) acc += __expf(lo_f(o[j]) - m);
+    if (2 * j + 1 < valid) acc += __expf(hi_f(o[j]) - m);
+  }
+  s += acc;
+}
+
 // Loads 16 consecutive bf16 values packed two per word; elements at or past `valid` read 0.
 __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint32_t (&w)[8], int valid,
                                                     bool vec) {
@@ -929,8 +967,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
           }
         }
-      } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH) {
+      } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH || args.mode == UFP8_EPI_XENT) {
         // RS_PUSH: this row goes to its owner's staging slot for this rank (peer memory).
+        // XENT: bf16 logits (soft-capped if asked) and the softmax partials of this warp's 128 columns.
+        const bool xent = args.mode == UFP8_EPI_XENT;
+        float xm = -INFINITY, xs = 0.0f;
         __nv_bfloat16* rs_row = nullptr;
         if (args.mode == UFP8_EPI_RS_PUSH && row_ok) {
           const long long owner = row / args.rs_rows;
@@ -963,12 +1004,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j)
                 o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
+              if (xent) xent_chunk(o, valid, args.xent_cap, xm, xs);
               __nv_bfloat16* p = rs_row ? rs_row + col0
                                         : static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
               store_bf16x32_packed_h(p, o, valid, vec, stream);
             }
           }
         }
+        if (xent && row_ok && nb * kBN + chalf * 128 < args.N)
+          *reinterpret_cast<float2*>(args.xent_stats + 2 * (static_cast<long long>(row) * args.xent_ld + nb * 2 + chalf)) =
+              make_float2(xm, xs);
       } else if (args.mode == UFP8_EPI_SWIGLU) {
         // TMEM columns [0,128) hold up, [128,256) hold gate for hidden units nb*128 + c.
 #pragma unroll 1
@@ -1547,8 +1592,21 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (d.batch > 1 && d.k_batches > 1)
     return set_error(UFP8_ERR_UNSUPPORTED, "batch > 1 together with k_batches > 1 is not supported");
   if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU &&
-      d.epilogue != UFP8_EPI_RS_PUSH)
+      d.epilogue != UFP8_EPI_RS_PUSH && d.epilogue != UFP8_EPI_XENT)
     return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
+  if (d.epilogue == UFP8_EPI_XENT) {
+    if (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1)
+      return set_error(UFP8_ERR_INVALID, "XENT needs bf16 output and batch 1");
+    if (!d.xent_stats || d.xent_ld_stats < (d.N + 127) / 128)
+      return set_error(UFP8_ERR_INVALID, "XENT needs xent_stats with xent_ld_stats >= ceil(N / 128)");
+    if (reinterpret_cast<uintptr_t>(d.xent_stats) & 7u)
+      return set_error(UFP8_ERR_ALIGN, "XENT: xent_stats is not 8-byte aligned");
+    if (!(d.xent_cap >= 0.0f) || std::isinf(d.xent_cap))
+      return set_error(UFP8_ERR_INVALID, "XENT: xent_cap must be 0 or a finite positive value");
+    if (variant == UFP8_GEMM_SINGLE_CTA)
+      return set_error(UFP8_ERR_UNSUPPORTED, "XENT runs on the CTA-pair kernel only");
+    if (d.K == 0 && d.M > 0 && d.N > 0) return set_error(UFP8_ERR_UNSUPPORTED, "XENT with K == 0");
+  }
   const bool rs = d.epilogue == UFP8_EPI_RS_PUSH;
   if (rs && (!d.rs_slots || d.rs_rows_per_rank <= 0 || d.rs_rank < 0 || d.d_dtype != UFP8_OUT_BF16 ||
              d.batch != 1 || d.M % d.rs_rows_per_rank != 0 || d.rs_rank >= d.M / d.rs_rows_per_rank))
@@ -1612,6 +1670,9 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.ag_epoch = d.ag_epoch;
   a.ag_rank = d.ag_rank;
   a.ag_rows = d.ag_rows_per_rank;
+  a.xent_stats = d.epilogue == UFP8_EPI_XENT ? d.xent_stats : nullptr;
+  a.xent_ld = d.xent_ld_stats;
+  a.xent_cap = d.xent_cap;
 
   if (d.K == 0) {
     if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");

@@ -122,7 +122,8 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
          d_batch_stride: int = 0, batch: int = 1, k_batches: int = 1, epilogue: int = C.EPI_STORE,
          h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
          ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None, rs_slots: int | None = None,
-         rs_rank: int = 0, rs_rows_per_rank: int = 0, ag: tuple | None = None) -> None:
+         rs_rank: int = 0, rs_rows_per_rank: int = 0, ag: tuple | None = None,
+         xent: tuple | None = None) -> None:
     desc = C.GemmDesc()
     desc.M, desc.N, desc.K = M, N, K
     desc.batch, desc.k_batches = batch, k_batches
@@ -140,6 +141,8 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
         desc.rs_slots, desc.rs_rank, desc.rs_rows_per_rank = rs_slots, rs_rank, rs_rows_per_rank
     if ag is not None:  # (flags pointer, epoch, rank, rows per rank): A rows arrive by all-gather
         desc.ag_flags, desc.ag_epoch, desc.ag_rank, desc.ag_rows_per_rank = ag
+    if xent is not None:  # (stats tensor, pitch in pairs, soft cap): the XENT epilogue's partials
+        desc.xent_stats, desc.xent_ld_stats, desc.xent_cap = xent[0].data_ptr(), xent[1], xent[2]
     n_eff = 2 * N if epilogue == C.EPI_SWIGLU else N
     flops = 2.0 * M * n_eff * K * batch * k_batches
     _launch("gemm", flops, lambda: C.gemm(desc, _stream()))
@@ -376,3 +379,114 @@ def rmsnorm_backward(x2d: torch.Tensor, scale: torch.Tensor | None, centered: bo
         dy2d.data_ptr(), d, dx.data_ptr(), d, dscale.data_ptr() if dscale is not None else None,
         ws.data_ptr() if ws is not None else None, nbytes, _stream()))
     return dx, dscale
+
+
+# ----------------------------------------------------------------------------- lm_head + loss
+# The output head of LlamaModel.get_logits (ueaj/model/model.py:140-165: final RMSNorm, lm_head
+# Einsum "bnd,dv->bnv", optional 15 * tanh(l / 15)) followed by the per-token next-token loss of
+# chunked_softmax_cross_entropy (ueaj/opt/next_token_loss.py:99-174).  x [T, d] bf16, w [d, V]
+# bf16, labels int32 [T], mask uint8 [T] or None.  The lm_head weight is quantised into a
+# [d, Vp] buffer, Vp = V rounded up to 16 (the MN-major operand's 16-byte pitch rule); the
+# logits and the fp8 logit gradient use the same pitch.
+def _pad16(n: int) -> int:
+    return (n + 15) // 16 * 16
+
+
+def xent_rows(logits: torch.Tensor, labels: torch.Tensor, mask: torch.Tensor | None, V: int | None = None):
+    """(lse, loss, qrow) f32 [rows] from bf16 logits [rows, >= V] (ufp8_xent_forward)."""
+    if not logits.is_cuda or logits.dtype != torch.bfloat16 or logits.stride(1) != 1:
+        raise ValueError("xent_rows: logits must be a CUDA bf16 tensor with unit column stride")
+    rows = logits.shape[0]
+    V = logits.shape[1] if V is None else V
+    lse, loss, qrow = (torch.empty(rows, dtype=torch.float32, device=logits.device) for _ in range(3))
+    _launch("xent_rows", 2.0 * rows * V, lambda: C.xent_forward(
+        logits.data_ptr(), rows, V, logits.stride(0), labels.data_ptr(),
+        mask.data_ptr() if mask is not None else None, lse.data_ptr(), loss.data_ptr(), qrow.data_ptr(), _stream()))
+    return lse, loss, qrow
+
+
+def xent_grad(logits: torch.Tensor, labels: torch.Tensor, mask: torch.Tensor | None, lse: torch.Tensor,
+              qrow: torch.Tensor | None, dloss: torch.Tensor | None, cap: float, fmt: int, V: int | None = None):
+    """dlogits from bf16 logits (ufp8_xent_backward): a bf16 [rows, V] tensor for fmt BF16, else an
+    Fp8Tensor [rows, Vp] (pitch Vp) with its per-tensor factors."""
+    rows = logits.shape[0]
+    V = logits.shape[1] if V is None else V
+    dev = logits.device
+    if fmt == C.BF16:
+        out = torch.empty((rows, V), dtype=torch.bfloat16, device=dev)
+        ldo, amax_t, inv = V, None, None
+    else:
+        ldo = _pad16(V)
+        out = torch.empty((rows, ldo), dtype=FP8_DTYPE[fmt], device=dev)
+        amax_t = torch.empty(1, dtype=torch.float32, device=dev)
+        inv = torch.empty(1, dtype=torch.float32, device=dev)
+    nbytes = (2.0 + (2.0 if fmt == C.BF16 else 1.0)) * rows * V
+    _launch("xent_grad", nbytes, lambda: C.xent_backward(
+        logits.data_ptr(), rows, V, logits.stride(0), labels.data_ptr(),
+        mask.data_ptr() if mask is not None else None, lse.data_ptr(),
+        qrow.data_ptr() if qrow is not None else None, dloss.data_ptr() if dloss is not None else None,
+        float(cap), fmt, out.data_ptr(), ldo, amax_t.data_ptr() if amax_t is not None else None,
+        inv.data_ptr() if inv is not None else None, _stream()))
+    return out if fmt == C.BF16 else Fp8Tensor(out, inv, amax_t)
+
+
+def quantize_head_weight(w: torch.Tensor) -> Fp8Tensor:
+    """e4m3 per-tensor quantisation of the lm_head weight [d, V] into a [d, Vp] buffer."""
+    w = _check_bf16_cuda(w, "lm_head w")
+    d, V = w.shape
+    Vp = _pad16(V)
+    if Vp != V:
+        w = torch.nn.functional.pad(w, (0, Vp - V))  # zero columns leave amax unchanged
+    return quantize(w, C.E4M3)
+
+
+def head_logits(qx: Fp8Tensor, qw: Fp8Tensor, V: int, cap: float):
+    """logits = x W with the XENT epilogue: (logits bf16 [T, Vp] (columns < V valid), stats)."""
+    T, d = qx.q.shape
+    Vp = qw.q.shape[1]
+    groups = (V + 127) // 128
+    logits = torch.empty((T, Vp), dtype=torch.bfloat16, device=qx.q.device)
+    stats = torch.empty((T, groups, 2), dtype=torch.float32, device=qx.q.device)
+    gemm(operand(qx, C.K_MAJOR, d), operand(qw, C.MN_MAJOR, Vp), T, V, d, logits, Vp, epilogue=C.EPI_XENT,
+         xent=(stats, groups, float(cap)))
+    return logits, stats
+
+
+def xent_combine(stats: torch.Tensor, logits: torch.Tensor, V: int, labels: torch.Tensor,
+                 mask: torch.Tensor | None):
+    """(lse, loss, qrow) from the XENT epilogue's partials (ufp8_xent_combine)."""
+    T, groups = stats.shape[0], stats.shape[1]
+    lse, loss, qrow = (torch.empty(T, dtype=torch.float32, device=logits.device) for _ in range(3))
+    _launch("xent_combine", 8.0 * T * groups, lambda: C.xent_combine(
+        stats.data_ptr(), groups, logits.data_ptr(), T, V, logits.stride(0), labels.data_ptr(),
+        mask.data_ptr() if mask is not None else None, lse.data_ptr(), loss.data_ptr(), qrow.data_ptr(), _stream()))
+    return lse, loss, qrow
+
+
+def head_xent_forward(x2d: torch.Tensor, scale: torch.Tensor | None, centered: bool, eps: float, w: torch.Tensor,
+                      labels: torch.Tensor, mask: torch.Tensor | None, cap: float):
+    """Fused final norm -> FP8 lm_head -> next-token loss.  Returns (loss f32 [T], saved)."""
+    x2d = _check_bf16_cuda(x2d, "x")
+    V = w.shape[1]
+    qx, rstd = rmsnorm_quant(x2d, scale, centered, eps, C.E4M3)
+    qw = quantize_head_weight(w)
+    logits, stats = head_logits(qx, qw, V, cap)
+    lse, loss, qrow = xent_combine(stats, logits, V, labels, mask)
+    return loss, (qx, rstd, qw, logits, lse, qrow, V)
+
+
+def head_xent_backward(dloss: torch.Tensor, saved, labels: torch.Tensor, mask: torch.Tensor | None, cap: float,
+                       need_dw: bool = True, fmt: int = C.E5M2):
+    """Backward of head_xent_forward up to the norm: (dxn bf16 [T, d], dw bf16 [d, V] or None).
+    `fmt`: the fp8 format of the logit gradient (the lm_head's bwd_dtype)."""
+    qx, rstd, qw, logits, lse, qrow, V = saved
+    T, d = qx.q.shape
+    qd = xent_grad(logits, labels, mask, lse, qrow, dloss, cap, fmt, V)
+    Vp = qd.q.shape[1]
+    dxn = torch.empty((T, d), dtype=torch.bfloat16, device=qx.q.device)
+    gemm(operand(qd, C.K_MAJOR, Vp), operand(qw, C.K_MAJOR, Vp), T, d, V, dxn, d)
+    dw = None
+    if need_dw:
+        dw = torch.empty((d, V), dtype=torch.bfloat16, device=qx.q.device)
+        gemm(operand(qx, C.MN_MAJOR, d), operand(qd, C.MN_MAJOR, Vp), d, V, T, dw, V)
+    return dxn, dw

@@ -15,7 +15,9 @@ What it restates (reference file:line, relative to the macrogpt-jax repository):
     accumulate, bf16 out), which the reference does not contain: it is the recipe the
     FP8 mode is specified with, composed here from the primitives above;
   * RMSNorm.__call__  ueaj/model/rmsnorm.py:68-84 (norm.py), with the summation order and
-    the rsqrt the CUDA kernel uses.
+    the rsqrt the CUDA kernel uses;
+  * the next-token loss on the lm_head logits (xent.py): ntp_args / chunked_softmax_cross_entropy
+    ueaj/opt/next_token_loss.py:13-174 and LlamaModel.get_logits ueaj/model/model.py:140-165.
 
 Parity pinning:
   * fp8 cast bytes: pinned.  fp8.py's own round-to-nearest-even cast is checked against
@@ -24,4 +26,4 @@ Parity pinning:
     here (jax, flax, optax absent, no network) and the reference ships no golden vectors;
     these functions are restatements, checked against an independent einsum (torch) only.
 """
-from . import fp8, norm, path  # noqa: F401
+from . import fp8, norm, path, xent  # noqa: F401

@@ -35,7 +35,9 @@ def test_header_constants_match_binding():
     assert (int(consts["UFP8_E4M3"]), int(consts["UFP8_E5M2"])) == (C.E4M3, C.E5M2)
     assert (int(consts["UFP8_K_MAJOR"]), int(consts["UFP8_MN_MAJOR"])) == (C.K_MAJOR, C.MN_MAJOR)
     assert (int(consts["UFP8_EPI_STORE"]), int(consts["UFP8_EPI_SWIGLU"]), int(consts["UFP8_EPI_DSWIGLU"]),
-            int(consts["UFP8_EPI_RS_PUSH"])) == (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU, C.EPI_RS_PUSH)
+            int(consts["UFP8_EPI_RS_PUSH"]), int(consts["UFP8_EPI_XENT"])) == \
+        (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU, C.EPI_RS_PUSH, C.EPI_XENT)
+    assert int(consts["UFP8_BF16"]) == C.BF16
     assert tuple(int(consts[k]) for k in ("UFP8_GEMM_AUTO", "UFP8_GEMM_SINGLE_CTA", "UFP8_GEMM_CTA_PAIR",
                                           "UFP8_GEMM_CTA_PAIR_DIRECT")) == \
         (C.GEMM_AUTO, C.GEMM_SINGLE_CTA, C.GEMM_CTA_PAIR, C.GEMM_CTA_PAIR_DIRECT)
@@ -84,6 +86,19 @@ def test_struct_layout_matches_header(tmp_path):
      C.ERR_INVALID, "null x"),
     (lambda L: L.ufp8_rmsnorm_backward(ctypes.c_void_p(16), 1, 9000, 9000, None, 0, 0, None, None, 9000, None, 9000,
                                        None, None, 0, None), C.ERR_UNSUPPORTED, "d 9000"),
+    (lambda L: L.ufp8_xent_forward(None, 4, 0, 0, None, None, None, None, None, None), C.ERR_INVALID, "V >= 1"),
+    (lambda L: L.ufp8_xent_forward(None, 2, 8, 4, None, None, None, None, None, None), C.ERR_INVALID, "ldl < V"),
+    (lambda L: L.ufp8_xent_forward(None, 2, 8, 8, None, None, None, None, None, None), C.ERR_INVALID,
+     "null logits"),
+    (lambda L: L.ufp8_xent_combine(ctypes.c_void_p(16), 1, ctypes.c_void_p(16), 1, 300, 300, ctypes.c_void_p(16),
+                                   None, None, None, None, None), C.ERR_INVALID, "ld_stats < ceil(V / 128)"),
+    (lambda L: L.ufp8_xent_backward(ctypes.c_void_p(16), 1, 8, 8, ctypes.c_void_p(16), None, None, None, None, 0.0,
+                                    5, None, 8, None, None, None), C.ERR_INVALID, "fmt 5"),
+    (lambda L: L.ufp8_xent_backward(ctypes.c_void_p(16), 1, 8, 8, ctypes.c_void_p(16), None, None, None, None, -1.0,
+                                    C.BF16, None, 8, None, None, None), C.ERR_INVALID, "cap must be"),
+    (lambda L: L.ufp8_xent_backward(ctypes.c_void_p(16), 1, 8, 8, ctypes.c_void_p(16), None, None, None, None, 0.0,
+                                    C.E5M2, ctypes.c_void_p(16), 8, None, None, None), C.ERR_INVALID,
+     "null lse, qrow or dlogits"),
     (lambda L: L.ufp8_amax(None, -1, None, None), C.ERR_INVALID, "n < 0"),
     (lambda L: L.ufp8_quantize(None, 4, 7, None, None, None, None), C.ERR_INVALID, "fmt 7"),
     (lambda L: L.ufp8_amax_quant(None, 4, 3, None, None, None, None), C.ERR_INVALID, "fmt 3"),
