@@ -38,6 +38,9 @@ CONFIGS = {
     # quantisation of its output) -> GMLP, forward and backward
     "norm_gmlp_d4096": dict(kind="gmlp", d=4096, h=14336, B=4, S=4096, norm=True),
     "attn_d2048": dict(kind="attn", d=2048, heads=16, head_d=128, B=16, S=1024),
+    # the output head of the Llama-3-8B shape (final RMSNorm, lm_head 4096 -> 128256, soft cap) and
+    # the next-token loss, forward and backward, on one GPU
+    "head_xent_v128256": dict(kind="head", d=4096, V=128256, B=4, S=4096),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
 GMLP_D4096_GEMM_TRAFFIC = 1.651e9  # DRAM bytes per GEMM launch, T 16384 / d 4096 / h 14336, from one ncu
@@ -53,6 +56,12 @@ def flops_per_step(T, d, h):
 def attn_flops_per_step(T, d):
     """Attention projections fwd+bwd: QKV 2 T d 3d + O 2 T d d forward, twice that backward."""
     return 3.0 * (2.0 * T * d * 3 * d + 2.0 * T * d * d)
+
+
+def head_flops_per_step(T, d, V):
+    """lm_head fwd+bwd: logits 2 T d V, dX 2 T d V, dW 2 T d V (the reference's rematerialised
+    recomputation of the logits in its backward is not counted)."""
+    return 6.0 * T * d * V
 
 
 def load_peaks():
@@ -139,6 +148,43 @@ def cpu_oracle_step(d, h, T, seed=0):
     return time.perf_counter() - t0
 
 
+def cpu_head_step(d, V, T, seed=0):
+    """Seconds the oracle takes for one output-head step of T tokens over V classes on the host,
+    as (activation side, weight quantisation): the first is norm + fp8 quantisation, logits, soft
+    cap, loss, fp8 logit gradient, the two backward contractions and the norm backward; the second
+    the e4m3 quantisation of the [d, V] weight (independent of T)."""
+    import numpy as np
+    from oracle import fp8 as ofp8
+    from oracle import path as op
+    from oracle import xent as ox
+    op.FAST_CAST = True
+    ofp8.THREADED = True
+    rng = np.random.default_rng(seed)
+    w = op.bf16_normal(rng, (d, V), d ** -0.5)
+    x = op.bf16_normal(rng, (T, d))
+    scale = op.bf16_normal(rng, (d,), 0.1)
+    labels = rng.integers(0, V, T).astype(np.int32)
+    t0 = time.perf_counter()
+    qw = op.quant(w, ofp8.E4M3)
+    t1 = time.perf_counter()
+    _, saved = ox.head_forward(x, scale, False, 1e-6, qw, labels, None, 15.0, acc=np.float32)
+    ox.head_backward(np.ones(T, np.float32), saved, x, scale, False, labels, None, 15.0, acc=np.float32)
+    return time.perf_counter() - t1, t1 - t0
+
+
+CPU_VOCAB_SLICES = (1024, 4096)  # vocabulary widths the CPU port executes for the head workload
+CPU_HEAD_TOKENS = 4096  # tokens per executed CPU head step
+
+
+def head_cpu_estimate(d, V, T, samples):
+    """Full-config seconds from executed head steps [(V slice, t_act, t_wq)] at CPU_HEAD_TOKENS
+    tokens: t = (T / Ts) (a + b V) + c V, with a + b V fitted to the activation-side times (all of
+    that work is per token) and c the weight quantisation time per vocabulary column."""
+    act, a, b = fit_hidden([(vs, ta) for vs, ta, _ in samples], V)
+    c = sum(tw / vs for vs, _, tw in samples) / len(samples)
+    return (T / CPU_HEAD_TOKENS) * act + c * V, a, b, c
+
+
 def fit_hidden(samples, h_full):
     """Least-squares fit t(h) = a + b h over (hidden slice, seconds) samples taken at the full
     token count and d_model, evaluated at h_full.  The activation-side work (x and dY
@@ -165,6 +211,13 @@ def cpu_sample_desc(T, d, h, n_steps):
             "ml_dtypes casts, single-threaded elementwise")
 
 
+def head_sample_desc(T, d, V, n_steps):
+    return (f"{n_steps} oracle output-head fwd+bwd steps at {CPU_HEAD_TOKENS} of the {T} tokens, d_model {d}, on "
+            f"vocabulary slices {CPU_VOCAB_SLICES[0]} and {CPU_VOCAB_SLICES[1]} (alternating) of {V}, weight "
+            f"quantised each step (timed apart); estimated as (T / {CPU_HEAD_TOKENS}) (a + b V) + c V at "
+            f"T {T}, V {V}; numpy fp32 BLAS contractions on all host threads, ml_dtypes casts")
+
+
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -187,54 +240,77 @@ def gpu_arm_config(args, cfg, world):
 
 
 # ----------------------------------------------------------------------------- arms
+def head_arm_config(args, cfg):
+    d, V, T = cfg["d"], cfg["V"], cfg["B"] * cfg["S"]
+    return {"workload": args.config_desc, "tokens": T, "d_model": d, "vocab": V, "parallelism": "tp1",
+            "l2": "inputs larger than L2"}
+
+
 def run_reference(args, cfg, rank, world):
     """The CPU port of the path (oracle/), rank 0 only.  Every step runs the full token count
-    on a hidden slice; the printed ms_per_step is the measured time of those executed steps,
-    and `value` is the full-config throughput from the fit t(h) = a + b h (fields `executed`
-    and `extrapolation` give both)."""
+    on a hidden slice (the head workload: a vocabulary slice); the printed ms_per_step is the
+    measured time of those executed steps, and `value` is the full-config throughput from the
+    fit t(h) = a + b h (fields `executed` and `extrapolation` give both)."""
     if rank != 0:
         return None
-    d, h, T = cfg["d"], cfg["h"], cfg["B"] * cfg["S"]
-    samples = []
+    head = cfg["kind"] == "head"
+    d, T = cfg["d"], cfg["B"] * cfg["S"]
+    h = cfg["V"] if head else cfg["h"]
+    slices = CPU_VOCAB_SLICES if head else CPU_SLICES
+    samples, head_samples = [], []
     for i in range(args.warmup + args.steps):
-        hs = CPU_SLICES[i % 2]
-        t = cpu_oracle_step(d, hs, T, seed=i)
+        hs = slices[i % 2]
+        if head:
+            ta, tw = cpu_head_step(d, hs, CPU_HEAD_TOKENS, seed=i)
+            t = ta + tw
+        else:
+            t = cpu_oracle_step(d, hs, T, seed=i)
         if i >= args.warmup:
             samples.append((hs, t))
-    full_s, a, b = fit_hidden(samples, h)
+            if head:
+                head_samples.append((hs, ta, tw))
+    if head:
+        full_s, a, b, c = head_cpu_estimate(d, h, T, head_samples)
+    else:
+        full_s, a, b = fit_hidden(samples, h)
     exec_ms = 1000.0 * sum(s[1] for s in samples) / len(samples)
     value = T / full_s
     by_h = {str(hs): 1000.0 * sum(s[1] for s in samples if s[0] == hs) / max(1, sum(1 for s in samples if s[0] == hs))
-            for hs in CPU_SLICES}
+            for hs in slices}
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": exec_ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp8",
         "data": "synthetic (seeded)",
-        "config": gpu_arm_config(args, cfg, world),
-        "tflops_per_gpu": flops_per_step(T, d, h) / full_s / 1e12,
+        "config": head_arm_config(args, cfg) if head else gpu_arm_config(args, cfg, world),
+        "tflops_per_gpu": (head_flops_per_step(T, d, h) if head else flops_per_step(T, d, h)) / full_s / 1e12,
         "executed": {"steps": args.steps, "warmup_steps": args.warmup, "tokens": T, "d_model": d,
-                     "hidden_slices": list(CPU_SLICES), "ms_per_step": exec_ms, "ms_per_step_by_hidden": by_h,
+                     ("vocab_slices" if head else "hidden_slices"): list(slices), "ms_per_step": exec_ms,
+                     "ms_per_step_by_slice": by_h,
                      "note": "ms_per_step is the mean measured time of these executed steps"},
-        "extrapolation": {"model": "t(h) = a + b*h, least squares over the executed steps",
+        "extrapolation": {"model": ("t = (T / Ts) (a + b V) + c V; a, b least squares over the executed steps' "
+                                    "activation-side times, c their weight quantisation time per column") if head
+                          else "t(h) = a + b*h, least squares over the executed steps",
                           "a_ms": 1000.0 * a, "b_ms_per_hidden": 1000.0 * b, "to_hidden": h,
                           "est_ms_per_step_full": 1000.0 * full_s, "factor": 1000.0 * full_s / exec_ms,
                           "note": "value (tokens/s) = tokens / est_ms_per_step_full: an estimate for the full "
                                   "config, not a measurement of it"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
-                         "sample": cpu_sample_desc(T, d, h, args.steps)},
+                         "sample": head_sample_desc(T, d, h, args.steps) if head else
+                         cpu_sample_desc(T, d, h, args.steps)},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     return out
 
 
-def e2e_pipelined(step_fn, x_in, dy_in, steps, barrier, graph=False):
+def e2e_pipelined(step_fn, x_in, dy_in, steps, barrier, graph=False, y_like=None):
     """Milliseconds for `steps` end-to-end steps: each step's x and dY are copied from pinned
     host memory into one of two device buffers on a copy stream (the copy for step i+1 runs
     while step i computes), and each step's y is copied back to pinned host memory on a second
     copy stream as soon as the forward has produced it.  step_fn(x, dy) -> (y, event after
     which y is final, or None for the end of the step).  Timed with CUDA events on the compute
-    stream, which waits for both copy streams before the end event."""
+    stream, which waits for both copy streams before the end event.  y_like: a tensor of y's shape
+    and dtype (default: x's shape in bf16)."""
     import torch
     cur = torch.cuda.current_stream()
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
@@ -242,7 +318,10 @@ def e2e_pipelined(step_fn, x_in, dy_in, steps, barrier, graph=False):
     dy_host = dy_in.cpu().pin_memory()
     xb = [torch.empty_like(x_in) for _ in range(2)]
     dyb = [torch.empty_like(dy_in) for _ in range(2)]
-    yh = [torch.empty(x_in.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    if y_like is None:
+        yh = [torch.empty(x_in.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    else:
+        yh = [torch.empty(y_like.shape, dtype=y_like.dtype).pin_memory() for _ in range(2)]
     in_ready = [torch.cuda.Event() for _ in range(2)]
     buf_free = [torch.cuda.Event() for _ in range(2)]
     y_done = [torch.cuda.Event() for _ in range(2)]
@@ -343,6 +422,8 @@ def run_ours(args, cfg, rank, world, local_rank):
     _capi.set_gemm_variant(args.gemm_variant)
     if cfg["kind"] == "attn":
         return run_attn(args, cfg, rank, world, local_rank, dev)
+    if cfg["kind"] == "head":
+        return run_head(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
     if world > 1 and cfg.get("norm"):
@@ -642,6 +723,104 @@ def run_attn(args, cfg, rank, world, local_rank, dev):
     return out
 
 
+def run_head(args, cfg, rank, world, local_rank, dev):
+    """Output head + next-token loss: chunked_softmax_cross_entropy(tokens, x, head.get_logits) with
+    an OutputHead (final RMSNorm, FP8 lm_head, soft cap), then the backward of the summed loss."""
+    import torch
+    from macrogpt_jax_b200 import _capi, ops
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.head import OutputHead
+    from macrogpt_jax_b200.next_token_loss import _fused_head, chunked_softmax_cross_entropy
+    if world > 1:
+        raise SystemExit("the output-head workload runs on one GPU")
+    d, V, B, S = cfg["d"], cfg["V"], cfg["B"], cfg["S"]
+    T = B * S
+    head = OutputHead.override(lm_head=Einsum.override(initializer=scaled_normal_init(d ** -0.5)))(
+        d, V, head_cap="tanh", rngs=Rngs(0))
+    assert _fused_head(head.get_logits) is head
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    x = torch.randn((B, S, d), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    tokens = torch.randint(0, V, (B, S), generator=gen, device=dev, dtype=torch.int64)
+    params = list(head.parameters())
+
+    def fwd_bwd(xb, tb):
+        xl = xb.detach().requires_grad_(True)
+        loss = chunked_softmax_cross_entropy(tb, xl, head.get_logits)
+        ev = torch.cuda.Event()
+        ev.record()
+        loss.sum().backward()
+        for p in params:
+            p.grad = None
+        return loss, ev
+
+    for _ in range(args.warmup):
+        fwd_bwd(x, tokens)
+    torch.cuda.synchronize()
+    timer = ops.KernelTimer()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = _capi.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.set_timer(timer)
+    ev0.record()
+    for _ in range(args.steps):
+        fwd_bwd(x, tokens)
+    ev1.record()
+    ops.set_timer(None)
+    torch.cuda.synchronize()
+    launches = _capi.launches - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    summ = timer.summary()
+
+    e2e = None
+    if not args.no_e2e:
+        ems = e2e_pipelined(fwd_bwd, x, tokens, args.steps, lambda: None, y_like=torch.empty((B, S)))
+        e2e = {"value": T * args.steps / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems / args.steps,
+               "h2d_bytes_per_step": x.numel() * 2 + tokens.numel() * 8, "d2h_bytes_per_step": T * 4,
+               "path": "chunked_softmax_cross_entropy(tokens, x, head.get_logits) and the backward of the summed "
+                       "loss; every step copies its activations and tokens from pinned host memory (side stream, "
+                       "double-buffered) and reads its per-token loss back (side stream, overlapping the backward)"}
+
+    peaks, peak_src = load_peaks()
+    fl = head_flops_per_step(T, d, V)
+    g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
+    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
+    tflops = fl * args.steps / (ms / 1000.0) / 1e12
+    hbm = {}
+    for k in ("xent_grad", "xent_combine", "quantize", "amax", "norm_quant", "norm_bwd"):
+        if k in summ:
+            n, kms, b = summ[k]
+            hbm[k] = {"bound": "hbm", "unit": "GB/s", "launches": n, "achieved": b / (kms / 1000.0) / 1e9,
+                      "peak": peaks["hbm_gbs"], "frac": b / (kms / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                      "time_share": kms / ms}
+    out = {
+        "metric": "FP8 output head + next-token loss fwd+bwd tokens/s (TFLOP/s/GPU)",
+        "value": T * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)", "config": head_arm_config(args, cfg),
+        "tflops_per_gpu": tflops,
+        "roofline": {"kernel": "gemm_fp8_pair_kernel", "bound": "tensor", "achieved": achieved, "peak": peak_fp8,
+                     "unit": "TFLOP/s", "frac": (achieved / peak_fp8) if achieved else None,
+                     "peak_source": f"2 x bf16_tflops_sustained, {peak_src}", "launches": g_n,
+                     "time_share": g_ms / ms if ms else None, "traffic": None},
+        "roofline_hbm_kernels": hbm,
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if e2e:
+        out["e2e"] = e2e
+    if not args.no_cpu_baseline:
+        samples = [(vs,) + cpu_head_step(d, vs, CPU_HEAD_TOKENS, seed=k) for k, vs in enumerate(CPU_VOCAB_SLICES)]
+        step_s, a, b, c = head_cpu_estimate(d, V, T, samples)
+        out["cpu_baseline"] = {"value": T / step_s, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                               "sample": head_sample_desc(T, d, V, len(samples)), "est_ms_per_step": step_s * 1000.0,
+                               "executed_ms": {str(vs): 1000.0 * (ta + tw) for vs, ta, tw in samples},
+                               "tflops": fl / step_s / 1e12}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -678,6 +857,10 @@ def main():
                             f"{cfg['heads']} heads x {cfg['head_d']}, FP8 e4m3/e5m2")
         if args.impl == "reference":
             raise SystemExit("the CPU arm covers the GMLP workloads")
+    elif cfg["kind"] == "head":
+        args.config_desc = (f"output head fwd+bwd (final RMSNorm -> FP8 lm_head {cfg['d']}->{cfg['V']} -> 15*tanh(l/15) "
+                            f"-> next-token cross-entropy), {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
+                            "FP8 e4m3/e5m2")
     else:
         args.config_desc = (f"GMLP fwd+bwd, {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
                             f"d_model {cfg['d']}, hidden {cfg['h']}, FP8 e4m3/e5m2")

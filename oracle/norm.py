@@ -59,10 +59,11 @@ def rmsnorm(x_bits: np.ndarray, scale_bits=None, centered: bool = False, eps: fl
     return f32_to_bf16_bits(y), r
 
 
-def rmsnorm_quant(x_bits, scale_bits=None, centered=False, eps=1e-6, fmt: int = 0):
-    """RMSNorm followed by the per-tensor fp8 recipe on its output: (codes, amax, inv, y, rstd)."""
+def rmsnorm_quant(x_bits, scale_bits=None, centered=False, eps=1e-6, fmt: int = 0, fast: bool = False):
+    """RMSNorm followed by the per-tensor fp8 recipe on its output: (codes, amax, inv, y, rstd).
+    fast: the ml_dtypes-backed cast (same codes; see fp8.quantize_bits)."""
     y, r = rmsnorm(x_bits, scale_bits, centered, eps)
-    codes, amax, inv = quantize_bits(y.reshape(-1), fmt)
+    codes, amax, inv = quantize_bits(y.reshape(-1), fmt, fast=fast)
     return codes.reshape(y.shape), amax, inv, y, r
 
 

@@ -27,7 +27,9 @@ from __future__ import annotations
 import numpy as np
 
 from . import norm as onorm
-from .fp8 import E4M3, E5M2, bf16_bits_to_f32, f32_to_bf16_bits, f32_to_fp8, round_bf16, scale_from_amax
+from . import path as _path
+from .fp8 import (E4M3, E5M2, bf16_bits_to_f32, f32_to_bf16_bits, f32_to_fp8, f32_to_fp8_fast, round_bf16,
+                  scale_from_amax)
 from .path import Q, gemm, quant
 
 BF16 = 2  # unquantised gradient output
@@ -120,7 +122,8 @@ def xent_backward(logit_bits: np.ndarray, labels, mask, lse, qrow, dloss=None, c
     amax = np.float32(0.0) if rows == 0 else (np.float32(np.nan) if np.isnan(per).any() else per.max())
     s = scale_from_amax(amax, fmt)
     with np.errstate(over="ignore", invalid="ignore"):
-        codes = f32_to_fp8((v * s).astype(np.float32), fmt)
+        cast = f32_to_fp8_fast if _path.FAST_CAST else f32_to_fp8  # same codes (fp8.py)
+        codes = cast((v * s).astype(np.float32), fmt)
         inv = np.float32(np.float32(1.0) / s)
     return codes, np.float32(amax), inv
 
@@ -128,7 +131,7 @@ def xent_backward(logit_bits: np.ndarray, labels, mask, lse, qrow, dloss=None, c
 def head_forward(x_bits, scale_bits, centered, eps, w_bits, labels, mask=None, cap: float = 0.0, acc=np.float64):
     """Final RMSNorm -> FP8 lm_head "bnd,dv->bnv" -> (soft cap) -> per-token masked loss.
     x [T, d], w [d, V] as bf16 bits.  Returns (loss f32 [T], saved dict)."""
-    codes, amax, inv, y, rstd = onorm.rmsnorm_quant(x_bits, scale_bits, centered, eps, E4M3)
+    codes, amax, inv, y, rstd = onorm.rmsnorm_quant(x_bits, scale_bits, centered, eps, E4M3, fast=_path.FAST_CAST)
     qx = Q(codes, E4M3, amax, inv)
     qw = w_bits if isinstance(w_bits, Q) else quant(w_bits, E4M3)
     logits = gemm(qx, qw, "td", "dv", "tv", acc)
