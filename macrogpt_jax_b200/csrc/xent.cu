@@ -10,12 +10,15 @@
 //                        UFP8_EPI_XENT epilogue wrote, so the forward never re-reads the logits.
 //   xent_amax_kernel     the backward's per-tensor fp8 scale, from the per-row results alone:
 //                        max |dl| over a row is |g| * (1 - softmax[label]) (the label column).
-//   xent_grad_kernel     one streaming pass logits -> dlogits (bf16 read, fp8 or bf16 written).
+//   xent_grad_kernel     one streaming pass logits -> dlogits (bf16 read, fp8 or bf16 written) by a
+//                        resident grid walking (row, 8192-column) units.
 //
 // All arithmetic is f32.  Partials merge as (m, s) + (m', s') = (M, s e^(m-M) + s' e^(m'-M)),
 // M = max(m, m'); every merge order is fixed, so results do not depend on scheduling.  exp is the
-// MUFU approximation (__expf, a few ulp) throughout, and the same expression gives softmax[label]
-// in the forward (qrow) and in the backward, so the fp8 amax is exactly the largest |dl|.
+// MUFU approximation (__expf, a few ulp) in the sums.  A softmax value is
+// p = 2^fma(c, log2 e, -lse * log2 e) (one FMA and the MUFU ex2.approx), and the same expression
+// gives softmax[label] in the forward (qrow) and in the backward, so the fp8 amax is exactly the
+// largest |dl|.
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -71,6 +74,17 @@ __device__ __forceinline__ float bf(uint32_t bits16) { return __uint_as_float(bi
 __device__ __forceinline__ float wlo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float whi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// softmax value of logit c in a row with -lse * log2 e = nl2
+__device__ __forceinline__ float softmax_p(float c, float nl2) { return ex2_approx(__fmaf_rn(c, kLog2e, nl2)); }
+
 // Column of a label: negative labels count from the end; outside [-V, V): none (-1).
 __device__ __forceinline__ int64_t label_col(int32_t lab, int64_t V) {
   int64_t l = lab;
@@ -125,7 +139,7 @@ __device__ __forceinline__ void finish_row(const XentArgs& a, int64_t row, float
   const float mk = a.mask ? static_cast<float>(a.mask[row]) : 1.0f;
   a.lse[row] = lse;
   a.loss[row] = __fmul_rn(__fsub_rn(lse, cl), mk);
-  a.qrow[row] = col >= 0 ? __fsub_rn(1.0f, __expf(__fsub_rn(cl, lse))) : 1.0f;
+  a.qrow[row] = col >= 0 ? __fsub_rn(1.0f, softmax_p(cl, __fmul_rn(lse, -kLog2e))) : 1.0f;
 }
 
 __global__ void __launch_bounds__(kXThreads) xent_rows_kernel(const XentArgs a) {
@@ -205,9 +219,11 @@ __global__ void __launch_bounds__(kXAmaxThreads) xent_amax_kernel(const XentArgs
   }
 }
 
-__device__ __forceinline__ float xent_dl(float c, bool is_label, float lse, float ge, int cap_on, float inv_cap) {
-  const float p = __expf(__fsub_rn(c, lse));
-  float v = __fmul_rn(ge, is_label ? __fsub_rn(p, 1.0f) : p);
+// dl of one logit c, times the row's output factor wr (g for a bf16 gradient, g * s for fp8):
+// v = (p - [label]) * wr, then v * (1 - (c / cap)^2) with the soft cap.
+__device__ __forceinline__ float xent_dl(float c, bool is_label, float nl2, float wr, int cap_on, float inv_cap) {
+  const float p = softmax_p(c, nl2);
+  float v = __fmul_rn(is_label ? __fsub_rn(p, 1.0f) : p, wr);
   if (cap_on) {
     const float t = __fmul_rn(c, inv_cap);
     v = __fmul_rn(v, __fsub_rn(1.0f, __fmul_rn(t, t)));
@@ -215,73 +231,132 @@ __device__ __forceinline__ float xent_dl(float c, bool is_label, float lse, floa
   return v;
 }
 
-// One CTA: kXCols columns of one row.  Vector units (8 columns: a 16-byte load, an 8-byte fp8 or
-// 16-byte bf16 store) where the unit lies inside the row; element by element otherwise.
+// Eight products -> eight fp8 bytes.  The hardware conversion rounds like the cast except where
+// a product is special (NaN, or past the format's overflow threshold; fp8cast.cuh): one check on
+// the largest magnitude bit pattern of the eight (a NaN pattern is above every other) decides
+// whether any needs the re-encoding of cvt2.
+__device__ __forceinline__ uint2 cvt8(const float (&p)[8], int fmt) {
+  uint32_t mb = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(p[i]) & 0x7FFFFFFFu);
+  const bool plain = fmt == UFP8_E4M3 ? mb <= 0x43E80000u /* 464 */ : mb < 0x47700000u /* 61440 */;
+  uint32_t w[4];
+  if (plain) {
+    const __nv_fp8_interpretation_t kind = fmt == UFP8_E4M3 ? __NV_E4M3 : __NV_E5M2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      w[i] = static_cast<uint32_t>(
+          __nv_cvt_float2_to_fp8x2(make_float2(p[2 * i], p[2 * i + 1]), __NV_SATFINITE, kind));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = cvt2(p[2 * i], p[2 * i + 1], fmt);
+  }
+  return make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+}
+
+// Work unit = kXCols columns of one row; a resident grid walks the units (row-major order), the
+// 16-byte loads of its next unit issued before the current one is computed.  Vector units of 8
+// columns (a 16-byte load, an 8-byte fp8 or 16-byte bf16 store) where the unit lies inside the
+// row, element by element otherwise.
 template <bool kFp8>
-__global__ void __launch_bounds__(kXThreads) xent_grad_kernel(const XentArgs a) {
-  const int64_t row = blockIdx.x / a.ctas_per_row;
-  const int64_t c0 = (static_cast<int64_t>(blockIdx.x) - row * a.ctas_per_row) * kXCols;
-  const float lse = a.lse_in[row];
-  const float g = a.dloss ? a.dloss[row] : 1.0f;
-  const float mk = a.mask ? static_cast<float>(a.mask[row]) : 1.0f;
-  const float ge = __fmul_rn(g, mk);
-  const int64_t lab = label_col(a.labels[row], a.V);
-  const float sc = kFp8 ? scale_from_amax(*a.amax, a.fmt) : 1.0f;
+__device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t u, float sc, const uint4 (&w)[kXUnits]) {
+  const int64_t row = u / a.ctas_per_row;
+  const int64_t c0 = (u - row * a.ctas_per_row) * kXCols;
   const uint16_t* lr = a.logits + row * a.ldl;
   uint8_t* q8 = static_cast<uint8_t*>(a.out) + row * a.ldo;     // kFp8
   uint16_t* q16 = static_cast<uint16_t*>(a.out) + row * a.ldo;  // !kFp8
-  auto put1 = [&](int64_t col, float v) {
+  const float nl2 = __fmul_rn(a.lse_in[row], -kLog2e);
+  const float g = a.dloss ? a.dloss[row] : 1.0f;
+  const float mk = a.mask ? static_cast<float>(a.mask[row]) : 1.0f;
+  const float ge = __fmul_rn(g, mk);
+  const float wr = kFp8 ? __fmul_rn(ge, sc) : ge;
+  const int64_t lab = label_col(a.labels[row], a.V);
+  auto put1 = [&](int64_t cc, float v) {
     if (kFp8)
-      q8[col] = static_cast<uint8_t>(cvt2(__fmul_rn(v, sc), 0.0f, a.fmt) & 0xFFu);
+      q8[cc] = static_cast<uint8_t>(cvt2(v, 0.0f, a.fmt) & 0xFFu);
     else
-      q16[col] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+      q16[cc] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
   };
-  if (a.vec) {
-    uint4 w[kXUnits];
-    int64_t col[kXUnits];
-#pragma unroll
-    for (int k = 0; k < kXUnits; ++k) {
-      col[k] = c0 + static_cast<int64_t>(k * kXThreads + threadIdx.x) * 8;
-      if (col[k] + 8 <= a.V) w[k] = ld_stream16(lr + col[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < kXUnits; ++k) {
-      if (col[k] + 8 <= a.V) {
-        const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[2 * j] = xent_dl(wlo(ws[j]), col[k] + 2 * j == lab, lse, ge, a.cap_on, a.inv_cap);
-          v[2 * j + 1] = xent_dl(whi(ws[j]), col[k] + 2 * j + 1 == lab, lse, ge, a.cap_on, a.inv_cap);
-        }
-        if (kFp8) {
-          uint2 o;
-          o.x = cvt2(__fmul_rn(v[0], sc), __fmul_rn(v[1], sc), a.fmt) |
-                (cvt2(__fmul_rn(v[2], sc), __fmul_rn(v[3], sc), a.fmt) << 16);
-          o.y = cvt2(__fmul_rn(v[4], sc), __fmul_rn(v[5], sc), a.fmt) |
-                (cvt2(__fmul_rn(v[6], sc), __fmul_rn(v[7], sc), a.fmt) << 16);
-          *reinterpret_cast<uint2*>(q8 + col[k]) = o;
-        } else {
-          uint4 o;
-          uint32_t* ow = &o.x;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-            ow[j] = *reinterpret_cast<const uint32_t*>(&b);
-          }
-          *reinterpret_cast<uint4*>(q16 + col[k]) = o;
-        }
-      } else {
-        for (int64_t cc = col[k]; cc < a.V && cc < col[k] + 8; ++cc)
-          put1(cc, xent_dl(bf(lr[cc]), cc == lab, lse, ge, a.cap_on, a.inv_cap));
-      }
-    }
-  } else {
+  if (!a.vec) {
     for (int i = 0; i < kXCols / kXThreads; ++i) {
       const int64_t cc = c0 + static_cast<int64_t>(i) * kXThreads + threadIdx.x;
-      if (cc < a.V) put1(cc, xent_dl(bf(lr[cc]), cc == lab, lse, ge, a.cap_on, a.inv_cap));
+      if (cc < a.V) put1(cc, xent_dl(bf(lr[cc]), cc == lab, nl2, wr, a.cap_on, a.inv_cap));
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kXUnits; ++k) {
+    const int64_t col = c0 + static_cast<int64_t>(k * kXThreads + threadIdx.x) * 8;
+    if (col + 8 <= a.V) {
+      const int64_t rel = lab - col;
+      const int lj = (rel >= 0 && rel < 8) ? static_cast<int>(rel) : -1;  // label's slot in the unit
+      const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[2 * j] = xent_dl(wlo(ws[j]), 2 * j == lj, nl2, wr, a.cap_on, a.inv_cap);
+        v[2 * j + 1] = xent_dl(whi(ws[j]), 2 * j + 1 == lj, nl2, wr, a.cap_on, a.inv_cap);
+      }
+      if (kFp8) {
+        *reinterpret_cast<uint2*>(q8 + col) = cvt8(v, a.fmt);
+      } else {
+        uint4 o;
+        uint32_t* ow = &o.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+          ow[j] = *reinterpret_cast<const uint32_t*>(&b);
+        }
+        *reinterpret_cast<uint4*>(q16 + col) = o;
+      }
+    } else {
+      for (int64_t cc = col; cc < a.V && cc < col + 8; ++cc)
+        put1(cc, xent_dl(bf(lr[cc]), cc == lab, nl2, wr, a.cap_on, a.inv_cap));
     }
   }
+}
+
+template <int kU>
+__device__ __forceinline__ void xent_grad_load(const XentArgs& a, int64_t u, uint4 (&w)[kU]) {
+  const int64_t row = u / a.ctas_per_row;
+  const int64_t c0 = (u - row * a.ctas_per_row) * kXCols;
+  const uint16_t* lr = a.logits + row * a.ldl;
+#pragma unroll
+  for (int k = 0; k < kU; ++k) {
+    const int64_t col = c0 + static_cast<int64_t>(k * kXThreads + threadIdx.x) * 8;
+    w[k] = col + 8 <= a.V ? ld_stream16(lr + col) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <bool kFp8>
+__global__ void __launch_bounds__(kXThreads) xent_grad_kernel(const XentArgs a) {
+  const float sc = kFp8 ? scale_from_amax(*a.amax, a.fmt) : 1.0f;
+  const int64_t units = a.rows * a.ctas_per_row;
+  int64_t u = blockIdx.x;
+  if (u >= units) return;
+  uint4 w[kXUnits], wn[kXUnits];
+  if (a.vec) xent_grad_load(a, u, w);
+  for (; u < units; u += gridDim.x) {
+    const int64_t un = u + gridDim.x;
+    if (a.vec && un < units) xent_grad_load(a, un, wn);
+    xent_grad_unit<kFp8>(a, u, sc, w);
+#pragma unroll
+    for (int k = 0; k < kXUnits; ++k) w[k] = wn[k];
+  }
+}
+
+// Resident CTAs of a kernel on this device (cached per device and kernel).
+int resident_ctas(const void* fn, const DeviceInfo& dev, int slot, int64_t* out) {
+  static thread_local int dev_of[2] = {-1, -1}, per_sm[2] = {0, 0};
+  if (dev_of[slot] != dev.device) {
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kXThreads, 0);
+    if (e != cudaSuccess) return cuda_error(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor(xent)");
+    per_sm[slot] = n < 1 ? 1 : n;
+    dev_of[slot] = dev.device;
+  }
+  *out = static_cast<int64_t>(dev.sm_count) * per_sm[slot];
+  return UFP8_OK;
 }
 
 bool al(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; }
@@ -371,7 +446,6 @@ extern "C" int ufp8_xent_backward(const void* logits_bf16, int64_t rows, int64_t
   if (fp8 && (!amax || !inv_scale)) return set_error(UFP8_ERR_INVALID, "ufp8_xent_backward: null amax or inv_scale");
   if (!fp8 && !al(dlogits, 2)) return set_error(UFP8_ERR_ALIGN, "ufp8_xent_backward: dlogits not 2-byte aligned");
   const int64_t cpr = (V + kXCols - 1) / kXCols;
-  if (rows * cpr >= (int64_t(1) << 31)) return set_error(UFP8_ERR_INVALID, "ufp8_xent_backward: too many rows");
   DeviceInfo* dev;
   if (int rc = device_info(&dev)) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -396,7 +470,11 @@ extern "C" int ufp8_xent_backward(const void* logits_bf16, int64_t rows, int64_t
   a.vec = al(logits_bf16, 16) && ldl % 8 == 0 && ldo % 8 == 0 && al(dlogits, fp8 ? 8 : 16);
   if (fp8) xent_amax_kernel<<<1, kXAmaxThreads, 0, s>>>(a);
   if (rows > 0) {
-    const unsigned grid = static_cast<unsigned>(rows * cpr);
+    const void* fn = fp8 ? reinterpret_cast<const void*>(xent_grad_kernel<true>)
+                         : reinterpret_cast<const void*>(xent_grad_kernel<false>);
+    int64_t cap_ctas = 0;
+    if (int rc = resident_ctas(fn, *dev, fp8 ? 0 : 1, &cap_ctas)) return rc;
+    const unsigned grid = static_cast<unsigned>(rows * cpr < cap_ctas ? rows * cpr : cap_ctas);
     if (fp8)
       xent_grad_kernel<true><<<grid, kXThreads, 0, s>>>(a);
     else

@@ -213,6 +213,32 @@ def norm_bench(args, dev):
     print(json.dumps({"tokens": T, "d": d, **res}), flush=True)
 
 
+def xent_bench(args, dev):
+    """Cross-entropy kernels on [tokens, vocab] bf16 logits: the row pass (2 B/element), the
+    combine of 128-column partials, and the backward to e5m2 and to bf16 (2 B read + 1 or 2 B
+    written per element); algorithmic GB/s."""
+    T, V = args.tokens, args.vocab
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    logits = (torch.randn((T, V), generator=gen, device=dev) * 3).to(torch.bfloat16)
+    labels = torch.randint(0, V, (T,), generator=gen, device=dev, dtype=torch.int32)
+    dloss = torch.randn((T,), generator=gen, device=dev)
+    lse, _, qrow = ops.xent_rows(logits, labels, None)
+    groups = (V + 127) // 128
+    stats = torch.rand((T, groups, 2), generator=gen, device=dev)
+    n = T * V
+    res = {}
+    for kind, fn, nbytes in (
+            ("rows", lambda: ops.xent_rows(logits, labels, None), 2 * n),
+            ("combine", lambda: ops.xent_combine(stats, logits, V, labels, None), 8 * T * groups),
+            ("grad_e5m2", lambda: ops.xent_grad(logits, labels, None, lse, qrow, dloss, 0.0, C.E5M2), 3 * n),
+            ("grad_e5m2_cap", lambda: ops.xent_grad(logits, labels, None, lse, qrow, dloss, 15.0, C.E5M2), 3 * n),
+            ("grad_bf16", lambda: ops.xent_grad(logits, labels, None, lse, qrow, dloss, 0.0, C.BF16), 4 * n)):
+        us = _time_us(fn, args.reps, args.warmup)
+        res[kind] = {"us": us, "gbs": nbytes / us / 1e3}
+    print(json.dumps({"tokens": T, "vocab": V, **res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
@@ -227,6 +253,8 @@ def main():
     ap.add_argument("--group-m", type=int, default=0, help="tile raster group (0 = library default)")
     ap.add_argument("--quant", action="store_true", help="time amax and quantize on the GMLP tensor sizes instead")
     ap.add_argument("--norm", action="store_true", help="time the RMSNorm kernels on [tokens, d] instead")
+    ap.add_argument("--xent", action="store_true", help="time the cross-entropy kernels on [tokens, vocab] instead")
+    ap.add_argument("--vocab", type=int, default=128256)
     ap.add_argument("--rs-push", action="store_true",
                     help="time the TP-2/4/8 F2 and B4 GEMMs storing locally vs pushing rows to a peer GPU")
     args = ap.parse_args()
@@ -239,6 +267,8 @@ def main():
         return quant_bench(args, dev)
     if args.norm:
         return norm_bench(args, dev)
+    if args.xent:
+        return xent_bench(args, dev)
     if args.rs_push:
         return rs_push_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)

@@ -394,13 +394,14 @@ def _pad16(n: int) -> int:
 
 def xent_rows(logits: torch.Tensor, labels: torch.Tensor, mask: torch.Tensor | None, V: int | None = None):
     """(lse, loss, qrow) f32 [rows] from bf16 logits [rows, >= V] (ufp8_xent_forward)."""
-    if not logits.is_cuda or logits.dtype != torch.bfloat16 or logits.stride(1) != 1:
+    if not logits.is_cuda or logits.dtype != torch.bfloat16 or (logits.numel() and logits.stride(1) != 1):
         raise ValueError("xent_rows: logits must be a CUDA bf16 tensor with unit column stride")
     rows = logits.shape[0]
     V = logits.shape[1] if V is None else V
     lse, loss, qrow = (torch.empty(rows, dtype=torch.float32, device=logits.device) for _ in range(3))
+    ldl = logits.stride(0) if rows else V  # an empty tensor's strides carry no pitch
     _launch("xent_rows", 2.0 * rows * V, lambda: C.xent_forward(
-        logits.data_ptr(), rows, V, logits.stride(0), labels.data_ptr(),
+        logits.data_ptr(), rows, V, ldl, labels.data_ptr(),
         mask.data_ptr() if mask is not None else None, lse.data_ptr(), loss.data_ptr(), qrow.data_ptr(), _stream()))
     return lse, loss, qrow
 
@@ -421,8 +422,9 @@ def xent_grad(logits: torch.Tensor, labels: torch.Tensor, mask: torch.Tensor | N
         amax_t = torch.empty(1, dtype=torch.float32, device=dev)
         inv = torch.empty(1, dtype=torch.float32, device=dev)
     nbytes = (2.0 + (2.0 if fmt == C.BF16 else 1.0)) * rows * V
+    ldl = logits.stride(0) if rows else V
     _launch("xent_grad", nbytes, lambda: C.xent_backward(
-        logits.data_ptr(), rows, V, logits.stride(0), labels.data_ptr(),
+        logits.data_ptr(), rows, V, ldl, labels.data_ptr(),
         mask.data_ptr() if mask is not None else None, lse.data_ptr(),
         qrow.data_ptr() if qrow is not None else None, dloss.data_ptr() if dloss is not None else None,
         float(cap), fmt, out.data_ptr(), ldo, amax_t.data_ptr() if amax_t is not None else None,

@@ -78,7 +78,8 @@ def label_cols(labels, V: int) -> np.ndarray:
 
 def xent_rows(logit_bits: np.ndarray, labels, mask=None):
     """Per row of bf16 logits [rows, V]: (lse, loss, qrow) as f32.  lse = logsumexp in f64;
-    loss = (lse - c[label]) * mask (NaN without a label column); qrow = 1 - exp(c[label] - lse)."""
+    loss = (lse - c[label]) * mask (NaN without a label column); qrow = 1 - exp(c[label] - lse)
+    (float64 here; the kernels compute it with softmax_p's f32 operations)."""
     c = bf16_bits_to_f32(np.asarray(logit_bits, np.uint16)).astype(np.float64)
     rows, V = c.shape
     with np.errstate(invalid="ignore", over="ignore"):
@@ -94,37 +95,55 @@ def xent_rows(logit_bits: np.ndarray, labels, mask=None):
     return lse.astype(np.float32), loss.astype(np.float32), qrow.astype(np.float32)
 
 
+LOG2E = np.float32(1.4426950408889634)
+
+
+def softmax_p(c: np.ndarray, lse: np.ndarray) -> np.ndarray:
+    """p = 2^(c * log2 e - lse * log2 e): the product with log2 e and the sum rounded once (the
+    kernel's FMA; float64 holds the f32 product exactly), exp2 in f32."""
+    nl2 = (np.asarray(lse, np.float32) * -LOG2E).astype(np.float32)
+    x = (c.astype(np.float64) * np.float64(LOG2E) + nl2.astype(np.float64)[..., None]).astype(np.float32)
+    with np.errstate(over="ignore", under="ignore"):
+        return np.exp2(x).astype(np.float32)
+
+
 def xent_backward(logit_bits: np.ndarray, labels, mask, lse, qrow, dloss=None, cap: float = 0.0, fmt: int = E5M2):
-    """dlogits with the kernel's f32 operation order: p = exp(c - lse); d = p - [j == label];
-    v = (dloss * mask) * d; with a cap, v *= 1 - (c * (1 / cap))^2.  fmt BF16: bf16 bits of v.
-    fp8: amax = max_r |g_r| * qrow_r, s = FMAX / amax, codes = fp8(v * s); returns
-    (codes, amax, inv_scale)."""
+    """dlogits with the kernel's f32 operation order: p = softmax_p(c, lse); d = p - [j == label];
+    the row factor w = g (bf16 output) or g * s (fp8), g = dloss * mask; v = d * w; with a cap,
+    v *= 1 - (c * (1 / cap))^2.  fmt BF16: bf16 bits of v.  fp8: amax = max_r |g_r| * qrow_r,
+    s = FMAX / amax, codes = fp8(v); returns (codes, amax, inv_scale)."""
     c = bf16_bits_to_f32(np.asarray(logit_bits, np.uint16))
     rows, V = c.shape
     lse = np.asarray(lse, np.float32).reshape(rows)
     g = np.ones(rows, np.float32) if dloss is None else np.asarray(dloss, np.float32).reshape(rows)
     mk = np.ones(rows, np.float32) if mask is None else np.asarray(mask).astype(np.float32).reshape(rows)
     ge = (g * mk).astype(np.float32)
+    amax = s = inv = None
+    if fmt == BF16:
+        w = ge
+    else:
+        qr = np.asarray(qrow, np.float32).reshape(rows)
+        with np.errstate(invalid="ignore"):
+            per = (np.abs(ge) * qr).astype(np.float32)
+        amax = np.float32(0.0) if rows == 0 else (np.float32(np.nan) if np.isnan(per).any() else per.max())
+        s = scale_from_amax(amax, fmt)
+        with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+            inv = np.float32(np.float32(1.0) / s)
+            w = (ge * s).astype(np.float32)
     with np.errstate(over="ignore", invalid="ignore"):
-        p = np.exp((c - lse[:, None]).astype(np.float32)).astype(np.float32)
+        p = softmax_p(c, lse)
         col = label_cols(labels, V)
         r = np.nonzero(col >= 0)[0]
         p[r, col[r]] = (p[r, col[r]] - np.float32(1.0)).astype(np.float32)
-        v = (ge[:, None] * p).astype(np.float32)
+        v = (p * w[:, None]).astype(np.float32)
         if cap > 0:
             t = (c * np.float32(1.0 / np.float32(cap))).astype(np.float32)
             v = (v * (np.float32(1.0) - (t * t).astype(np.float32)).astype(np.float32)).astype(np.float32)
     if fmt == BF16:
         return f32_to_bf16_bits(v)
-    qr = np.asarray(qrow, np.float32).reshape(rows)
-    with np.errstate(invalid="ignore"):
-        per = (np.abs(ge) * qr).astype(np.float32)
-    amax = np.float32(0.0) if rows == 0 else (np.float32(np.nan) if np.isnan(per).any() else per.max())
-    s = scale_from_amax(amax, fmt)
     with np.errstate(over="ignore", invalid="ignore"):
         cast = f32_to_fp8_fast if _path.FAST_CAST else f32_to_fp8  # same codes (fp8.py)
-        codes = cast((v * s).astype(np.float32), fmt)
-        inv = np.float32(np.float32(1.0) / s)
+        codes = cast(v, fmt)
     return codes, np.float32(amax), inv
 
 

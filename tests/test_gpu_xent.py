@@ -204,18 +204,25 @@ def test_output_head_fused_loss_against_oracle(cuda, cap, V):
 
 def test_fused_and_generic_paths_agree(cuda):
     """The generic path (any projection: the reference's chunking, checkpointed chunks, the
-    bf16-logit kernels) against the fused node on the same head.  The losses agree within the
-    bf16 resolution of the logits (torch's soft cap divides by 15 through a reciprocal, the fused
-    epilogue with an IEEE division, so a capped logit may differ by one bf16 step; with several
-    chunks the input's fp8 scale is per chunk).  The gradients are two fp8 quantisations of the
-    logit gradient with different scales (the generic Einsum takes max |dl| of the bf16 gradient,
-    the fused node its bound from the row results), so they agree within e5m2 resolution."""
+    bf16-logit kernels) against the fused node on the same head, and, with several chunks,
+    against the oracle's head applied chunk by chunk.
+
+    One chunk: the losses agree within the bf16 resolution of the logits (torch's soft cap divides
+    by 15 through a reciprocal, the fused epilogue with an IEEE division, so a capped logit may
+    differ by one bf16 step).  The gradients are two fp8 quantisations of the logit gradient with
+    different scales (the generic Einsum takes max |dl| of the bf16 gradient, the fused node its
+    bound from the row results): each term of dX = dL W^T may round by up to 2^-3 in either, so an
+    element may differ by up to 2 x 2^-3 of its largest terms (max relative error 0.25); the cosine
+    is the tight check.  Several chunks: every chunk quantises its input with its own scale, as the
+    reference's chunks do, so the losses follow the per-chunk oracle, and the gradients differ from
+    the fused node's by the input's e4m3 rounding as well (cosine 0.99)."""
     import torch
     from macrogpt_jax_b200 import next_token_loss as ntl
     B, S, d, V = 2, 96, 256, 1024
     head = _head(cuda, d, V, "tanh", seed=3)
     rng = np.random.default_rng(9)
-    inputs = _dev(rng.integers(0, V, (B, S)), cuda)
+    tokens = rng.integers(0, V, (B, S))
+    inputs = _dev(tokens, cuda)
     xb = op.bf16_normal(rng, (B * S, d))
 
     def run(proj, chunk):
@@ -226,12 +233,23 @@ def test_fused_and_generic_paths_agree(cuda):
         return _np(loss), x.grad.float().cpu().numpy(), head.lm_head.w.grad.float().cpu().numpy()
 
     fused = run(head.get_logits, 1024)
-    for chunk in (1024, 64):  # one chunk; chunks of 64 and 32 positions
-        other = run(lambda a: head.get_logits(a), chunk)
-        np.testing.assert_allclose(other[0], fused[0], atol=2e-2)
-        assert np.abs(other[0] - fused[0]).mean() <= 2e-3
-        compare(other[1], fused[1], rel_tol=5e-2, cos_tol=0.998)
-        compare(other[2], fused[2], rel_tol=5e-2, cos_tol=0.998)
+    one = run(lambda a: head.get_logits(a), 1024)
+    np.testing.assert_allclose(one[0], fused[0], atol=2e-2)
+    assert np.abs(one[0] - fused[0]).mean() <= 2e-3
+    compare(one[1], fused[1], rel_tol=0.25, cos_tol=0.998)
+    compare(one[2], fused[2], rel_tol=0.25, cos_tol=0.998)
+    chunked = run(lambda a: head.get_logits(a), 64)  # chunks of 64 and 32 positions
+    targets, mask = ox.ntp_args(tokens)
+    xs = xb.reshape(B, S, d)
+    sb, wb = torch_bf16_to_bits(head.norm.scale), torch_bf16_to_bits(head.lm_head.w)
+    for s0, e0 in ((0, 64), (64, 96)):
+        rl, _ = ox.head_forward(xs[:, s0:e0].reshape(-1, d), sb, False, head.norm.eps, wb,
+                                targets[:, s0:e0].reshape(-1), mask[:, s0:e0].reshape(-1), 15.0)
+        got = chunked[0][:, s0:e0].reshape(-1)
+        np.testing.assert_allclose(got, rl, atol=2e-2)
+        assert np.abs(got - rl).mean() <= 3e-3
+    compare(chunked[1], fused[1], rel_tol=0.25, cos_tol=0.99)
+    compare(chunked[2], fused[2], rel_tol=0.25, cos_tol=0.99)
 
 
 def test_full_vocabulary_properties(cuda):
