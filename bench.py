@@ -41,6 +41,9 @@ CONFIGS = {
     # the output head of the Llama-3-8B shape (final RMSNorm, lm_head 4096 -> 128256, soft cap) and
     # the next-token loss, forward and backward, on one GPU
     "head_xent_v128256": dict(kind="head", d=4096, V=128256, B=4, S=4096),
+    # Muon's Newton-Schulz orthogonalisation of one GMLP block's gradients at d 4096 / h 14336:
+    # the fused weight's two [4096, 14336] slices and the down weight [14336, 4096], f32 in and out
+    "muon_ns_d4096_h14336": dict(kind="muon", d=4096, h=14336, steps=5),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
 GMLP_D4096_GEMM_TRAFFIC = 1.651e9  # DRAM bytes per GEMM launch, T 16384 / d 4096 / h 14336, from one ncu
@@ -62,6 +65,13 @@ def head_flops_per_step(T, d, V):
     """lm_head fwd+bwd: logits 2 T d V, dX 2 T d V, dW 2 T d V (the reference's rematerialised
     recomputation of the logits in its backward is not counted)."""
     return 6.0 * T * d * V
+
+
+def ns_flops(m, n, steps):
+    """Newton-Schulz on one [m, n] slice: per step X X^T (2 s^2 l), A A (2 s^3), B X (2 s^2 l)
+    with s = min(m, n), l = max(m, n)."""
+    s_, l_ = min(m, n), max(m, n)
+    return steps * (4.0 * s_ * s_ * l_ + 2.0 * s_ ** 3)
 
 
 def load_peaks():
@@ -424,6 +434,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         return run_attn(args, cfg, rank, world, local_rank, dev)
     if cfg["kind"] == "head":
         return run_head(args, cfg, rank, world, local_rank, dev)
+    if cfg["kind"] == "muon":
+        return run_muon(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
     if world > 1 and cfg.get("norm"):
@@ -821,6 +833,86 @@ def run_head(args, cfg, rank, world, local_rank, dev):
     return out
 
 
+def run_muon(args, cfg, rank, world, local_rank, dev):
+    """orthogonalize(grad_fused) and orthogonalize(grad_down) (ueaj/opt/multiscale.py:110-141) per
+    step, the canonical GMLP weight layouts [2, d, h] and [h, d], f32 in and out."""
+    import numpy as np
+    import torch
+    from macrogpt_jax_b200 import _capi, ops
+    from macrogpt_jax_b200.muon import orthogonalize
+    if world > 1:
+        raise SystemExit("the Newton-Schulz workload runs on one GPU")
+    d, h, steps = cfg["d"], cfg["h"], cfg["steps"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    gf = torch.randn((2, d, h), generator=gen, device=dev) * 1e-3
+    gd = torch.randn((h, d), generator=gen, device=dev) * 1e-3
+    fl = 3 * ns_flops(d, h, steps)
+
+    def step(a, b):
+        return orthogonalize(a, ns_steps=steps), orthogonalize(b, ns_steps=steps)
+
+    for _ in range(args.warmup):
+        step(gf, gd)
+    torch.cuda.synchronize()
+    timer = ops.KernelTimer()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = _capi.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.set_timer(timer)
+    ev0.record()
+    for _ in range(args.steps):
+        step(gf, gd)
+    ev1.record()
+    ops.set_timer(None)
+    torch.cuda.synchronize()
+    launches = _capi.launches - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    summ = timer.summary()
+    peaks, peak_src = load_peaks()
+    n_n, n_ms, n_fl = summ.get("newton_schulz", (0, 0.0, 0.0))
+    achieved = n_fl / (n_ms / 1000.0) / 1e12 if n_n else None
+    out = {
+        "metric": "Muon Newton-Schulz orthogonalisation TFLOP/s (bf16 tcgen05 GEMMs)",
+        "value": fl * args.steps / (ms / 1000.0) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": args.config_desc, "slices": [[d, h], [d, h], [h, d]], "ns_steps": steps,
+                   "parallelism": "single GPU", "l2": "inputs larger than L2"},
+        "roofline": {"kernel": "ufp8_newton_schulz (bf16 gemm_fp8_pair_kernel + normalisation)", "bound": "tensor",
+                     "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": (achieved / peaks["bf16_tflops_sustained"]) if achieved else None,
+                     "peak_source": f"bf16_tflops_sustained (cuBLAS bf16 under the power cap), {peak_src}",
+                     "launches": n_n, "time_share": n_ms / ms if ms else None, "traffic": None},
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if not args.no_e2e:
+        def e2e_step(xb, yb):
+            _, b = step(xb, yb)
+            return b, None
+        ems = e2e_pipelined(e2e_step, gf, gd, args.steps, lambda: None, y_like=gd)
+        out["e2e"] = {"value": fl * args.steps / (ems / 1000.0) / 1e12, "unit": "TFLOP/s",
+                      "ms_per_step": ems / args.steps, "h2d_bytes_per_step": (gf.numel() + gd.numel()) * 4,
+                      "d2h_bytes_per_step": gd.numel() * 4,
+                      "path": "orthogonalize() on both gradients; every step copies them from pinned host memory "
+                              "(side stream, double-buffered) and reads the down weight's update back"}
+    if not args.no_cpu_baseline:
+        from oracle import muon as om
+        rng = np.random.default_rng(0)
+        g1 = rng.standard_normal((1, d, h)).astype(np.float32)
+        t0 = time.perf_counter()
+        om.orthogonalize_f64(g1, om.coefficients(steps), dtype=np.float32)
+        t1 = time.perf_counter() - t0
+        est = 3 * t1  # the three slices have the same shape up to a transpose
+        out["cpu_baseline"] = {"value": fl / est / 1e12, "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+                               "sample": f"the oracle's Newton-Schulz (numpy float32 BLAS on all host threads) on "
+                                         f"one [{d}, {h}] slice, {steps} steps, times 3 slices",
+                               "est_ms_per_step": est * 1000.0}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -855,6 +947,12 @@ def main():
         args.config_desc = (f"attention projections fwd+bwd (fused QKV {cfg['d']}->{3 * cfg['d']}, O "
                             f"{cfg['d']}->{cfg['d']}), {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
                             f"{cfg['heads']} heads x {cfg['head_d']}, FP8 e4m3/e5m2")
+        if args.impl == "reference":
+            raise SystemExit("the CPU arm covers the GMLP workloads")
+    elif cfg["kind"] == "muon":
+        args.config_desc = (f"Muon Newton-Schulz ({cfg['steps']} steps, coefficients 3.4445/-4.7750/2.0315) of a GMLP "
+                            f"block's gradients: [2, {cfg['d']}, {cfg['h']}] and [{cfg['h']}, {cfg['d']}], f32 in/out, "
+                            "bf16 GEMMs")
         if args.impl == "reference":
             raise SystemExit("the CPU arm covers the GMLP workloads")
     elif cfg["kind"] == "head":

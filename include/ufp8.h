@@ -58,7 +58,8 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 /* fp8 formats (values match the MMA instruction-descriptor encoding) */
 #define UFP8_E4M3 0 /* float8_e4m3fn: forward operands, max 448   */
 #define UFP8_E5M2 1 /* float8_e5m2:   gradients,        max 57344 */
-#define UFP8_BF16 2 /* unquantised bf16 (output format of ufp8_xent_backward only) */
+#define UFP8_BF16 2 /* bf16: the operand format of the 16-bit GEMM (both operands of a ufp8_gemm), and the
+                     unquantised gradient output of ufp8_xent_backward */
 
 /* operand storage order */
 #define UFP8_K_MAJOR 0  /* stored [rows = M or N][K], K contiguous   */
@@ -74,6 +75,7 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_EPI_DSWIGLU 2 /* dH = acc*sa*sb; D[0]=dU, D[1]=dG from saved U,G; amax |dUG| */
 #define UFP8_EPI_RS_PUSH 3 /* D rows stored into their owner rank's reduce-scatter staging slot */
 #define UFP8_EPI_XENT 4    /* D = logits (bf16, optionally soft-capped) + per-row softmax partials  */
+#define UFP8_EPI_AXPBY 5   /* D = alpha * acc * sa * sb + beta * C (bf16 operands only)            */
 
 const char* ufp8_last_error(void);
 int ufp8_abi_version(void);
@@ -204,6 +206,15 @@ typedef struct ufp8_gemm_desc {
   int64_t xent_ld_stats;
   float xent_cap;
   int32_t xent_reserved;
+  /* AXPBY: D = alpha * (acc * sa * sb) + beta * C, with C bf16 [batch][M, N] (pitch ldc elements,
+   * slice pitch c_batch_stride); each product and the sum rounded once in f32, then D's type.
+   * With bf16 operands (fmt UFP8_BF16 for both A and B) inv_scale may be NULL (factor 1); only
+   * the STORE and AXPBY epilogues take bf16 operands, on the CTA-pair kernel. */
+  const void* c;
+  int64_t ldc;
+  int64_t c_batch_stride;
+  float alpha;
+  float beta;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);
@@ -239,6 +250,22 @@ int ufp8_xent_combine(const float* stats, int64_t ld_stats, const void* logits_b
 int ufp8_xent_backward(const void* logits_bf16, int64_t rows, int64_t V, int64_t ldl, const int32_t* labels,
                        const uint8_t* mask, const float* lse, const float* qrow, const float* dloss, float cap,
                        int fmt, void* dlogits, int64_t ldo, float* amax, float* inv_scale, ufp8_stream_t stream);
+
+/* ---- Newton-Schulz orthogonalisation (Muon) ------------------------------------------------
+ * Replaces orthogonalize (ueaj/opt/multiscale.py:110-141): optax.contrib's
+ * orthogonalize_via_newton_schulz (optax 0.2.6) mapped over `batch` slices g[b] of shape [m, n]
+ * (f32 or bf16, contiguous).  Per slice: work on X^T when m > n; X = X / (||X||_F + eps); then for
+ * each of `steps` coefficient triples (a, b, c) (host array coeffs[steps][3]):
+ *   A = X X^T, B = b A + c A A, X = a X + B X,
+ * each product a bf16 tcgen05 GEMM (fp32 accumulation) and each update its AXPBY epilogue; X, A
+ * and B are rounded to bf16 between the GEMMs (optax runs the iteration in the input's dtype, f32
+ * under the reference's Muon), and the last step is written to `out` (f32 or bf16, [batch][m][n]).
+ * m and n must be multiples of 8; batch <= 65535.  workspace: ufp8_newton_schulz_workspace bytes,
+ * 256-byte aligned.  Stream-ordered; 2 + 3 * steps launches. */
+int ufp8_newton_schulz_workspace(int64_t batch, int64_t m, int64_t n, int64_t* bytes);
+int ufp8_newton_schulz(const void* g, int g_dtype, int64_t batch, int64_t m, int64_t n, int steps,
+                       const float* coeffs, float eps, void* out, int out_dtype, void* workspace,
+                       int64_t workspace_bytes, ufp8_stream_t stream);
 
 /* ---- tensor-parallel reduce-scatter over NVLink peer memory ------------------------------
  * Replaces the reduce-scatter XLA/GSPMD would insert after the row-split down projection of

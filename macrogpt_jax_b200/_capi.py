@@ -16,10 +16,10 @@ STATUS_WAIT_TIMEOUT, STATUS_PEER_TIMEOUT = 1, 2
 IPC_HANDLE_BYTES = 64
 AG_COPY_ENGINE, AG_SM = 0, 1
 E4M3, E5M2 = 0, 1
-BF16 = 2  # unquantised output of ufp8_xent_backward
+BF16 = 2  # bf16 GEMM operands; unquantised output of ufp8_xent_backward
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
-EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH, EPI_XENT = 0, 1, 2, 3, 4
+EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH, EPI_XENT, EPI_AXPBY = 0, 1, 2, 3, 4, 5
 GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE, GEMM_CTA_PAIR_N512 = (
     0, 1, 2, 3, 4, 5)
 
@@ -53,6 +53,8 @@ EXPORTED_SYMBOLS = (
     "ufp8_xent_forward",
     "ufp8_xent_combine",
     "ufp8_xent_backward",
+    "ufp8_newton_schulz_workspace",
+    "ufp8_newton_schulz",
 )
 
 
@@ -101,6 +103,11 @@ class GemmDesc(ctypes.Structure):
         ("xent_ld_stats", ctypes.c_int64),
         ("xent_cap", ctypes.c_float),
         ("xent_reserved", ctypes.c_int32),
+        ("c", ctypes.c_void_p),
+        ("ldc", ctypes.c_int64),
+        ("c_batch_stride", ctypes.c_int64),
+        ("alpha", ctypes.c_float),
+        ("beta", ctypes.c_float),
     ]
 
 
@@ -156,12 +163,15 @@ def load() -> ctypes.CDLL:
     lib.ufp8_xent_forward.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, vp]
     lib.ufp8_xent_combine.argtypes = [vp, i64, vp, i64, i64, i64, vp, vp, vp, vp, vp, vp]
     lib.ufp8_xent_backward.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, f32, i32, vp, i64, vp, vp, vp]
+    lib.ufp8_newton_schulz_workspace.argtypes = [i64, i64, i64, ctypes.POINTER(i64)]
+    lib.ufp8_newton_schulz.argtypes = [vp, i32, i64, i64, i64, i32, vp, f32, vp, i32, vp, i64, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
                  "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
                  "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
-                 "ufp8_rmsnorm_backward", "ufp8_xent_forward", "ufp8_xent_combine", "ufp8_xent_backward"):
+                 "ufp8_rmsnorm_backward", "ufp8_xent_forward", "ufp8_xent_combine", "ufp8_xent_backward",
+                 "ufp8_newton_schulz_workspace", "ufp8_newton_schulz"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -245,6 +255,21 @@ def xent_backward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, qrow_
     check(load().ufp8_xent_backward(logits_ptr, rows, V, ldl, labels_ptr, mask_ptr, lse_ptr, qrow_ptr, dloss_ptr,
                                     cap, fmt, out_ptr, ldo, amax_ptr, inv_ptr, stream))
     _count((1 if fmt != BF16 else 0) + (1 if rows > 0 else 0))
+
+
+def newton_schulz_workspace(batch: int, m: int, n: int) -> int:
+    out = ctypes.c_int64(0)
+    check(load().ufp8_newton_schulz_workspace(batch, m, n, ctypes.byref(out)))
+    return out.value
+
+
+def newton_schulz(g_ptr, g_dtype, batch, m, n, coeffs, eps, out_ptr, out_dtype, ws_ptr, ws_bytes, stream) -> None:
+    """ufp8_newton_schulz; coeffs: a sequence of (a, b, c) triples, one per step."""
+    flat = [float(v) for abc in coeffs for v in abc]
+    arr = (ctypes.c_float * len(flat))(*flat)
+    check(load().ufp8_newton_schulz(g_ptr, g_dtype, batch, m, n, len(flat) // 3, arr, eps, out_ptr, out_dtype,
+                                    ws_ptr, ws_bytes, stream))
+    _count((2 + 3 * (len(flat) // 3)) if batch > 0 else 0)
 
 
 def gemm(desc: GemmDesc, stream: int) -> None:

@@ -81,6 +81,10 @@ struct GemmArgs {
   float* xent_stats;  // XENT: per-row (max, sum exp) of each 128-column group
   long long xent_ld;
   float xent_cap;     // XENT: soft cap (0 = none)
+  const __nv_bfloat16* c;  // AXPBY (bf16 operands): D = alpha * acc * sa * sb + beta * C
+  long long ldc, c_bstride;
+  float alpha_mul, beta;
+  int c_vec;  // AXPBY: C rows 16-byte aligned
 };
 
 // Waits until the all-gather block of rank s has arrived (flag == epoch), bounded like the
@@ -632,7 +636,12 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 // KCH = 128-byte K chunks per ring stage (1 or 2): a stage holds KCH A sub-tiles followed by KCH
 // B sub-tiles of 16 KiB each, and the MMA thread issues 4 * KCH MMAs per stage, so the per-stage
 // barrier hand-offs (full -> MMA issue -> commit -> empty -> next load) occur half as often.
-template <int NSTAGES, int kVar, int KCH = 1>
+// kBf16: bf16 operands (tcgen05.mma kind::f16).  The ring stages hold the same bytes: a 128-byte K
+// chunk is 64 elements, a K-major sub-tile 128 rows x 128 B as for fp8, and an MN-major sub-tile
+// two 64-element (128-byte) MN atoms of 64 K rows each, 8 KiB apart (the descriptor's leading
+// byte offset).  Each MMA consumes K = 16 (32 bytes), four per chunk as with fp8.  Only the STORE
+// and AXPBY epilogues are compiled in.
+template <int NSTAGES, int kVar, int KCH = 1, bool kBf16 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmUG, const __grid_constant__ CUtensorMap tmD,
@@ -714,7 +723,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         for (int ks = 0; ks < total_k; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
           const int kb = ks / args.ksteps;
-          const int k0 = (ks - kb * args.ksteps) * (KCH * kBK);
+          constexpr int kKc = kBf16 ? kBK / 2 : kBK;  // K elements per 128-byte chunk
+          const int k0 = (ks - kb * args.ksteps) * (KCH * kKc);
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + KCH * kPHalfBytes;
           if (leader) {
@@ -734,16 +744,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
 #pragma unroll
           for (int j = 0; j < KCH; ++j) {
-            // K chunks past K (or past this slice's K for k_batches) read as zeros.
-            const int kj = k0 + j * kBK;
-            if (args.a_major == UFP8_K_MAJOR)
-              tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, kj, row0, az);
-            else
-              tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, row0, kj, az);
-            if (args.b_major == UFP8_K_MAJOR)
-              tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, kj, n0, bz);
-            else
-              tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, n0, kj, bz);
+            // K chunks past K (or past this slice's K for k_batches) read as zeros.  The tensor
+            // maps address bytes along their contiguous dimension.
+            const int kj = k0 + j * kKc;
+            if constexpr (kBf16) {
+              if (args.a_major == UFP8_K_MAJOR) {
+                tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, 2 * kj, row0, az);
+              } else {
+                tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, 2 * row0, kj, az);
+                tma_load_3d_pair(sa + j * kPHalfBytes + kPHalfBytes / 2, &tmA, bar, 2 * row0 + 128, kj, az);
+              }
+              if (args.b_major == UFP8_K_MAJOR) {
+                tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, 2 * kj, n0, bz);
+              } else {
+                tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, 2 * n0, kj, bz);
+                tma_load_3d_pair(sb + j * kPHalfBytes + kPHalfBytes / 2, &tmB, bar, 2 * n0 + 128, kj, bz);
+              }
+            } else {
+              if (args.a_major == UFP8_K_MAJOR)
+                tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, kj, row0, az);
+              else
+                tma_load_3d_pair(sa + j * kPHalfBytes, &tmA, bar, row0, kj, az);
+              if (args.b_major == UFP8_K_MAJOR)
+                tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, kj, n0, bz);
+              else
+                tma_load_3d_pair(sb + j * kPHalfBytes, &tmB, bar, n0, kj, bz);
+            }
           }
           if (++stage == NSTAGES) {
             stage = 0;
@@ -786,11 +812,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             const uint32_t sb = sa0 + (KCH + j) * kPHalfBytes;
 #pragma unroll
             for (int kk = 0; kk < kBK / 32; ++kk) {
+              // MN-major: an MMA's K rows are 128 bytes apart (32 rows for fp8, 16 for bf16); the
+              // bf16 sub-tile's second MN atom sits half a sub-tile further (leading byte offset).
+              constexpr uint32_t kMnStep = kBf16 ? 16 * 128 : 32 * 128;
+              constexpr uint32_t kMnLbo = kBf16 ? kPHalfBytes / 2 : kPHalfBytes;
               const uint64_t adesc = args.a_major == UFP8_K_MAJOR ? make_sdesc_sw128(sa + kk * 32, 16, 1024)
-                                                                  : make_sdesc_sw128(sa + kk * 32 * 128, kPHalfBytes, 1024);
+                                                                  : make_sdesc_sw128(sa + kk * kMnStep, kMnLbo, 1024);
               const uint64_t bdesc = args.b_major == UFP8_K_MAJOR ? make_sdesc_sw128(sb + kk * 32, 16, 1024)
-                                                                  : make_sdesc_sw128(sb + kk * 32 * 128, kPHalfBytes, 1024);
-              umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | j | kk) != 0 ? 1u : 0u);
+                                                                  : make_sdesc_sw128(sb + kk * kMnStep, kMnLbo, 1024);
+              if constexpr (kBf16)
+                umma_f16_pair(d_tmem, adesc, bdesc, args.idesc, (ks | j | kk) != 0 ? 1u : 0u);
+              else
+                umma_f8f6f4_pair(d_tmem, adesc, bdesc, args.idesc, (ks | j | kk) != 0 ? 1u : 0u);
             }
           }
           umma_commit_pair(&empty[stage], 0x3);
@@ -813,7 +846,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     const int quad = warp & 3;   // TMEM lanes this warp may read: [32*quad, 32*quad+32)
     const int chalf = e >> 2;    // which half of the tile's columns this warp handles
     const int row_in_tile = static_cast<int>(rank) * kBM + quad * 32 + lane;
-    const float alpha = __fmul_rn(*args.inv_a, *args.inv_b);
+    // fp8: alpha = sa * sb; bf16 operands: scales optional (1), times the AXPBY / STORE multiplier.
+    const float alpha = kBf16 ? __fmul_rn(__fmul_rn(args.inv_a ? *args.inv_a : 1.0f, args.inv_b ? *args.inv_b : 1.0f),
+                                          args.alpha_mul)
+                              : __fmul_rn(*args.inv_a, *args.inv_b);
     const int vec = args.vec_ok;
     const uint32_t tempty_leader0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint64_t stream = l2_policy_evict_first();  // outputs are not re-read by this kernel
@@ -967,7 +1003,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             }
           }
         }
-      } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH || args.mode == UFP8_EPI_XENT) {
+      } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH || args.mode == UFP8_EPI_XENT ||
+                 args.mode == UFP8_EPI_AXPBY) {
         // RS_PUSH: this row goes to its owner's staging slot for this rank (peer memory).
         // XENT: bf16 logits (soft-capped if asked) and the softmax partials of this warp's 128 columns.
         const bool xent = args.mode == UFP8_EPI_XENT;
@@ -986,24 +1023,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           const int col0 = nb * kBN + c;
           if (row_ok && col0 < args.N) {
             const int valid = args.N - col0;
+            float am = alpha;  // the accumulator multiplier of the stores below
+            if constexpr (kBf16) {
+              if (args.c != nullptr) {
+                // AXPBY: v = acc * alpha + beta * C, each product and the sum rounded once.
+                const __nv_bfloat16* cp = args.c + g * args.c_bstride + static_cast<long long>(row) * args.ldc + col0;
+                uint32_t cw[2][8];
+                load_bf16x16_packed(cp, cw[0], valid, args.c_vec);
+                load_bf16x16_packed(cp + 16, cw[1], valid - 16, args.c_vec);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const uint32_t w2 = cw[j >> 4][(j & 15) >> 1];
+                  const float cv = (j & 1) ? hi_f(w2) : lo_f(w2);
+                  r[j] = __float_as_uint(__fadd_rn(__fmul_rn(__uint_as_float(r[j]), alpha), __fmul_rn(cv, args.beta)));
+                }
+                am = 1.0f;
+              }
+            }
             if (args.d_f32) {
               float* p = static_cast<float*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
               if (vec && valid >= 32) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
                   reinterpret_cast<float4*>(p)[i] =
-                      make_float4(__uint_as_float(r[4 * i]) * alpha, __uint_as_float(r[4 * i + 1]) * alpha,
-                                  __uint_as_float(r[4 * i + 2]) * alpha, __uint_as_float(r[4 * i + 3]) * alpha);
+                      make_float4(__uint_as_float(r[4 * i]) * am, __uint_as_float(r[4 * i + 1]) * am,
+                                  __uint_as_float(r[4 * i + 2]) * am, __uint_as_float(r[4 * i + 3]) * am);
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                  if (j < valid) p[j] = __uint_as_float(r[j]) * alpha;
+                  if (j < valid) p[j] = __uint_as_float(r[j]) * am;
               }
             } else {
               uint32_t o[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j)
-                o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * alpha, __uint_as_float(r[2 * j + 1]) * alpha);
+                o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * am, __uint_as_float(r[2 * j + 1]) * am);
               if (xent) xent_chunk(o, valid, args.xent_cap, xm, xs);
               __nv_bfloat16* p = rs_row ? rs_row + col0
                                         : static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride + row * args.ldd + col0;
@@ -1498,19 +1552,21 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 3-D map over one fp8 operand: x = contiguous index, y = the other matrix index,
-// z = batch slice.  Box = 128 x 128 x 1 bytes with 128-byte swizzle.
+// 3-D map over one operand in bytes: x = contiguous index (bytes), y = the other matrix index,
+// z = batch slice.  Box = 128 bytes x 128 rows (x 64 rows for an MN-major bf16 operand, whose
+// sub-tile is two such boxes) x 1, 128-byte swizzle.
 int encode_operand(CUtensorMap* map, const ufp8_operand& op, int64_t rows, int64_t K, const char* name) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return set_error(UFP8_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const int64_t esz = op.fmt == UFP8_BF16 ? 2 : 1;
   const int64_t inner = op.major == UFP8_K_MAJOR ? K : rows;
   const int64_t outer = op.major == UFP8_K_MAJOR ? rows : K;
   const int64_t slices = op.batch_count < 1 ? 1 : op.batch_count;
   const int64_t bstride = slices > 1 ? op.batch_stride : op.ld * outer;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner * esz), static_cast<cuuint64_t>(outer),
                         static_cast<cuuint64_t>(slices)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld), static_cast<cuuint64_t>(bstride)};
-  cuuint32_t box[3] = {128, 128, 1};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(op.ld * esz), static_cast<cuuint64_t>(bstride * esz)};
+  cuuint32_t box[3] = {128, (esz == 2 && op.major == UFP8_MN_MAJOR) ? 64u : 128u, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(op.ptr), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1558,9 +1614,10 @@ int encode_bf16_boxes(CUtensorMap* map, void* base, int64_t cols, int64_t rows, 
 
 int check_operand(const ufp8_operand& op, int64_t rows, int64_t K, int need_slices, const char* name) {
   if (!op.ptr) return set_error(UFP8_ERR_INVALID, "operand %s: null pointer", name);
-  if (!op.inv_scale) return set_error(UFP8_ERR_INVALID, "operand %s: null inv_scale", name);
-  if (op.fmt != UFP8_E4M3 && op.fmt != UFP8_E5M2)
-    return set_error(UFP8_ERR_INVALID, "operand %s: fmt %d is not UFP8_E4M3/UFP8_E5M2", name, op.fmt);
+  if (op.fmt != UFP8_E4M3 && op.fmt != UFP8_E5M2 && op.fmt != UFP8_BF16)
+    return set_error(UFP8_ERR_INVALID, "operand %s: fmt %d is not UFP8_E4M3/UFP8_E5M2/UFP8_BF16", name, op.fmt);
+  if (!op.inv_scale && op.fmt != UFP8_BF16) return set_error(UFP8_ERR_INVALID, "operand %s: null inv_scale", name);
+  const int64_t esz = op.fmt == UFP8_BF16 ? 2 : 1;
   if (op.major != UFP8_K_MAJOR && op.major != UFP8_MN_MAJOR)
     return set_error(UFP8_ERR_INVALID, "operand %s: major %d is not K/MN", name, op.major);
   const int64_t inner = op.major == UFP8_K_MAJOR ? K : rows;
@@ -1568,15 +1625,15 @@ int check_operand(const ufp8_operand& op, int64_t rows, int64_t K, int need_slic
                                       static_cast<long long>(op.ld), static_cast<long long>(inner));
   if (reinterpret_cast<uintptr_t>(op.ptr) & 15u)
     return set_error(UFP8_ERR_ALIGN, "operand %s: base pointer is not 16-byte aligned", name);
-  if (op.ld % 16 != 0)
+  if ((op.ld * esz) % 16 != 0)
     return set_error(UFP8_ERR_ALIGN, "operand %s: ld %lld is not a multiple of 16 bytes", name,
                      static_cast<long long>(op.ld));
-  if (op.batch_count > 1 && op.batch_stride % 16 != 0)
+  if (op.batch_count > 1 && (op.batch_stride * esz) % 16 != 0)
     return set_error(UFP8_ERR_ALIGN, "operand %s: batch_stride is not a multiple of 16 bytes", name);
   if (need_slices > 1 && op.batch_count < need_slices)
     return set_error(UFP8_ERR_INVALID, "operand %s: needs %d batch slices, has %d", name, need_slices,
                      op.batch_count);
-  if (inner >= (int64_t(1) << 31) || (op.major == UFP8_K_MAJOR ? rows : K) >= (int64_t(1) << 31))
+  if (inner * esz >= (int64_t(1) << 31) || (op.major == UFP8_K_MAJOR ? rows : K) >= (int64_t(1) << 31))
     return set_error(UFP8_ERR_INVALID, "operand %s: extent exceeds 2^31", name);
   return UFP8_OK;
 }
@@ -1592,8 +1649,21 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (d.batch > 1 && d.k_batches > 1)
     return set_error(UFP8_ERR_UNSUPPORTED, "batch > 1 together with k_batches > 1 is not supported");
   if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU &&
-      d.epilogue != UFP8_EPI_RS_PUSH && d.epilogue != UFP8_EPI_XENT)
+      d.epilogue != UFP8_EPI_RS_PUSH && d.epilogue != UFP8_EPI_XENT && d.epilogue != UFP8_EPI_AXPBY)
     return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
+  const bool bf16 = d.a.fmt == UFP8_BF16;
+  if (bf16 != (d.b.fmt == UFP8_BF16))
+    return set_error(UFP8_ERR_INVALID, "A and B must both be fp8 or both be bf16 (one MMA kind)");
+  if (bf16 && d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_AXPBY)
+    return set_error(UFP8_ERR_UNSUPPORTED, "bf16 operands take the STORE and AXPBY epilogues only");
+  if (d.epilogue == UFP8_EPI_AXPBY) {
+    if (!bf16) return set_error(UFP8_ERR_UNSUPPORTED, "AXPBY takes bf16 operands");
+    if (!d.c || d.ldc < d.N) return set_error(UFP8_ERR_INVALID, "AXPBY needs c with ldc >= N");
+    if (reinterpret_cast<uintptr_t>(d.c) & 1u) return set_error(UFP8_ERR_ALIGN, "AXPBY: c not 2-byte aligned");
+    if (d.K == 0 && d.M > 0 && d.N > 0) return set_error(UFP8_ERR_UNSUPPORTED, "AXPBY with K == 0");
+  }
+  if (bf16 && (variant == UFP8_GEMM_SINGLE_CTA || d.ag_flags != nullptr))
+    return set_error(UFP8_ERR_UNSUPPORTED, "bf16 operands run on the CTA-pair kernel without all-gather");
   if (d.epilogue == UFP8_EPI_XENT) {
     if (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1)
       return set_error(UFP8_ERR_INVALID, "XENT needs bf16 output and batch 1");
@@ -1673,6 +1743,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.xent_stats = d.epilogue == UFP8_EPI_XENT ? d.xent_stats : nullptr;
   a.xent_ld = d.xent_ld_stats;
   a.xent_cap = d.xent_cap;
+  a.c = d.epilogue == UFP8_EPI_AXPBY ? static_cast<const __nv_bfloat16*>(d.c) : nullptr;
+  a.ldc = d.ldc;
+  a.c_bstride = d.c_batch_stride;
+  a.alpha_mul = d.epilogue == UFP8_EPI_AXPBY ? d.alpha : 1.0f;
+  a.beta = d.beta;
+  a.c_vec = a.c != nullptr && aligned16(d.c) && (d.ldc * 2) % 16 == 0 && (d.c_batch_stride * 2) % 16 == 0;
 
   if (d.K == 0) {
     if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");
@@ -1711,8 +1787,8 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     a.group_m = static_cast<int>(std::min<int64_t>(a.group_m, d.ag_rows_per_rank / bm));
   }
   a.idesc = (1u << 4)                                       // f32 accumulator
-            | (static_cast<uint32_t>(d.a.fmt) << 7)         // A format
-            | (static_cast<uint32_t>(d.b.fmt) << 10)        // B format
+            | (static_cast<uint32_t>(bf16 ? 1 : d.a.fmt) << 7)   // A format (kind::f16: 1 = bf16)
+            | (static_cast<uint32_t>(bf16 ? 1 : d.b.fmt) << 10)  // B format
             | (static_cast<uint32_t>(d.a.major) << 15)      // A major
             | (static_cast<uint32_t>(d.b.major) << 16)      // B major
             | (static_cast<uint32_t>(kBN >> 3) << 17)       // N = 256
@@ -1757,6 +1833,9 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
                                cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWideUg);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(gemm_fp8_n512_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kWSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmemBytesWide);
     if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm smem)");
     attr_device = dev.device;
   }
@@ -1781,19 +1860,20 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   // long-K GMLP contractions (F2 650 vs 680 us, B4 1250 vs 1311 us, B3 1305 vs 1333 us), but
   // half as many tiles quantise worse onto the persistent grid and a ragged N wastes more.
   bool n512 = pair && var == kVarDirect && !a.d_f32 && (d.epilogue == UFP8_EPI_STORE || swiglu) &&
-              variant == UFP8_GEMM_CTA_PAIR_N512;
-  if (pair && var == kVarDirect && !a.d_f32 && d.epilogue == UFP8_EPI_STORE && variant == UFP8_GEMM_AUTO) {
+              variant == UFP8_GEMM_CTA_PAIR_N512 && !bf16;
+  if (pair && var == kVarDirect && !a.d_f32 && d.epilogue == UFP8_EPI_STORE && variant == UFP8_GEMM_AUTO && !bf16) {
     const int64_t nc = dev.sm_count / 2;
     const int64_t t256 = static_cast<int64_t>(a.tiles_m) * ((d.N + 255) / 256) * d.batch;
     const int64_t t512 = static_cast<int64_t>(a.tiles_m) * ((d.N + 511) / 512) * d.batch;
     n512 = 1.84 * static_cast<double>((t512 + nc - 1) / nc) <= static_cast<double>((t256 + nc - 1) / nc);
   }
-  const bool wide = !n512 && pair &&
+  const bool wide = bf16 || (!n512 && pair &&
                     ((var == kVarDirect && (variant == UFP8_GEMM_AUTO || variant == UFP8_GEMM_CTA_PAIR_WIDE)) ||
-                     (var != kVarDirect && variant == UFP8_GEMM_CTA_PAIR_WIDE));
+                     (var != kVarDirect && variant == UFP8_GEMM_CTA_PAIR_WIDE)));
   if (n512) a.tiles_n = static_cast<int>((d.N + 2 * bn - 1) / (2 * bn));
   const int kch = wide ? 2 : 1;
-  a.ksteps = static_cast<int>((d.K + kch * kBK - 1) / (kch * kBK));
+  const int kelems = bf16 ? kBK / 2 : kBK;  // K elements per 128-byte chunk
+  a.ksteps = static_cast<int>((d.K + kch * kelems - 1) / (kch * kelems));
   CUtensorMap tmUG, tmD;
   std::memset(&tmUG, 0, sizeof(tmUG));
   std::memset(&tmD, 0, sizeof(tmD));
@@ -1812,6 +1892,9 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   } else if (var == kVarUgStaged) {
     pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWideStaged, kVarUgStaged, 2> : gemm_fp8_pair_kernel<kPStagesStaged, kVarUgStaged>;
     pair_smem = wide ? kPSmemBytesWideUg : kPSmemBytesUg;
+  } else if (bf16) {
+    pair_kernel = gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2, true>;
+    pair_smem = kPSmemBytesWide;
   } else {
     pair_kernel = wide ? gemm_fp8_pair_kernel<kPStagesWide, kVarDirect, 2> : gemm_fp8_pair_kernel<kPStages, kVarDirect>;
     pair_smem = wide ? kPSmemBytesWide : kPSmemBytes;
@@ -1819,12 +1902,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if (n512) pair_smem = kWSmemBytes;
   const void* pair_fn = n512 ? reinterpret_cast<const void*>(gemm_fp8_n512_kernel)
                              : reinterpret_cast<const void*>(pair_kernel);
-  const int occ_slot = n512 ? 6 : var + (wide ? 3 : 0);
+  const int occ_slot = bf16 ? 7 : (n512 ? 6 : var + (wide ? 3 : 0));
   const long long num_tiles = static_cast<long long>(a.tiles_m) * a.tiles_n * a.batch;
   if (num_tiles >= (1ll << 31)) return set_error(UFP8_ERR_INVALID, "too many tiles");
   int ctas = ctas_override > 0 ? ctas_override : dev.sm_count;
   if (pair) {
-    static thread_local int occ_device[7] = {-1, -1, -1, -1, -1, -1, -1}, occ_clusters[7] = {0, 0, 0, 0, 0, 0, 0};
+    static thread_local int occ_device[8] = {-1, -1, -1, -1, -1, -1, -1, -1}, occ_clusters[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (occ_device[occ_slot] != dev.device) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * (dev.sm_count / 2), 1, 1);

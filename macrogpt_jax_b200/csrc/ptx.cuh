@@ -245,6 +245,17 @@ __device__ __forceinline__ void umma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_des
       : "memory");
 }
 
+// The same with 16-bit operands (kind::f16: bf16 or f16 A and B of one type, fp32 accumulate).
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives once on the mbarrier at `bar`'s offset in every CTA of `cta_mask` when all
 // tcgen05 operations issued so far by this thread complete.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {

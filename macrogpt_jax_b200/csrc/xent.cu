@@ -231,17 +231,16 @@ __device__ __forceinline__ float xent_dl(float c, bool is_label, float nl2, floa
   return v;
 }
 
-// Eight products -> eight fp8 bytes.  The hardware conversion rounds like the cast except where
-// a product is special (NaN, or past the format's overflow threshold; fp8cast.cuh): one check on
-// the largest magnitude bit pattern of the eight (a NaN pattern is above every other) decides
-// whether any needs the re-encoding of cvt2.
+// Eight scaled gradient values -> eight fp8 bytes.  The hardware conversion rounds like the
+// cast except for NaN, infinities and magnitudes past the overflow threshold (fp8cast.cuh), and
+// no finite value here gets there: every |dl| of a row is at most |g| * qrow (the label column
+// holds the row's largest |softmax - onehot|), so |dl * s| <= FMAX up to rounding, far below the
+// threshold (61440 for e5m2, 464 for e4m3).  So one finiteness test of the eight values' sum (a
+// NaN or an infinity makes it non-finite) decides whether the re-encoding of cvt2 is needed.
 __device__ __forceinline__ uint2 cvt8(const float (&p)[8], int fmt) {
-  uint32_t mb = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(p[i]) & 0x7FFFFFFFu);
-  const bool plain = fmt == UFP8_E4M3 ? mb <= 0x43E80000u /* 464 */ : mb < 0x47700000u /* 61440 */;
+  const float sum = ((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7]));
   uint32_t w[4];
-  if (plain) {
+  if (isfinite(sum)) {
     const __nv_fp8_interpretation_t kind = fmt == UFP8_E4M3 ? __NV_E4M3 : __NV_E5M2;
 #pragma unroll
     for (int i = 0; i < 4; ++i)
@@ -254,14 +253,17 @@ __device__ __forceinline__ uint2 cvt8(const float (&p)[8], int fmt) {
   return make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
 }
 
-// Work unit = kXCols columns of one row; a resident grid walks the units (row-major order), the
-// 16-byte loads of its next unit issued before the current one is computed.  Vector units of 8
-// columns (a 16-byte load, an 8-byte fp8 or 16-byte bf16 store) where the unit lies inside the
-// row, element by element otherwise.
+// Work unit = kXCols columns of one row; a resident grid walks the units in row-major order,
+// advancing (row, chunk) by gridDim.x units without a division, and issues the 16-byte loads of
+// its next unit before computing the current one.  Vector units of 8 columns (a 16-byte load, an
+// 8-byte fp8 or 16-byte bf16 store) where the unit lies inside the row, element by element
+// otherwise.  Per element: p = softmax_p(c), minus 1 in the one unit of the row that holds the
+// label, times the row factor, times the soft cap's derivative.
 template <bool kFp8>
-__device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t u, float sc, const uint4 (&w)[kXUnits]) {
-  const int64_t row = u / a.ctas_per_row;
-  const int64_t c0 = (u - row * a.ctas_per_row) * kXCols;
+__device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t row, int ch, float sc,
+                                               const uint4 (&w)[kXUnits]) {
+  const int c0 = ch * kXCols;
+  const int V = static_cast<int>(a.V);
   const uint16_t* lr = a.logits + row * a.ldl;
   uint8_t* q8 = static_cast<uint8_t*>(a.out) + row * a.ldo;     // kFp8
   uint16_t* q16 = static_cast<uint16_t*>(a.out) + row * a.ldo;  // !kFp8
@@ -270,8 +272,8 @@ __device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t u, flo
   const float mk = a.mask ? static_cast<float>(a.mask[row]) : 1.0f;
   const float ge = __fmul_rn(g, mk);
   const float wr = kFp8 ? __fmul_rn(ge, sc) : ge;
-  const int64_t lab = label_col(a.labels[row], a.V);
-  auto put1 = [&](int64_t cc, float v) {
+  const int lab = static_cast<int>(label_col(a.labels[row], a.V));  // -1: no column
+  auto put1 = [&](int cc, float v) {
     if (kFp8)
       q8[cc] = static_cast<uint8_t>(cvt2(v, 0.0f, a.fmt) & 0xFFu);
     else
@@ -279,23 +281,34 @@ __device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t u, flo
   };
   if (!a.vec) {
     for (int i = 0; i < kXCols / kXThreads; ++i) {
-      const int64_t cc = c0 + static_cast<int64_t>(i) * kXThreads + threadIdx.x;
-      if (cc < a.V) put1(cc, xent_dl(bf(lr[cc]), cc == lab, nl2, wr, a.cap_on, a.inv_cap));
+      const int cc = c0 + i * kXThreads + static_cast<int>(threadIdx.x);
+      if (cc < V) put1(cc, xent_dl(bf(lr[cc]), cc == lab, nl2, wr, a.cap_on, a.inv_cap));
     }
     return;
   }
 #pragma unroll
   for (int k = 0; k < kXUnits; ++k) {
-    const int64_t col = c0 + static_cast<int64_t>(k * kXThreads + threadIdx.x) * 8;
-    if (col + 8 <= a.V) {
-      const int64_t rel = lab - col;
-      const int lj = (rel >= 0 && rel < 8) ? static_cast<int>(rel) : -1;  // label's slot in the unit
-      const uint32_t ws[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+    const int col = c0 + (k * kXThreads + static_cast<int>(threadIdx.x)) * 8;
+    if (col + 8 <= V) {
+      const float c[8] = {wlo(w[k].x), whi(w[k].x), wlo(w[k].y), whi(w[k].y),
+                          wlo(w[k].z), whi(w[k].z), wlo(w[k].w), whi(w[k].w)};
       float v[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[2 * j] = xent_dl(wlo(ws[j]), 2 * j == lj, nl2, wr, a.cap_on, a.inv_cap);
-        v[2 * j + 1] = xent_dl(whi(ws[j]), 2 * j + 1 == lj, nl2, wr, a.cap_on, a.inv_cap);
+      for (int j = 0; j < 8; ++j) v[j] = softmax_p(c[j], nl2);
+      const unsigned rel = static_cast<unsigned>(lab - col);
+      if (rel < 8u) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (static_cast<unsigned>(j) == rel) v[j] = __fsub_rn(v[j], 1.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], wr);
+      if (a.cap_on) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float t = __fmul_rn(c[j], a.inv_cap);
+          v[j] = __fmul_rn(v[j], __fsub_rn(1.0f, __fmul_rn(t, t)));
+        }
       }
       if (kFp8) {
         *reinterpret_cast<uint2*>(q8 + col) = cvt8(v, a.fmt);
@@ -310,36 +323,46 @@ __device__ __forceinline__ void xent_grad_unit(const XentArgs& a, int64_t u, flo
         *reinterpret_cast<uint4*>(q16 + col) = o;
       }
     } else {
-      for (int64_t cc = col; cc < a.V && cc < col + 8; ++cc)
+      for (int cc = col; cc < V && cc < col + 8; ++cc)
         put1(cc, xent_dl(bf(lr[cc]), cc == lab, nl2, wr, a.cap_on, a.inv_cap));
     }
   }
 }
 
-template <int kU>
-__device__ __forceinline__ void xent_grad_load(const XentArgs& a, int64_t u, uint4 (&w)[kU]) {
-  const int64_t row = u / a.ctas_per_row;
-  const int64_t c0 = (u - row * a.ctas_per_row) * kXCols;
+__device__ __forceinline__ void xent_grad_load(const XentArgs& a, int64_t row, int ch, uint4 (&w)[kXUnits]) {
+  const int V = static_cast<int>(a.V);
   const uint16_t* lr = a.logits + row * a.ldl;
 #pragma unroll
-  for (int k = 0; k < kU; ++k) {
-    const int64_t col = c0 + static_cast<int64_t>(k * kXThreads + threadIdx.x) * 8;
-    w[k] = col + 8 <= a.V ? ld_stream16(lr + col) : make_uint4(0, 0, 0, 0);
+  for (int k = 0; k < kXUnits; ++k) {
+    const int col = ch * kXCols + (k * kXThreads + static_cast<int>(threadIdx.x)) * 8;
+    w[k] = col + 8 <= V ? ld_stream16(lr + col) : make_uint4(0, 0, 0, 0);
   }
 }
 
 template <bool kFp8>
 __global__ void __launch_bounds__(kXThreads) xent_grad_kernel(const XentArgs a) {
   const float sc = kFp8 ? scale_from_amax(*a.amax, a.fmt) : 1.0f;
-  const int64_t units = a.rows * a.ctas_per_row;
-  int64_t u = blockIdx.x;
-  if (u >= units) return;
+  const int cpr = static_cast<int>(a.ctas_per_row);
+  if (static_cast<int64_t>(blockIdx.x) >= a.rows * cpr) return;
+  int64_t row = blockIdx.x / cpr;
+  int ch = static_cast<int>(blockIdx.x - row * cpr);
+  const int64_t step_r = gridDim.x / cpr;
+  const int step_c = static_cast<int>(gridDim.x % cpr);
   uint4 w[kXUnits], wn[kXUnits];
-  if (a.vec) xent_grad_load(a, u, w);
-  for (; u < units; u += gridDim.x) {
-    const int64_t un = u + gridDim.x;
-    if (a.vec && un < units) xent_grad_load(a, un, wn);
-    xent_grad_unit<kFp8>(a, u, sc, w);
+  if (a.vec) xent_grad_load(a, row, ch, w);
+  while (true) {
+    int64_t rn = row + step_r;
+    int chn = ch + step_c;
+    if (chn >= cpr) {
+      chn -= cpr;
+      ++rn;
+    }
+    const bool more = rn < a.rows;
+    if (a.vec && more) xent_grad_load(a, rn, chn, wn);
+    xent_grad_unit<kFp8>(a, row, ch, sc, w);
+    if (!more) break;
+    row = rn;
+    ch = chn;
 #pragma unroll
     for (int k = 0; k < kXUnits; ++k) w[k] = wn[k];
   }
@@ -445,6 +468,7 @@ extern "C" int ufp8_xent_backward(const void* logits_bf16, int64_t rows, int64_t
     return set_error(UFP8_ERR_INVALID, "ufp8_xent_backward: null lse, qrow or dlogits");
   if (fp8 && (!amax || !inv_scale)) return set_error(UFP8_ERR_INVALID, "ufp8_xent_backward: null amax or inv_scale");
   if (!fp8 && !al(dlogits, 2)) return set_error(UFP8_ERR_ALIGN, "ufp8_xent_backward: dlogits not 2-byte aligned");
+  if (V >= (int64_t(1) << 31) - kXCols) return set_error(UFP8_ERR_INVALID, "ufp8_xent_backward: V exceeds 2^31");
   const int64_t cpr = (V + kXCols - 1) / kXCols;
   DeviceInfo* dev;
   if (int rc = device_info(&dev)) return rc;

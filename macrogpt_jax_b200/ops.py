@@ -118,12 +118,19 @@ def operand(t: Fp8Tensor, major: int, ld: int, batch_stride: int = 0, batch_coun
     return C.Operand(t.q.data_ptr(), t.fmt, major, ld, batch_stride, batch_count, 0, inv.data_ptr())
 
 
+def bf16_operand(t: torch.Tensor, major: int, ld: int, batch_stride: int = 0, batch_count: int = 1) -> C.Operand:
+    """A bf16 GEMM operand (tcgen05 kind::f16), no scale factor."""
+    if t.dtype != torch.bfloat16 or not t.is_cuda:
+        raise ValueError("bf16_operand: expected a CUDA bfloat16 tensor")
+    return C.Operand(t.data_ptr(), C.BF16, major, ld, batch_stride, batch_count, 0, None)
+
+
 def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ldd: int,
          d_batch_stride: int = 0, batch: int = 1, k_batches: int = 1, epilogue: int = C.EPI_STORE,
          h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
          ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None, rs_slots: int | None = None,
          rs_rank: int = 0, rs_rows_per_rank: int = 0, ag: tuple | None = None,
-         xent: tuple | None = None) -> None:
+         xent: tuple | None = None, axpby: tuple | None = None) -> None:
     desc = C.GemmDesc()
     desc.M, desc.N, desc.K = M, N, K
     desc.batch, desc.k_batches = batch, k_batches
@@ -143,6 +150,9 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
         desc.ag_flags, desc.ag_epoch, desc.ag_rank, desc.ag_rows_per_rank = ag
     if xent is not None:  # (stats tensor, pitch in pairs, soft cap): the XENT epilogue's partials
         desc.xent_stats, desc.xent_ld_stats, desc.xent_cap = xent[0].data_ptr(), xent[1], xent[2]
+    if axpby is not None:  # (C tensor, ldc, c batch stride, alpha, beta): D = alpha acc + beta C
+        desc.c, desc.ldc, desc.c_batch_stride = axpby[0].data_ptr(), axpby[1], axpby[2]
+        desc.alpha, desc.beta = axpby[3], axpby[4]
     n_eff = 2 * N if epilogue == C.EPI_SWIGLU else N
     flops = 2.0 * M * n_eff * K * batch * k_batches
     _launch("gemm", flops, lambda: C.gemm(desc, _stream()))
@@ -492,3 +502,25 @@ def head_xent_backward(dloss: torch.Tensor, saved, labels: torch.Tensor, mask: t
         dw = torch.empty((d, V), dtype=torch.bfloat16, device=qx.q.device)
         gemm(operand(qx, C.MN_MAJOR, d), operand(qd, C.MN_MAJOR, Vp), d, V, T, dw, V)
     return dxn, dw
+
+
+# ----------------------------------------------------------------------------- Newton-Schulz
+def newton_schulz(g: torch.Tensor, coeffs, eps: float = 1e-8, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """ufp8_newton_schulz over g [batch, m, n] (f32 or bf16, CUDA): the orthogonalisation of Muon
+    (ueaj/opt/multiscale.py:110-141) with one (a, b, c) triple per step.  Returns [batch, m, n] in
+    out_dtype (default: g's dtype; f32 or bf16)."""
+    if not g.is_cuda or g.dim() != 3 or g.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("newton_schulz: expected a CUDA f32 or bf16 tensor [batch, m, n]")
+    g = g.contiguous()
+    batch, m, n = g.shape
+    out_dtype = g.dtype if out_dtype is None else out_dtype
+    out = torch.empty((batch, m, n), dtype=out_dtype, device=g.device)
+    nbytes = C.newton_schulz_workspace(batch, m, n)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=g.device)
+    dt = {torch.float32: C.OUT_F32, torch.bfloat16: C.OUT_BF16}
+    s, l = min(m, n), max(m, n)
+    flops = float(batch) * len(coeffs) * (4.0 * s * s * l + 2.0 * s ** 3)
+    _launch("newton_schulz", flops, lambda: C.newton_schulz(
+        g.data_ptr(), dt[g.dtype], batch, m, n, coeffs, eps, out.data_ptr(), dt[out_dtype], ws.data_ptr(), nbytes,
+        _stream()))
+    return out

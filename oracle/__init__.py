@@ -17,7 +17,9 @@ What it restates (reference file:line, relative to the macrogpt-jax repository):
   * RMSNorm.__call__  ueaj/model/rmsnorm.py:68-84 (norm.py), with the summation order and
     the rsqrt the CUDA kernel uses;
   * the next-token loss on the lm_head logits (xent.py): ntp_args / chunked_softmax_cross_entropy
-    ueaj/opt/next_token_loss.py:13-174 and LlamaModel.get_logits ueaj/model/model.py:140-165.
+    ueaj/opt/next_token_loss.py:13-174 and LlamaModel.get_logits ueaj/model/model.py:140-165;
+  * Muon's Newton-Schulz orthogonalisation (muon.py): ueaj/opt/multiscale.py:110-200 and the
+    optax 0.2.6 iteration it maps over the slices of a weight.
 
 Parity pinning:
   * fp8 cast bytes: pinned.  fp8.py's own round-to-nearest-even cast is checked against
@@ -26,4 +28,4 @@ Parity pinning:
     here (jax, flax, optax absent, no network) and the reference ships no golden vectors;
     these functions are restatements, checked against an independent einsum (torch) only.
 """
-from . import fp8, norm, path, xent  # noqa: F401
+from . import fp8, muon, norm, path, xent  # noqa: F401

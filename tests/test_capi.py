@@ -38,6 +38,7 @@ def test_header_constants_match_binding():
             int(consts["UFP8_EPI_RS_PUSH"]), int(consts["UFP8_EPI_XENT"])) == \
         (C.EPI_STORE, C.EPI_SWIGLU, C.EPI_DSWIGLU, C.EPI_RS_PUSH, C.EPI_XENT)
     assert int(consts["UFP8_BF16"]) == C.BF16
+    assert int(consts["UFP8_EPI_AXPBY"]) == C.EPI_AXPBY
     assert tuple(int(consts[k]) for k in ("UFP8_GEMM_AUTO", "UFP8_GEMM_SINGLE_CTA", "UFP8_GEMM_CTA_PAIR",
                                           "UFP8_GEMM_CTA_PAIR_DIRECT")) == \
         (C.GEMM_AUTO, C.GEMM_SINGLE_CTA, C.GEMM_CTA_PAIR, C.GEMM_CTA_PAIR_DIRECT)
@@ -99,6 +100,15 @@ def test_struct_layout_matches_header(tmp_path):
     (lambda L: L.ufp8_xent_backward(ctypes.c_void_p(16), 1, 8, 8, ctypes.c_void_p(16), None, None, None, None, 0.0,
                                     C.E5M2, ctypes.c_void_p(16), 8, None, None, None), C.ERR_INVALID,
      "null lse, qrow or dlogits"),
+    (lambda L: L.ufp8_newton_schulz(None, 7, 1, 8, 8, 5, None, 1e-8, None, 0, None, 0, None), C.ERR_INVALID,
+     "g_dtype"),
+    (lambda L: L.ufp8_newton_schulz(None, C.OUT_F32, 1, 8, 8, 0, None, 1e-8, None, C.OUT_F32, None, 0, None),
+     C.ERR_INVALID, "steps must be 1..64"),
+    (lambda L: L.ufp8_newton_schulz(None, C.OUT_F32, 1, 12, 8, 1, (ctypes.c_float * 3)(1, 2, 3), 1e-8, None,
+                                    C.OUT_F32, None, 0, None), C.ERR_UNSUPPORTED, "multiples of 8"),
+    (lambda L: L.ufp8_newton_schulz(None, C.OUT_F32, 1, 16, 8, 1, (ctypes.c_float * 3)(1, 2, 3), 1e-8, None,
+                                    C.OUT_F32, None, 0, None), C.ERR_INVALID, "workspace of"),
+    (lambda L: L.ufp8_newton_schulz_workspace(-1, 8, 8, None), C.ERR_INVALID, "null pointer"),
     (lambda L: L.ufp8_amax(None, -1, None, None), C.ERR_INVALID, "n < 0"),
     (lambda L: L.ufp8_quantize(None, 4, 7, None, None, None, None), C.ERR_INVALID, "fmt 7"),
     (lambda L: L.ufp8_amax_quant(None, 4, 3, None, None, None, None), C.ERR_INVALID, "fmt 3"),
