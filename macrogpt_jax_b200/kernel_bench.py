@@ -239,6 +239,21 @@ def xent_bench(args, dev):
     print(json.dumps({"tokens": T, "vocab": V, **res}), flush=True)
 
 
+def ns_bench(args, dev):
+    """Newton-Schulz (ufp8_newton_schulz) on [batch, d, hidden] f32 slices, 5 'muon' steps;
+    algorithmic TF/s = 5 (4 s^2 l + 2 s^3) per slice / time."""
+    from .muon import ns_coefficients
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    g = torch.randn((args.batch, args.d, args.hidden), generator=gen, device=dev)
+    co = ns_coefficients(5, "muon")
+    s_, l_ = min(args.d, args.hidden), max(args.d, args.hidden)
+    fl = args.batch * 5 * (4.0 * s_ * s_ * l_ + 2.0 * s_ ** 3)
+    us = _time_us(lambda: ops.newton_schulz(g, co), args.reps, args.warmup)
+    print(json.dumps({"batch": args.batch, "m": args.d, "n": args.hidden, "us": us, "tflops": fl / us / 1e6}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
@@ -255,6 +270,8 @@ def main():
     ap.add_argument("--norm", action="store_true", help="time the RMSNorm kernels on [tokens, d] instead")
     ap.add_argument("--xent", action="store_true", help="time the cross-entropy kernels on [tokens, vocab] instead")
     ap.add_argument("--vocab", type=int, default=128256)
+    ap.add_argument("--ns", action="store_true", help="time Newton-Schulz on [batch, d, hidden] instead")
+    ap.add_argument("--batch", type=int, default=2)
     ap.add_argument("--rs-push", action="store_true",
                     help="time the TP-2/4/8 F2 and B4 GEMMs storing locally vs pushing rows to a peer GPU")
     args = ap.parse_args()
@@ -269,6 +286,8 @@ def main():
         return norm_bench(args, dev)
     if args.xent:
         return xent_bench(args, dev)
+    if args.ns:
+        return ns_bench(args, dev)
     if args.rs_push:
         return rs_push_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)
