@@ -267,6 +267,46 @@ int ufp8_newton_schulz(const void* g, int g_dtype, int64_t batch, int64_t m, int
                        const float* coeffs, float eps, void* out, int out_dtype, void* workspace,
                        int64_t workspace_bytes, ufp8_stream_t stream);
 
+/* ---- RoPE and softmax attention ----------------------------------------------------------
+ * RoPE (ueaj/model/rope.py:10-104): ufp8_rope_table writes, for `count` positions (f32) and
+ * `half` = rope_d / 2 frequencies inv_freq (f32, the caller's 1 / theta^(j / half)), the bf16
+ * tables sin / cos [count][half] of angle = position * inv_freq.  ufp8_rope rotates x (bf16
+ * [tokens][heads][d], contiguous) in place or into `out`: with x1 = x[..., :d/2], x2 = x[..., d/2:],
+ * (x1 c - x2 s, x2 c + x1 s), each product and sum rounded to bf16 as the reference's bf16
+ * expression is; token t uses table row t % period; inverse != 0 applies the transpose (the
+ * backward). */
+int ufp8_rope_table(const float* positions, int64_t count, int64_t half, const float* inv_freq, void* sin_bf16,
+                    void* cos_bf16, ufp8_stream_t stream);
+int ufp8_rope(const void* x_bf16, int64_t tokens, int64_t heads, int64_t d, const void* sin_bf16,
+              const void* cos_bf16, int64_t period, int inverse, void* out_bf16, ufp8_stream_t stream);
+
+/* Softmax attention: the flash_attention call of SoftmaxAttention.__call__ (ueaj/model/soft_attn.py:
+ * 186-196; kvax 0.1.2).  q [batch][seq][kv_heads * group][head_dim], k and v [batch][seq][kv_heads]
+ * [head_dim], out like q, all bf16; query head (h, i) attends with key/value head h.  Query p sees key
+ * p' of the same batch element iff positions[p'] <= positions[p] and both segment ids are equal and
+ * non-negative (a negative id is padding); a row that sees nothing outputs 0.  P = softmax(scale *
+ * Q K^T) over the visible keys.  Products are bf16 tcgen05 GEMMs with fp32 accumulation; the scores
+ * (f32) of one batch element live in `workspace`, the probabilities (bf16) of all of them in `saved`
+ * for the backward (sizes from ufp8_attention_workspace, 256-byte aligned).  Segment ids and
+ * positions: int32 [batch][seq], NULL = all 0 / 0..seq-1.  seq and head_dim multiples of 8. */
+typedef struct ufp8_attn_desc {
+  int64_t batch, seq, kv_heads, group, head_dim;
+  const int32_t* q_segment_ids;
+  const int32_t* kv_segment_ids;
+  const int32_t* q_positions;
+  const int32_t* kv_positions;
+  float scale;
+  int32_t reserved;
+} ufp8_attn_desc;
+int ufp8_attention_workspace(const ufp8_attn_desc* desc, int64_t* fwd_bytes, int64_t* saved_bytes,
+                             int64_t* bwd_bytes);
+int ufp8_attention_forward(const ufp8_attn_desc* desc, const void* q, const void* k, const void* v, void* out,
+                           void* saved, void* workspace, ufp8_stream_t stream);
+/* dq, dk, dv (bf16, shaped like q, k, v) of a loss with gradient dout at out. */
+int ufp8_attention_backward(const ufp8_attn_desc* desc, const void* q, const void* k, const void* v, const void* out,
+                            const void* dout, const void* saved, void* dq, void* dk, void* dv, void* workspace,
+                            ufp8_stream_t stream);
+
 /* ---- tensor-parallel reduce-scatter over NVLink peer memory ------------------------------
  * Replaces the reduce-scatter XLA/GSPMD would insert after the row-split down projection of
  * a tensor-parallel GMLP (implied by ueaj/model/mlp.py:96 'tensor' on the hidden axis and

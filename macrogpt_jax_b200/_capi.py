@@ -55,6 +55,11 @@ EXPORTED_SYMBOLS = (
     "ufp8_xent_backward",
     "ufp8_newton_schulz_workspace",
     "ufp8_newton_schulz",
+    "ufp8_rope_table",
+    "ufp8_rope",
+    "ufp8_attention_workspace",
+    "ufp8_attention_forward",
+    "ufp8_attention_backward",
 )
 
 
@@ -108,6 +113,22 @@ class GemmDesc(ctypes.Structure):
         ("c_batch_stride", ctypes.c_int64),
         ("alpha", ctypes.c_float),
         ("beta", ctypes.c_float),
+    ]
+
+
+class AttnDesc(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int64),
+        ("seq", ctypes.c_int64),
+        ("kv_heads", ctypes.c_int64),
+        ("group", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("q_segment_ids", ctypes.c_void_p),
+        ("kv_segment_ids", ctypes.c_void_p),
+        ("q_positions", ctypes.c_void_p),
+        ("kv_positions", ctypes.c_void_p),
+        ("scale", ctypes.c_float),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -165,13 +186,20 @@ def load() -> ctypes.CDLL:
     lib.ufp8_xent_backward.argtypes = [vp, i64, i64, i64, vp, vp, vp, vp, vp, f32, i32, vp, i64, vp, vp, vp]
     lib.ufp8_newton_schulz_workspace.argtypes = [i64, i64, i64, ctypes.POINTER(i64)]
     lib.ufp8_newton_schulz.argtypes = [vp, i32, i64, i64, i64, i32, vp, f32, vp, i32, vp, i64, vp]
+    lib.ufp8_rope_table.argtypes = [vp, i64, i64, vp, vp, vp, vp]
+    lib.ufp8_rope.argtypes = [vp, i64, i64, i64, vp, vp, i64, i32, vp, vp]
+    ap = ctypes.POINTER(AttnDesc)
+    lib.ufp8_attention_workspace.argtypes = [ap, ctypes.POINTER(i64), ctypes.POINTER(i64), ctypes.POINTER(i64)]
+    lib.ufp8_attention_forward.argtypes = [ap, vp, vp, vp, vp, vp, vp, vp]
+    lib.ufp8_attention_backward.argtypes = [ap, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]
     for name in ("ufp8_amax", "ufp8_quantize", "ufp8_amax_quant", "ufp8_cast", "ufp8_gemm", "ufp8_device_status",
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
                  "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
                  "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
                  "ufp8_rmsnorm_backward", "ufp8_xent_forward", "ufp8_xent_combine", "ufp8_xent_backward",
-                 "ufp8_newton_schulz_workspace", "ufp8_newton_schulz"):
+                 "ufp8_newton_schulz_workspace", "ufp8_newton_schulz", "ufp8_rope_table", "ufp8_rope",
+                 "ufp8_attention_workspace", "ufp8_attention_forward", "ufp8_attention_backward"):
         getattr(lib, name).restype = i32
     _lib = lib
     return lib
@@ -270,6 +298,33 @@ def newton_schulz(g_ptr, g_dtype, batch, m, n, coeffs, eps, out_ptr, out_dtype, 
     check(load().ufp8_newton_schulz(g_ptr, g_dtype, batch, m, n, len(flat) // 3, arr, eps, out_ptr, out_dtype,
                                     ws_ptr, ws_bytes, stream))
     _count((2 + 3 * (len(flat) // 3)) if batch > 0 else 0)
+
+
+def rope_table(pos_ptr, count, half, inv_freq_ptr, sin_ptr, cos_ptr, stream) -> None:
+    check(load().ufp8_rope_table(pos_ptr, count, half, inv_freq_ptr, sin_ptr, cos_ptr, stream))
+    _count(1 if count > 0 else 0)
+
+
+def rope(x_ptr, tokens, heads, d, sin_ptr, cos_ptr, period, inverse, out_ptr, stream) -> None:
+    check(load().ufp8_rope(x_ptr, tokens, heads, d, sin_ptr, cos_ptr, period, 1 if inverse else 0, out_ptr, stream))
+    _count(1 if tokens > 0 else 0)
+
+
+def attention_workspace(desc: AttnDesc):
+    """(forward workspace, saved, backward workspace) bytes."""
+    f, s, b = ctypes.c_int64(0), ctypes.c_int64(0), ctypes.c_int64(0)
+    check(load().ufp8_attention_workspace(ctypes.byref(desc), ctypes.byref(f), ctypes.byref(s), ctypes.byref(b)))
+    return f.value, s.value, b.value
+
+
+def attention_forward(desc: AttnDesc, q, k, v, out, saved, ws, stream) -> None:
+    check(load().ufp8_attention_forward(ctypes.byref(desc), q, k, v, out, saved, ws, stream))
+    _count(desc.batch * (2 * desc.kv_heads + 1))
+
+
+def attention_backward(desc: AttnDesc, q, k, v, out, dout, saved, dq, dk, dv, ws, stream) -> None:
+    check(load().ufp8_attention_backward(ctypes.byref(desc), q, k, v, out, dout, saved, dq, dk, dv, ws, stream))
+    _count(desc.batch * (4 * desc.kv_heads + 1))
 
 
 def gemm(desc: GemmDesc, stream: int) -> None:

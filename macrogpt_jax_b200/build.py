@@ -15,7 +15,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "lib"
 LIB_PATH = LIB_DIR / "libufp8.so"
 INCLUDE = PKG.parent / "include"
-SOURCES = ["quant.cu", "norm.cu", "xent.cu", "ns.cu", "gemm.cu", "tp.cu", "noalloc.cu", "capi.cu"]
+SOURCES = ["quant.cu", "norm.cu", "xent.cu", "ns.cu", "attn.cu", "gemm.cu", "tp.cu", "noalloc.cu", "capi.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -1,0 +1,433 @@
+// Softmax attention of the reference's SoftmaxAttention (ueaj/model/soft_attn.py:142-202) and its
+// RoPE (ueaj/model/rope.py:10-104).
+//
+// The reference calls kvax 0.1.2's flash_attention (requirements.txt:35, not installable here):
+// out = softmax(scale * Q K^T + mask) V per query head, the mask allowing query position p to see
+// key position p' of the same sequence iff p' <= p and both carry the same segment id, padding
+// (a negative segment id) seeing and seen by nothing; a row that sees nothing gives 0.  Grouped
+// query attention: query head (h, i) uses key/value head h.
+//
+// B200 layout of the computation: the products are the bf16 CTA-pair GEMM (tcgen05 kind::f16, fp32
+// accumulation) launched per (batch element, kv head) over the group's query heads; the key/value
+// head is a broadcast operand (batch_count 1), and dK, dV concatenate the contraction over the
+// group (k_batches).  The scores S (f32) and probabilities P (bf16) of one batch element are
+// materialised in HBM (HI x n x n per batch element; P is kept for the backward), and the masked
+// softmax and its backward are row kernels between the GEMMs:
+//   forward:  S_g = Q_g K_h^T            softmax rows -> P_g (bf16), lse     O_g = P_g V_h
+//   backward: dP_g = dO_g V_h^T          dS_g = scale * P_g (dP_g - rowsum(dO_g O_g))
+//             dQ_g = dS_g K_h            dK_h = sum_i dS_g^T Q_g             dV_h = sum_i P_g^T dO_g
+// No transposed copy is made (MN-major operands).  RoPE: one kernel builds the bf16 sin/cos table
+// from positions (f32 angle = position * inv_freq, sinf/cosf, then bf16, as the reference's
+// compute_rope_embedding), one applies the rotation (bf16 rounding after each product and sum, as
+// the reference's bf16 expression does) or its transpose for the backward.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "internal.h"
+
+namespace ufp8 {
+namespace {
+
+constexpr int kAThreads = 256;
+
+__device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__global__ void __launch_bounds__(kAThreads) rope_table_kernel(const float* __restrict__ pos, int64_t count, int half,
+                                                               const float* __restrict__ inv_freq,
+                                                               __nv_bfloat16* __restrict__ sin_t,
+                                                               __nv_bfloat16* __restrict__ cos_t) {
+  const int64_t n = count * half;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kAThreads) {
+    const int64_t p = i / half;
+    const int j = static_cast<int>(i - p * half);
+    const float a = __fmul_rn(pos[p], inv_freq[j]);
+    sin_t[i] = __float2bfloat16_rn(sinf(a));
+    cos_t[i] = __float2bfloat16_rn(cosf(a));
+  }
+}
+
+// x [tokens][heads][d] bf16; token t uses table row t % period.  Forward: (x1 c - x2 s, x2 c + x1 s);
+// inverse (the transpose, for the backward): (y1 c + y2 s, y2 c - y1 s).
+__global__ void __launch_bounds__(kAThreads) rope_apply_kernel(const __nv_bfloat16* __restrict__ x, int64_t tokens,
+                                                               int heads, int half, int64_t period,
+                                                               const __nv_bfloat16* __restrict__ sin_t,
+                                                               const __nv_bfloat16* __restrict__ cos_t, int inverse,
+                                                               __nv_bfloat16* __restrict__ out) {
+  const int64_t n = tokens * heads * half;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kAThreads) {
+    const int64_t row = i / half;  // (token, head)
+    const int j = static_cast<int>(i - row * half);
+    const int64_t t = row / heads;
+    const int64_t tr = (t % period) * half + j;
+    const float s = __bfloat162float(sin_t[tr]), c = __bfloat162float(cos_t[tr]);
+    const int64_t b = row * 2 * half;
+    const float x1 = __bfloat162float(x[b + j]), x2 = __bfloat162float(x[b + half + j]);
+    float o1, o2;
+    if (!inverse) {
+      o1 = __fsub_rn(bfr(__fmul_rn(x1, c)), bfr(__fmul_rn(x2, s)));
+      o2 = __fadd_rn(bfr(__fmul_rn(x2, c)), bfr(__fmul_rn(x1, s)));
+    } else {
+      o1 = __fadd_rn(bfr(__fmul_rn(x1, c)), bfr(__fmul_rn(x2, s)));
+      o2 = __fsub_rn(bfr(__fmul_rn(x2, c)), bfr(__fmul_rn(x1, s)));
+    }
+    out[b + j] = __float2bfloat16_rn(o1);
+    out[b + half + j] = __float2bfloat16_rn(o2);
+  }
+}
+
+struct SoftArgs {
+  const float* S;    // [rows][n] scores of one batch element (rows = HI * n, row = g * n + q)
+  int64_t rows, n;
+  const int32_t* qseg;  // [n] of this batch element (NULL: 0)
+  const int32_t* kseg;
+  const int32_t* qpos;  // NULL: arange
+  const int32_t* kpos;
+  float scale;
+  __nv_bfloat16* P;  // [rows][n]
+  float* lse;        // [rows]
+  // backward
+  const float* dP;
+  const __nv_bfloat16* O;   // [n][HI][d] of this batch element
+  const __nv_bfloat16* dO;
+  int64_t hi, d;
+  __nv_bfloat16* dS;
+};
+
+__device__ __forceinline__ bool visible(const SoftArgs& a, int64_t q, int64_t k, int32_t sq, int32_t pq) {
+  const int32_t sk = a.kseg ? a.kseg[k] : 0;
+  const int32_t pk = a.kpos ? a.kpos[k] : static_cast<int32_t>(k);
+  return sq >= 0 && sk == sq && pk <= pq;
+}
+
+__device__ __forceinline__ void block_max_sum(float& m, float& s, float* sm, float* ss) {
+  // merge (m, s) pairs over the CTA in a fixed order
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float m2 = __shfl_xor_sync(0xFFFFFFFFu, m, off), s2 = __shfl_xor_sync(0xFFFFFFFFu, s, off);
+    const float mn = fmaxf(m, m2);
+    if (mn != -INFINITY) {
+      s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+      m = mn;
+    }
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sm[w] = m;
+    ss[w] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = sm[0], S = ss[0];
+    for (int i = 1; i < kAThreads / 32; ++i) {
+      const float mn = fmaxf(M, sm[i]);
+      if (mn != -INFINITY) {
+        S = S * __expf(M - mn) + ss[i] * __expf(sm[i] - mn);
+        M = mn;
+      }
+    }
+    sm[0] = M;
+    ss[0] = S;
+  }
+  __syncthreads();
+  m = sm[0];
+  s = ss[0];
+}
+
+// One CTA per score row: masked online (max, sum exp) of scale * s, then P = exp(scale s - M) / S.
+__global__ void __launch_bounds__(kAThreads) attn_softmax_kernel(const SoftArgs a) {
+  const int64_t row = blockIdx.x;
+  const int64_t q = row % a.n;
+  const float* sr = a.S + row * a.n;
+  const int32_t sq = a.qseg ? a.qseg[q] : 0;
+  const int32_t pq = a.qpos ? a.qpos[q] : static_cast<int32_t>(q);
+  float m = -INFINITY, s = 0.0f;
+  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
+    if (!visible(a, q, k, sq, pq)) continue;
+    const float v = __fmul_rn(sr[k], a.scale);
+    if (v > m) {
+      s *= __expf(m - v);
+      m = v;
+    }
+    s += __expf(v - m);
+  }
+  __shared__ float sm[kAThreads / 32], ss[kAThreads / 32];
+  block_max_sum(m, s, sm, ss);
+  const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
+  __nv_bfloat16* pr = a.P + row * a.n;
+  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
+    const float p = visible(a, q, k, sq, pq) ? __fmul_rn(__expf(__fsub_rn(__fmul_rn(sr[k], a.scale), m)), inv) : 0.0f;
+    pr[k] = __float2bfloat16_rn(p);
+  }
+  if (threadIdx.x == 0) a.lse[row] = s > 0.0f ? __fadd_rn(m, logf(s)) : -INFINITY;
+}
+
+// One CTA per row: D = sum_d dO O (f32, fixed order), dS = bf16(scale * P (dP - D)).
+__global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftArgs a) {
+  const int64_t row = blockIdx.x;
+  const int64_t g = row / a.n, q = row - g * a.n;
+  const __nv_bfloat16* o = a.O + (q * a.hi + g) * a.d;
+  const __nv_bfloat16* go = a.dO + (q * a.hi + g) * a.d;
+  float part = 0.0f;
+  for (int64_t j = threadIdx.x; j < a.d; j += kAThreads)
+    part = __fadd_rn(part, __fmul_rn(__bfloat162float(o[j]), __bfloat162float(go[j])));
+  __shared__ float red[kAThreads];
+  red[threadIdx.x] = part;
+  __syncthreads();
+  for (int off = kAThreads / 2; off > 0; off >>= 1) {
+    if (threadIdx.x < off) red[threadIdx.x] = __fadd_rn(red[threadIdx.x], red[threadIdx.x + off]);
+    __syncthreads();
+  }
+  const float D = red[0];
+  const __nv_bfloat16* pr = a.P + row * a.n;
+  const float* dpr = a.dP + row * a.n;
+  __nv_bfloat16* dsr = a.dS + row * a.n;
+  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
+    const float p = __bfloat162float(pr[k]);
+    dsr[k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(p, __fsub_rn(dpr[k], D)), a.scale));
+  }
+}
+
+ufp8_operand bop(const void* p, int major, int64_t ld, int64_t bstride, int32_t count) {
+  ufp8_operand o{};
+  o.ptr = p;
+  o.fmt = UFP8_BF16;
+  o.major = major;
+  o.ld = ld;
+  o.batch_stride = bstride;
+  o.batch_count = count;
+  return o;
+}
+
+int gemm_bf16(const ufp8_operand& A, const ufp8_operand& B, int64_t M, int64_t N, int64_t K, int32_t batch,
+              int32_t kb, void* D, int d_f32, int64_t ldd, int64_t dbs, cudaStream_t s, const DeviceInfo& dev) {
+  ufp8_gemm_desc d{};
+  d.M = M;
+  d.N = N;
+  d.K = K;
+  d.batch = batch;
+  d.k_batches = kb;
+  d.a = A;
+  d.b = B;
+  d.d = D;
+  d.d_dtype = d_f32 ? UFP8_OUT_F32 : UFP8_OUT_BF16;
+  d.epilogue = UFP8_EPI_STORE;
+  d.ldd = ldd;
+  d.d_batch_stride = dbs;
+  return launch_gemm(d, s, dev, 0, UFP8_GEMM_AUTO, 0);
+}
+
+int attn_check(const ufp8_attn_desc* d, const char* who) {
+  if (!d) return set_error(UFP8_ERR_INVALID, "%s: null descriptor", who);
+  if (d->batch < 0 || d->seq < 1 || d->kv_heads < 1 || d->group < 1 || d->head_dim < 2 || d->head_dim % 8)
+    return set_error(UFP8_ERR_INVALID, "%s: bad shape (seq, heads >= 1; head_dim even and a multiple of 8)", who);
+  if (d->seq % 8) return set_error(UFP8_ERR_UNSUPPORTED, "%s: seq must be a multiple of 8 (16-byte rows of P)", who);
+  if (d->seq >= (int64_t(1) << 31)) return set_error(UFP8_ERR_INVALID, "%s: seq exceeds 2^31", who);
+  return UFP8_OK;
+}
+
+struct AttnLayout {
+  int64_t S, total_fwd;       // forward workspace: S f32 of one batch element
+  int64_t P, lse, saved;      // saved: P bf16 and lse of every batch element
+  int64_t dP, dS, total_bwd;  // backward workspace: dP f32 and dS bf16 of one batch element
+};
+
+int64_t al256(int64_t b) { return (b + 255) / 256 * 256; }
+
+AttnLayout attn_layout(const ufp8_attn_desc& d) {
+  const int64_t hi = d.kv_heads * d.group, nn = d.seq * d.seq;
+  AttnLayout L{};
+  L.S = 0;
+  L.total_fwd = al256(hi * nn * 4);
+  L.P = 0;
+  L.lse = al256(d.batch * hi * nn * 2);
+  L.saved = L.lse + al256(d.batch * hi * d.seq * 4);
+  L.dP = 0;
+  L.dS = al256(hi * nn * 4);
+  L.total_bwd = L.dS + al256(hi * nn * 2);
+  return L;
+}
+
+}  // namespace
+}  // namespace ufp8
+
+using namespace ufp8;
+
+extern "C" int ufp8_rope_table(const float* positions, int64_t count, int64_t half, const float* inv_freq,
+                               void* sin_bf16, void* cos_bf16, ufp8_stream_t stream) {
+  if (count < 0 || half < 1 || half > (1 << 20)) return set_error(UFP8_ERR_INVALID, "ufp8_rope_table: bad shape");
+  if (count > 0 && (!positions || !inv_freq || !sin_bf16 || !cos_bf16))
+    return set_error(UFP8_ERR_INVALID, "ufp8_rope_table: null pointer");
+  if (count == 0) return UFP8_OK;
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  const int64_t n = count * half;
+  const int64_t grid = std::min<int64_t>((n + kAThreads - 1) / kAThreads, int64_t(dev->sm_count) * 16);
+  rope_table_kernel<<<static_cast<unsigned>(grid), kAThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      positions, count, static_cast<int>(half), inv_freq, static_cast<__nv_bfloat16*>(sin_bf16),
+      static_cast<__nv_bfloat16*>(cos_bf16));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "rope table launch");
+}
+
+extern "C" int ufp8_rope(const void* x_bf16, int64_t tokens, int64_t heads, int64_t d, const void* sin_bf16,
+                         const void* cos_bf16, int64_t period, int inverse, void* out_bf16, ufp8_stream_t stream) {
+  if (tokens < 0 || heads < 1 || d < 2 || d % 2 || period < 1)
+    return set_error(UFP8_ERR_INVALID, "ufp8_rope: bad shape (d even, heads and period >= 1)");
+  if (tokens > 0 && (!x_bf16 || !sin_bf16 || !cos_bf16 || !out_bf16))
+    return set_error(UFP8_ERR_INVALID, "ufp8_rope: null pointer");
+  if (tokens == 0) return UFP8_OK;
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  const int64_t n = tokens * heads * (d / 2);
+  const int64_t grid = std::min<int64_t>((n + kAThreads - 1) / kAThreads, int64_t(dev->sm_count) * 16);
+  rope_apply_kernel<<<static_cast<unsigned>(grid), kAThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x_bf16), tokens, static_cast<int>(heads), static_cast<int>(d / 2), period,
+      static_cast<const __nv_bfloat16*>(sin_bf16), static_cast<const __nv_bfloat16*>(cos_bf16), inverse ? 1 : 0,
+      static_cast<__nv_bfloat16*>(out_bf16));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? UFP8_OK : cuda_error(e, "rope launch");
+}
+
+extern "C" int ufp8_attention_workspace(const ufp8_attn_desc* d, int64_t* fwd_bytes, int64_t* saved_bytes,
+                                        int64_t* bwd_bytes) {
+  if (int rc = attn_check(d, "ufp8_attention_workspace")) return rc;
+  if (!fwd_bytes || !saved_bytes || !bwd_bytes) return set_error(UFP8_ERR_INVALID, "ufp8_attention_workspace: null");
+  const AttnLayout L = attn_layout(*d);
+  *fwd_bytes = L.total_fwd;
+  *saved_bytes = L.saved;
+  *bwd_bytes = L.total_bwd;
+  return UFP8_OK;
+}
+
+extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, const void* k, const void* v, void* out,
+                                      void* saved, void* workspace, ufp8_stream_t stream) {
+  const char* who = "ufp8_attention_forward";
+  if (int rc = attn_check(d, who)) return rc;
+  if (d->batch > 0 && (!q || !k || !v || !out || !saved || !workspace))
+    return set_error(UFP8_ERR_INVALID, "%s: null pointer", who);
+  if ((reinterpret_cast<uintptr_t>(saved) | reinterpret_cast<uintptr_t>(workspace)) & 255u)
+    return set_error(UFP8_ERR_ALIGN, "%s: saved / workspace not 256-byte aligned", who);
+  if (d->batch == 0) return UFP8_OK;
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const AttnLayout L = attn_layout(*d);
+  const int64_t n = d->seq, H = d->kv_heads, I = d->group, Dh = d->head_dim, hi = H * I, nn = n * n;
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  float* S = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + L.S);
+  auto* P0 = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(saved) + L.P);
+  float* lse0 = reinterpret_cast<float*>(static_cast<uint8_t*>(saved) + L.lse);
+  for (int64_t b = 0; b < d->batch; ++b) {
+    const __nv_bfloat16* qB = qb + b * n * hi * Dh;
+    const __nv_bfloat16* kB = kb + b * n * H * Dh;
+    const __nv_bfloat16* vB = vb + b * n * H * Dh;
+    __nv_bfloat16* P = P0 + b * hi * nn;
+    for (int64_t h = 0; h < H; ++h) {  // S_g = Q_g K_h^T over the group's query heads
+      int rc = gemm_bf16(bop(qB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
+                         bop(kB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
+                         S + h * I * nn, 1, n, nn, s, *dev);
+      if (rc) return rc;
+    }
+    SoftArgs a{};
+    a.S = S;
+    a.rows = hi * n;
+    a.n = n;
+    a.qseg = d->q_segment_ids ? d->q_segment_ids + b * n : nullptr;
+    a.kseg = d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr;
+    a.qpos = d->q_positions ? d->q_positions + b * n : nullptr;
+    a.kpos = d->kv_positions ? d->kv_positions + b * n : nullptr;
+    a.scale = d->scale;
+    a.P = P;
+    a.lse = lse0 + b * hi * n;
+    attn_softmax_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "attention softmax launch");
+    for (int64_t h = 0; h < H; ++h) {  // O_g = P_g V_h
+      int rc = gemm_bf16(bop(P + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
+                         bop(vB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
+                         ob + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev);
+      if (rc) return rc;
+    }
+  }
+  return UFP8_OK;
+}
+
+extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, const void* k, const void* v,
+                                       const void* out, const void* dout, const void* saved, void* dq, void* dk,
+                                       void* dv, void* workspace, ufp8_stream_t stream) {
+  const char* who = "ufp8_attention_backward";
+  if (int rc = attn_check(d, who)) return rc;
+  if (d->batch > 0 && (!q || !k || !v || !out || !dout || !saved || !dq || !dk || !dv || !workspace))
+    return set_error(UFP8_ERR_INVALID, "%s: null pointer", who);
+  if ((reinterpret_cast<uintptr_t>(saved) | reinterpret_cast<uintptr_t>(workspace)) & 255u)
+    return set_error(UFP8_ERR_ALIGN, "%s: saved / workspace not 256-byte aligned", who);
+  if (d->batch == 0) return UFP8_OK;
+  DeviceInfo* dev;
+  if (int rc = device_info(&dev)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const AttnLayout L = attn_layout(*d);
+  const int64_t n = d->seq, H = d->kv_heads, I = d->group, Dh = d->head_dim, hi = H * I, nn = n * n;
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v);
+  const auto* ob = static_cast<const __nv_bfloat16*>(out);
+  const auto* gob = static_cast<const __nv_bfloat16*>(dout);
+  auto* dqb = static_cast<__nv_bfloat16*>(dq);
+  auto* dkb = static_cast<__nv_bfloat16*>(dk);
+  auto* dvb = static_cast<__nv_bfloat16*>(dv);
+  const auto* P0 = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(saved) + L.P);
+  float* dP = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + L.dP);
+  auto* dS = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + L.dS);
+  for (int64_t b = 0; b < d->batch; ++b) {
+    const __nv_bfloat16* qB = qb + b * n * hi * Dh;
+    const __nv_bfloat16* kB = kb + b * n * H * Dh;
+    const __nv_bfloat16* vB = vb + b * n * H * Dh;
+    const __nv_bfloat16* oB = ob + b * n * hi * Dh;
+    const __nv_bfloat16* goB = gob + b * n * hi * Dh;
+    const __nv_bfloat16* P = P0 + b * hi * nn;
+    for (int64_t h = 0; h < H; ++h) {  // dP_g = dO_g V_h^T
+      int rc = gemm_bf16(bop(goB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
+                         bop(vB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
+                         dP + h * I * nn, 1, n, nn, s, *dev);
+      if (rc) return rc;
+    }
+    SoftArgs a{};
+    a.rows = hi * n;
+    a.n = n;
+    a.scale = d->scale;
+    a.P = const_cast<__nv_bfloat16*>(P);
+    a.dP = dP;
+    a.O = oB;
+    a.dO = goB;
+    a.hi = hi;
+    a.d = Dh;
+    a.dS = dS;
+    attn_softmax_bwd_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_error(e, "attention softmax backward launch");
+    for (int64_t h = 0; h < H; ++h) {
+      // dQ_g = dS_g K_h
+      int rc = gemm_bf16(bop(dS + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
+                         bop(kB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
+                         dqb + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev);
+      if (rc) return rc;
+      // dK_h = sum_i dS_g^T Q_g, dV_h = sum_i P_g^T dO_g (contraction over the group's query rows)
+      rc = gemm_bf16(bop(dS + h * I * nn, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(I)),
+                     bop(qB + h * I * Dh, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)), n, Dh, n, 1,
+                     static_cast<int32_t>(I), dkb + b * n * H * Dh + h * Dh, 0, H * Dh, 0, s, *dev);
+      if (rc) return rc;
+      rc = gemm_bf16(bop(P + h * I * nn, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(I)),
+                     bop(goB + h * I * Dh, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)), n, Dh, n, 1,
+                     static_cast<int32_t>(I), dvb + b * n * H * Dh + h * Dh, 0, H * Dh, 0, s, *dev);
+      if (rc) return rc;
+    }
+  }
+  return UFP8_OK;
+}

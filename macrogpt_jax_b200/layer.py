@@ -8,8 +8,8 @@ activations), and the backward runs the GMLP backward followed by ufp8_rmsnorm_b
 results are the same bits as norm then GMLP, because the GMLP quantises exactly the bf16 tensor
 the norm would have returned.
 
-The attention half uses the projections of SoftmaxAttention; the attention kernel itself (kvax
-flash attention in the reference) is not part of this library and comes in as a callable.
+The attention half is SoftmaxAttention: FP8 projections, RoPE and the softmax attention of
+attention.py (or a caller's attention callable).
 """
 from __future__ import annotations
 
@@ -82,6 +82,7 @@ class TransformerLayer(torch.nn.Module):
         self.model_d = model_d
 
     def forward(self, x: torch.Tensor, attention: Optional[Callable] = None, **kwargs) -> torch.Tensor:
-        """`attention(q, k, v) -> [b, n, h, i, v]` is the attention kernel (see module docstring)."""
-        x = x + self.attn(self.attn_norm(x), attention)
+        """kwargs as the reference's layer takes them (position_ids, segment ids, rope); `attention`
+        replaces the softmax attention with a callable attention(q, k, v) -> [b, n, h, i, v]."""
+        x = x + self.attn(self.attn_norm(x), attention, **kwargs)
         return x + norm_mlp(self.mlp_norm, self.mlp, x)

@@ -1,6 +1,9 @@
-"""The Q/K/V/O projections of `SoftmaxAttention` (ueaj/model/soft_attn.py:20-124) on the FP8
-Einsum.  The attention itself (kvax flash attention in the reference, soft_attn.py:186-196)
-is not part of this library: `forward` takes it as a callable.
+"""`SoftmaxAttention` (ueaj/model/soft_attn.py:20-202): the Q/K/V/O projections on the FP8 Einsum,
+RoPE on q and k, and the softmax attention of attention.py (the reference calls kvax's flash
+attention there, soft_attn.py:186-196).  `forward(x, **kwargs)` follows the reference's __call__:
+position_ids (default 0..n-1), query/kv positions and segment ids from kwargs, the 'sp' / 'mup'
+or numeric scale; `forward(x, attention)` with a callable attention(q, k, v) -> [b, n, h, i, v]
+keeps the projections-only use.
 
 Kept from the reference: the constructor, the projection expressions and canonical weight
 layouts ("bnd,dhk->bnhk" for k and v, "bnd,dhik->bnhik" for q, "bnhiv,hivd->bnd" for o with
@@ -15,8 +18,10 @@ from __future__ import annotations
 
 from typing import Callable, Literal, Optional
 
+import numpy as np
 import torch
 
+from .attention import RoPE, softmax_attention
 from .configurator import config
 from .einsum import Einsum, Rngs, zeros_init
 
@@ -55,6 +60,7 @@ class SoftmaxAttention(torch.nn.Module):
             down_shards = (None, None, None, "tensor")  # attention first, then ring matmul
         self.o = o("bnhiv,hivd->bnd", initializer=zeros_init, size_dict=size_dict, rngs=rngs, dtype=torch.bfloat16,
                    mesh=mesh, sharding=down_shards)
+        self.rope = RoPE(rope_theta=rope_theta, rope_d=kq_d, value_dtype=torch.bfloat16) if rope_theta else None
 
     def project_qkv(self, x: torch.Tensor):
         """q [b, n, h, i, k], k [b, n, h, k], v [b, n, h, v]."""
@@ -69,9 +75,33 @@ class SoftmaxAttention(torch.nn.Module):
         """attn [b, n, h, i, v] -> [b, n, d]."""
         return self.o(attn)
 
-    def forward(self, x: torch.Tensor, attention: Optional[Callable] = None) -> torch.Tensor:
-        if attention is None:
-            raise NotImplementedError("the attention kernel is not part of this library; pass "
-                                      "attention(q, k, v) -> [b, n, h, i, v]")
+    def scale(self) -> float:
+        if self.attn_scale == "mup":
+            return float(np.float32(1.0 / self.kq_d))
+        if self.attn_scale == "sp":
+            return float(np.float32(1.0 / (self.kq_d ** 0.5)))
+        return float(self.attn_scale)
+
+    def forward(self, x: torch.Tensor, attention: Optional[Callable] = None, **kwargs) -> torch.Tensor:
+        if attention is not None:
+            q, k, v = self.project_qkv(x)
+            return self.project_out(attention(q, k, v))
+        b, n = x.shape[:2]
+        position_ids = kwargs.get("position_ids")
+        if position_ids is None:
+            position_ids = torch.arange(n, device=x.device)
         q, k, v = self.project_qkv(x)
-        return self.project_out(attention(q, k, v))
+        if self.rope is not None:
+            k = self.rope(k, position_ids=position_ids, rope_freqs=kwargs.get("rope"))
+            q = self.rope(q, position_ids=position_ids, rope_freqs=kwargs.get("rope"))
+        h, i = q.shape[2], q.shape[3]
+        qr = q.reshape(b, n, h * i, self.kq_d)
+        qpos = kwargs.get("query_positions", position_ids)
+        kpos = kwargs.get("kv_positions", position_ids)
+        qseg = kwargs.get("query_segment_ids")
+        kseg = kwargs.get("kv_segment_ids", qseg)
+        out = softmax_attention(qr, k, v, qpos, qseg, kpos, kseg, kwargs.get("attention_mask"), self.scale())
+        out = out.reshape(b, n, h, i, self.kq_d)
+        if self.act_fn is not None:
+            out = self.act_fn(out)
+        return self.project_out(out)

@@ -19,7 +19,9 @@ What it restates (reference file:line, relative to the macrogpt-jax repository):
   * the next-token loss on the lm_head logits (xent.py): ntp_args / chunked_softmax_cross_entropy
     ueaj/opt/next_token_loss.py:13-174 and LlamaModel.get_logits ueaj/model/model.py:140-165;
   * Muon's Newton-Schulz orthogonalisation (muon.py): ueaj/opt/multiscale.py:110-200 and the
-    optax 0.2.6 iteration it maps over the slices of a weight.
+    optax 0.2.6 iteration it maps over the slices of a weight;
+  * RoPE and the softmax attention of SoftmaxAttention (attention.py): ueaj/model/rope.py:10-104
+    and the kvax flash_attention call of ueaj/model/soft_attn.py:186-196.
 
 Parity pinning:
   * fp8 cast bytes: pinned.  fp8.py's own round-to-nearest-even cast is checked against
@@ -28,4 +30,4 @@ Parity pinning:
     here (jax, flax, optax absent, no network) and the reference ships no golden vectors;
     these functions are restatements, checked against an independent einsum (torch) only.
 """
-from . import fp8, muon, norm, path, xent  # noqa: F401
+from . import attention, fp8, muon, norm, path, xent  # noqa: F401

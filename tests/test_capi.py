@@ -55,7 +55,7 @@ def test_struct_layout_matches_header(tmp_path):
     cc = shutil.which("gcc") or shutil.which("cc")
     if cc is None:
         pytest.skip("no C compiler")
-    checks = [("ufp8_operand", C.Operand), ("ufp8_gemm_desc", C.GemmDesc)]
+    checks = [("ufp8_operand", C.Operand), ("ufp8_gemm_desc", C.GemmDesc), ("ufp8_attn_desc", C.AttnDesc)]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "ufp8.h"', "int main(void) {"]
     for cname, py in checks:
         lines.append(f'printf("{cname} sizeof %zu\\n", sizeof({cname}));')
