@@ -44,6 +44,10 @@ CONFIGS = {
     # Muon's Newton-Schulz orthogonalisation of one GMLP block's gradients at d 4096 / h 14336:
     # the fused weight's two [4096, 14336] slices and the down weight [14336, 4096], f32 in and out
     "muon_ns_d4096_h14336": dict(kind="muon", d=4096, h=14336, steps=5),
+    # one Llama-3-8B transformer layer (ueaj/model/layer.py:40-58): RMSNorm -> FP8 q/k/v projections
+    # (32 query heads in 8 groups of 4, head 128) -> RoPE -> causal softmax attention -> FP8 o
+    # projection, then RMSNorm -> FP8 GMLP (h 14336); forward and backward on one GPU
+    "layer_llama3_8b": dict(kind="layer", d=4096, h=14336, kv_heads=8, group=4, head_d=128, B=4, S=4096),
 }
 FP8_NOMINAL_TFLOPS = 4500.0  # B200 dense FP8 datasheet figure
 GMLP_D4096_GEMM_TRAFFIC = 1.651e9  # DRAM bytes per GEMM launch, T 16384 / d 4096 / h 14336, from one ncu
@@ -72,6 +76,16 @@ def ns_flops(m, n, steps):
     with s = min(m, n), l = max(m, n)."""
     s_, l_ = min(m, n), max(m, n)
     return steps * (4.0 * s_ * s_ * l_ + 2.0 * s_ ** 3)
+
+
+def layer_flops(cfg, T, S, B):
+    """Algorithmic FLOPs of one layer fwd+bwd: GMLP 18 T d h; projections 3 x 2 T d (q + k + v + o
+    widths); causal attention 3 x 2 x 2 B HI S^2 Dh / 2 (QK^T and PV forward, four products backward,
+    half the score matrix visible)."""
+    d, h, H, I, Dh = cfg["d"], cfg["h"], cfg["kv_heads"], cfg["group"], cfg["head_d"]
+    proj = 3.0 * 2.0 * T * d * (2 * H * I * Dh + 2 * H * Dh)
+    attn = 3.0 * 2.0 * 2.0 * B * H * I * S * S * Dh / 2.0
+    return 18.0 * T * d * h + proj + attn, proj, attn
 
 
 def load_peaks():
@@ -436,6 +450,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         return run_head(args, cfg, rank, world, local_rank, dev)
     if cfg["kind"] == "muon":
         return run_muon(args, cfg, rank, world, local_rank, dev)
+    if cfg["kind"] == "layer":
+        return run_layer(args, cfg, rank, world, local_rank, dev)
     d, h, B, S = cfg["d"], cfg["h"], cfg["B"], cfg["S"]
     T = B * S
     if world > 1 and cfg.get("norm"):
@@ -913,6 +929,112 @@ def run_muon(args, cfg, rank, world, local_rank, dev):
     return out
 
 
+def run_layer(args, cfg, rank, world, local_rank, dev):
+    """TransformerLayer(x, query_segment_ids=...) forward and the backward of its summed output."""
+    import numpy as np
+    import torch
+    from macrogpt_jax_b200 import _capi, ops
+    from macrogpt_jax_b200.einsum import Einsum, Rngs, scaled_normal_init
+    from macrogpt_jax_b200.layer import TransformerLayer
+    from macrogpt_jax_b200.mlp import GMLP
+    from macrogpt_jax_b200.soft_attn import SoftmaxAttention
+    if world > 1:
+        raise SystemExit("the transformer-layer workload runs on one GPU")
+    d, h, H, I, Dh, B, S = (cfg[k] for k in ("d", "h", "kv_heads", "group", "head_d", "B", "S"))
+    T = B * S
+    init = Einsum.override(initializer=scaled_normal_init(d ** -0.5))
+    attn = SoftmaxAttention.override(kq_d=Dh, kv_heads=H, kv_q_ratio=I, q=init, k=init, v=init, o=init)
+    mlp = GMLP.override(hidden_d=h, fused_proj=init, down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))
+    layer = TransformerLayer(d, attn=attn, mlp=mlp, rngs=Rngs(0))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+    x = torch.randn((B, S, d), generator=gen, device=dev).to(torch.bfloat16)
+    dy = (torch.randn((B, S, d), generator=gen, device=dev) * 1e-3).to(torch.bfloat16)
+    seg = torch.zeros((B, S), dtype=torch.int32, device=dev)
+    params = list(layer.parameters())
+
+    def fwd_bwd(xb, dyb):
+        xl = xb.detach().requires_grad_(True)
+        y = layer(xl, query_segment_ids=seg)
+        ev = torch.cuda.Event()
+        ev.record()
+        y.backward(dyb)
+        for p in params:
+            p.grad = None
+        return y, ev
+
+    for _ in range(args.warmup):
+        fwd_bwd(x, dy)
+    torch.cuda.synchronize()
+    timer = ops.KernelTimer()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    launches0 = _capi.launches
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ops.set_timer(timer)
+    ev0.record()
+    for _ in range(args.steps):
+        fwd_bwd(x, dy)
+    ev1.record()
+    ops.set_timer(None)
+    torch.cuda.synchronize()
+    launches = _capi.launches - launches0
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    summ = timer.summary()
+    peaks, peak_src = load_peaks()
+    fl, proj_fl, attn_fl = layer_flops(cfg, T, S, B)
+    g_n, g_ms, g_fl = summ.get("gemm", (0, 0.0, 0.0))
+    peak_fp8 = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
+    out = {
+        "metric": "FP8 Llama-3-8B transformer layer fwd+bwd tokens/s (TFLOP/s/GPU)",
+        "value": T * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
+        "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h, "q_heads": H * I,
+                   "kv_heads": H, "head_dim": Dh, "parallelism": "single GPU", "l2": "inputs larger than L2"},
+        "tflops_per_gpu": fl * args.steps / (ms / 1000.0) / 1e12,
+        "flops_per_step": {"total": fl, "projections": proj_fl, "attention_causal": attn_fl,
+                           "gmlp": 18.0 * T * d * h},
+        "roofline": {"kernel": "gemm_fp8_pair_kernel (FP8 projections and GMLP)", "bound": "tensor",
+                     "achieved": achieved, "peak": peak_fp8, "unit": "TFLOP/s",
+                     "frac": (achieved / peak_fp8) if achieved else None,
+                     "peak_source": f"2 x bf16_tflops_sustained, {peak_src}", "launches": g_n,
+                     "time_share": g_ms / ms if ms else None, "traffic": None,
+                     "note": "the attention's bf16 GEMMs are launched inside ufp8_attention_* and not in this record"},
+        "gpu_launches": launches, "clocks": clk,
+        "time_share": {k: round(v[1] / ms, 4) for k, v in summ.items()},
+    }
+    if not args.no_e2e:
+        ems = e2e_pipelined(fwd_bwd, x, dy, args.steps, lambda: None)
+        out["e2e"] = {"value": T * args.steps / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems / args.steps,
+                      "h2d_bytes_per_step": 2 * x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                      "path": "TransformerLayer forward + backward; x and dY in from pinned host memory each step "
+                              "(side stream, double-buffered), y back (side stream, overlapping the backward)"}
+    if not args.no_cpu_baseline:
+        # The oracle's GMLP (hidden slice, full tokens) and attention (one kv-head group of one sequence)
+        # timed and scaled by FLOPs; the projections at the GMLP port's FLOP rate.
+        from oracle import attention as oa
+        from oracle import path as op
+        tg = cpu_oracle_step(d, 768, T, seed=0)
+        rate = 18.0 * T * d * 768 / tg
+        rng = np.random.default_rng(0)
+        q = op.bf16_normal(rng, (1, S, I, Dh))
+        k, v, go = op.bf16_normal(rng, (1, S, 1, Dh)), op.bf16_normal(rng, (1, S, 1, Dh)), op.bf16_normal(rng, (1, S, I, Dh))
+        t0 = time.perf_counter()
+        o, P = oa.attention_forward(q, k, v, scale=Dh ** -0.5)
+        oa.attention_backward(go, o, P, q, k, v, Dh ** -0.5)
+        ta = (time.perf_counter() - t0) * B * H
+        est = 18.0 * T * d * h / rate + proj_fl / rate + ta
+        out["cpu_baseline"] = {"value": T / est, "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+                               "sample": f"oracle GMLP at {T} tokens on a hidden slice of 768 (FLOP rate applied to the "
+                                         f"GMLP and projection FLOPs) plus the oracle attention fwd+bwd of one kv-head "
+                                         f"group of one {S}-token sequence times {B * H}",
+                               "est_ms_per_step": est * 1000.0}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -947,6 +1069,13 @@ def main():
         args.config_desc = (f"attention projections fwd+bwd (fused QKV {cfg['d']}->{3 * cfg['d']}, O "
                             f"{cfg['d']}->{cfg['d']}), {cfg['B'] * cfg['S']} tokens (B{cfg['B']} x S{cfg['S']}), "
                             f"{cfg['heads']} heads x {cfg['head_d']}, FP8 e4m3/e5m2")
+        if args.impl == "reference":
+            raise SystemExit("the CPU arm covers the GMLP workloads")
+    elif cfg["kind"] == "layer":
+        args.config_desc = (f"Llama-3-8B transformer layer fwd+bwd: RMSNorm -> FP8 q/k/v ({cfg['kv_heads'] * cfg['group']} "
+                            f"query heads, {cfg['kv_heads']} kv heads x {cfg['head_d']}) -> RoPE -> causal softmax "
+                            f"attention -> FP8 o, RMSNorm -> FP8 GMLP (h {cfg['h']}), {cfg['B'] * cfg['S']} tokens "
+                            f"(B{cfg['B']} x S{cfg['S']})")
         if args.impl == "reference":
             raise SystemExit("the CPU arm covers the GMLP workloads")
     elif cfg["kind"] == "muon":

@@ -156,7 +156,8 @@ typedef struct ufp8_operand {
   const float* inv_scale; /* device f32: 1/s of this operand */
 } ufp8_operand;
 
-/* D[g] = sum_{kb < k_batches} A[g or kb] * B[g or kb]^T for g < batch.
+/* D[g] = sum_{kb < k_batches} A[g * k_batches + kb] * B[g * k_batches + kb]^T for g < batch (with
+ * k_batches == 1: A[g] B[g]^T, a one-slice operand broadcast over the batch).
  * k_batches > 1 concatenates K over operand slices (e.g. dx = sum_i dUG[i] W[i]^T).
  * UFP8_EPI_SWIGLU reads B slice 0 as `up` and slice 1 as `gate` for the same N range;
  * D then holds U (slice 0) and G (slice 1) and `h` receives U * silu(G).

@@ -21,6 +21,7 @@ import numpy as np
 import torch
 
 from . import _capi as C
+from . import ops
 from .configurator import config
 
 
@@ -122,8 +123,10 @@ class _AttentionFn(torch.autograd.Function):
         ws = torch.empty(max(fwd, 1), dtype=torch.uint8, device=dev)
         saved = torch.empty(max(saved_b, 1), dtype=torch.uint8, device=dev)
         out = torch.empty_like(q)
-        C.attention_forward(desc, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), saved.data_ptr(),
-                            ws.data_ptr(), _stream())
+        fl = 2.0 * 2.0 * b * hi * n * n * dh  # QK^T and PV over the full score matrix
+        ops._launch("attention_fwd", fl, lambda: C.attention_forward(
+            desc, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), saved.data_ptr(), ws.data_ptr(),
+            _stream()))
         ctx.save_for_backward(q, k, v, out, saved, qseg, kseg, qpos, kpos)
         ctx.desc, ctx.bwd = desc, bwd
         return out
@@ -134,8 +137,11 @@ class _AttentionFn(torch.autograd.Function):
         dout = dout.to(torch.bfloat16).contiguous()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         ws = torch.empty(max(ctx.bwd, 1), dtype=torch.uint8, device=q.device)
-        C.attention_backward(ctx.desc, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
-                             saved.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), _stream())
+        b, n, hi, dh = q.shape
+        fl = 4.0 * 2.0 * b * hi * n * n * dh  # dP, dQ, dK, dV over the full score matrix
+        ops._launch("attention_bwd", fl, lambda: C.attention_backward(
+            ctx.desc, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(), saved.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ws.data_ptr(), _stream()))
         return dq, dk, dv, None, None, None, None, None, None
 
 

@@ -97,9 +97,7 @@ struct SoftArgs {
   __nv_bfloat16* dS;
 };
 
-__device__ __forceinline__ bool visible(const SoftArgs& a, int64_t q, int64_t k, int32_t sq, int32_t pq) {
-  const int32_t sk = a.kseg ? a.kseg[k] : 0;
-  const int32_t pk = a.kpos ? a.kpos[k] : static_cast<int32_t>(k);
+__device__ __forceinline__ bool visible(int32_t sq, int32_t pq, int32_t sk, int32_t pk) {
   return sq >= 0 && sk == sq && pk <= pq;
 }
 
@@ -137,35 +135,77 @@ __device__ __forceinline__ void block_max_sum(float& m, float& s, float* sm, flo
   s = ss[0];
 }
 
+// Visibility of the 4 keys k4 * 4 .. k4 * 4 + 3 for a query (segment sq, position pq).
+__device__ __forceinline__ void vis4(const SoftArgs& a, int64_t k4, int32_t sq, int32_t pq, bool (&v)[4]) {
+  const int4 ks = a.kseg ? reinterpret_cast<const int4*>(a.kseg)[k4] : make_int4(0, 0, 0, 0);
+  const int64_t k0 = k4 * 4;
+  const int4 kp = a.kpos ? reinterpret_cast<const int4*>(a.kpos)[k4]
+                         : make_int4(static_cast<int>(k0), static_cast<int>(k0 + 1), static_cast<int>(k0 + 2),
+                                     static_cast<int>(k0 + 3));
+  v[0] = visible(sq, pq, ks.x, kp.x);
+  v[1] = visible(sq, pq, ks.y, kp.y);
+  v[2] = visible(sq, pq, ks.z, kp.z);
+  v[3] = visible(sq, pq, ks.w, kp.w);
+}
+
+// Keys past `lim` (in groups of 4) cannot be visible: with the default key positions 0..n-1 a key
+// is visible only at position <= the query's.
+__device__ __forceinline__ int64_t row_limit4(const SoftArgs& a, int32_t sq, int32_t pq) {
+  if (sq < 0) return 0;
+  if (a.kpos) return a.n / 4;
+  const int64_t last = pq < 0 ? -1 : (pq >= a.n ? a.n - 1 : pq);
+  return (last + 4) / 4;
+}
+
 // One CTA per score row: masked online (max, sum exp) of scale * s, then P = exp(scale s - M) / S.
+// 16-byte score loads, 8-byte probability stores (n is a multiple of 8).
 __global__ void __launch_bounds__(kAThreads) attn_softmax_kernel(const SoftArgs a) {
   const int64_t row = blockIdx.x;
   const int64_t q = row % a.n;
-  const float* sr = a.S + row * a.n;
+  const float4* sr = reinterpret_cast<const float4*>(a.S + row * a.n);
   const int32_t sq = a.qseg ? a.qseg[q] : 0;
   const int32_t pq = a.qpos ? a.qpos[q] : static_cast<int32_t>(q);
+  const int64_t lim = row_limit4(a, sq, pq);
   float m = -INFINITY, s = 0.0f;
-  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
-    if (!visible(a, q, k, sq, pq)) continue;
-    const float v = __fmul_rn(sr[k], a.scale);
-    if (v > m) {
-      s *= __expf(m - v);
-      m = v;
+  for (int64_t k4 = threadIdx.x; k4 < lim; k4 += kAThreads) {
+    bool v[4];
+    vis4(a, k4, sq, pq, v);
+    const float4 x = sr[k4];
+    const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (!v[j]) continue;
+      const float t = __fmul_rn(xs[j], a.scale);
+      if (t > m) {
+        s *= __expf(m - t);
+        m = t;
+      }
+      s += __expf(t - m);
     }
-    s += __expf(v - m);
   }
   __shared__ float sm[kAThreads / 32], ss[kAThreads / 32];
   block_max_sum(m, s, sm, ss);
   const float inv = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
-  __nv_bfloat16* pr = a.P + row * a.n;
-  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
-    const float p = visible(a, q, k, sq, pq) ? __fmul_rn(__expf(__fsub_rn(__fmul_rn(sr[k], a.scale), m)), inv) : 0.0f;
-    pr[k] = __float2bfloat16_rn(p);
+  uint2* pr = reinterpret_cast<uint2*>(a.P + row * a.n);
+  for (int64_t k4 = threadIdx.x; k4 < a.n / 4; k4 += kAThreads) {
+    float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (k4 < lim) {
+      bool v[4];
+      vis4(a, k4, sq, pq, v);
+      const float4 x = sr[k4];
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (v[j]) p[j] = __fmul_rn(__expf(__fsub_rn(__fmul_rn(xs[j], a.scale), m)), inv);
+    }
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(p[0], p[1]), hi = __floats2bfloat162_rn(p[2], p[3]);
+    pr[k4] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
   }
   if (threadIdx.x == 0) a.lse[row] = s > 0.0f ? __fadd_rn(m, logf(s)) : -INFINITY;
 }
 
-// One CTA per row: D = sum_d dO O (f32, fixed order), dS = bf16(scale * P (dP - D)).
+// One CTA per row: D = sum_d dO O (f32, fixed order), dS = bf16(scale * P (dP - D)); past the row's
+// key limit P is 0 and dS is written as 0 without reading P or dP.
 __global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftArgs a) {
   const int64_t row = blockIdx.x;
   const int64_t g = row / a.n, q = row - g * a.n;
@@ -182,12 +222,27 @@ __global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftA
     __syncthreads();
   }
   const float D = red[0];
-  const __nv_bfloat16* pr = a.P + row * a.n;
-  const float* dpr = a.dP + row * a.n;
-  __nv_bfloat16* dsr = a.dS + row * a.n;
-  for (int64_t k = threadIdx.x; k < a.n; k += kAThreads) {
-    const float p = __bfloat162float(pr[k]);
-    dsr[k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(p, __fsub_rn(dpr[k], D)), a.scale));
+  const int32_t sq = a.qseg ? a.qseg[q] : 0;
+  const int32_t pq = a.qpos ? a.qpos[q] : static_cast<int32_t>(q);
+  const int64_t lim = row_limit4(a, sq, pq);
+  const uint2* pr = reinterpret_cast<const uint2*>(a.P + row * a.n);
+  const float4* dpr = reinterpret_cast<const float4*>(a.dP + row * a.n);
+  uint2* dsr = reinterpret_cast<uint2*>(a.dS + row * a.n);
+  for (int64_t k4 = threadIdx.x; k4 < a.n / 4; k4 += kAThreads) {
+    uint2 o2 = make_uint2(0u, 0u);
+    if (k4 < lim) {
+      const uint2 pw = pr[k4];
+      const float4 dp = dpr[k4];
+      const float p[4] = {__uint_as_float(pw.x << 16), __uint_as_float(pw.x & 0xFFFF0000u),
+                          __uint_as_float(pw.y << 16), __uint_as_float(pw.y & 0xFFFF0000u)};
+      const float dpv[4] = {dp.x, dp.y, dp.z, dp.w};
+      float r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) r[j] = __fmul_rn(__fmul_rn(p[j], __fsub_rn(dpv[j], D)), a.scale);
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(r[0], r[1]), hi = __floats2bfloat162_rn(r[2], r[3]);
+      o2 = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    }
+    dsr[k4] = o2;
   }
 }
 
@@ -226,6 +281,9 @@ int attn_check(const ufp8_attn_desc* d, const char* who) {
     return set_error(UFP8_ERR_INVALID, "%s: bad shape (seq, heads >= 1; head_dim even and a multiple of 8)", who);
   if (d->seq % 8) return set_error(UFP8_ERR_UNSUPPORTED, "%s: seq must be a multiple of 8 (16-byte rows of P)", who);
   if (d->seq >= (int64_t(1) << 31)) return set_error(UFP8_ERR_INVALID, "%s: seq exceeds 2^31", who);
+  const uintptr_t ids = reinterpret_cast<uintptr_t>(d->q_segment_ids) | reinterpret_cast<uintptr_t>(d->kv_segment_ids) |
+                        reinterpret_cast<uintptr_t>(d->q_positions) | reinterpret_cast<uintptr_t>(d->kv_positions);
+  if (ids & 15u) return set_error(UFP8_ERR_ALIGN, "%s: segment id / position arrays not 16-byte aligned", who);
   return UFP8_OK;
 }
 
@@ -409,6 +467,10 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
     a.hi = hi;
     a.d = Dh;
     a.dS = dS;
+    a.qseg = d->q_segment_ids ? d->q_segment_ids + b * n : nullptr;
+    a.kseg = d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr;
+    a.qpos = d->q_positions ? d->q_positions + b * n : nullptr;
+    a.kpos = d->kv_positions ? d->kv_positions + b * n : nullptr;
     attn_softmax_bwd_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "attention softmax backward launch");
@@ -418,16 +480,17 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
                          bop(kB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
                          dqb + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev);
       if (rc) return rc;
-      // dK_h = sum_i dS_g^T Q_g, dV_h = sum_i P_g^T dO_g (contraction over the group's query rows)
-      rc = gemm_bf16(bop(dS + h * I * nn, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(I)),
-                     bop(qB + h * I * Dh, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)), n, Dh, n, 1,
-                     static_cast<int32_t>(I), dkb + b * n * H * Dh + h * Dh, 0, H * Dh, 0, s, *dev);
-      if (rc) return rc;
-      rc = gemm_bf16(bop(P + h * I * nn, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(I)),
-                     bop(goB + h * I * Dh, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)), n, Dh, n, 1,
-                     static_cast<int32_t>(I), dvb + b * n * H * Dh + h * Dh, 0, H * Dh, 0, s, *dev);
-      if (rc) return rc;
     }
+    // dK_h = sum_i dS_g^T Q_g, dV_h = sum_i P_g^T dO_g: one launch over the kv heads (batch H), the
+    // contraction running over the group's query rows (k_batches I, slice h * I + i = g).
+    int rc = gemm_bf16(bop(dS, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
+                       bop(qB, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)), n, Dh, n,
+                       static_cast<int32_t>(H), static_cast<int32_t>(I), dkb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev);
+    if (rc) return rc;
+    rc = gemm_bf16(bop(P, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
+                   bop(goB, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)), n, Dh, n,
+                   static_cast<int32_t>(H), static_cast<int32_t>(I), dvb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev);
+    if (rc) return rc;
   }
   return UFP8_OK;
 }

@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
           if (args.a_major == UFP8_K_MAJOR)
             tma_load_3d(sa, &tmA, &full[stage], k0, mb * kBM, az);
           else
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               bz = half;
             } else {
               n0 = nb * kBN + half * 128;
-              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
             }
             if (args.b_major == UFP8_K_MAJOR)
               tma_load_3d(sb + half * kHalfBytesB, &tmB, &full[stage], k0, n0, bz);
@@ -733,14 +733,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
           int n0, bz;
           if (swiglu) {
             n0 = nb * 128;
             bz = static_cast<int>(rank);
           } else {
             n0 = nb * kBN + static_cast<int>(rank) * 128;
-            bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+            bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
           }
 #pragma unroll
           for (int j = 0; j < KCH; ++j) {
@@ -1297,7 +1297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
           if (args.a_major == UFP8_K_MAJOR)
             tma_load_3d_pair(sa, &tmA, bar, k0, row0, az);
           else
@@ -1310,7 +1310,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               bz = static_cast<int>(rank);
             } else {
               n0 = nb * 2 * kBN + j * kBN + static_cast<int>(rank) * 128;
-              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? kb : g);
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
             }
             uint8_t* sb = sa + (1 + j) * kPHalfBytes;
             if (args.b_major == UFP8_K_MAJOR)
@@ -1646,8 +1646,6 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
                 int variant, int group_m) {
   if (d.M < 0 || d.N < 0 || d.K < 0) return set_error(UFP8_ERR_INVALID, "negative GEMM extent");
   if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
-  if (d.batch > 1 && d.k_batches > 1)
-    return set_error(UFP8_ERR_UNSUPPORTED, "batch > 1 together with k_batches > 1 is not supported");
   if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU &&
       d.epilogue != UFP8_EPI_RS_PUSH && d.epilogue != UFP8_EPI_XENT && d.epilogue != UFP8_EPI_AXPBY)
     return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
@@ -1758,9 +1756,12 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   }
 
   const bool swiglu = d.epilogue == UFP8_EPI_SWIGLU;
-  int rc = check_operand(d.a, d.M, d.K, d.k_batches > 1 ? d.k_batches : (d.a.batch_count > 1 ? d.batch : 1), "A");
+  // k_batches > 1: operand slice g * k_batches + kb holds batch g's K block kb.
+  const int64_t kslices = static_cast<int64_t>(d.batch) * d.k_batches;
+  if (kslices >= (int64_t(1) << 31)) return set_error(UFP8_ERR_INVALID, "batch * k_batches exceeds 2^31");
+  int rc = check_operand(d.a, d.M, d.K, d.k_batches > 1 ? static_cast<int>(kslices) : (d.a.batch_count > 1 ? d.batch : 1), "A");
   if (rc) return rc;
-  rc = check_operand(d.b, d.N, d.K, swiglu ? 2 : (d.k_batches > 1 ? d.k_batches : (d.b.batch_count > 1 ? d.batch : 1)),
+  rc = check_operand(d.b, d.N, d.K, swiglu ? 2 : (d.k_batches > 1 ? static_cast<int>(kslices) : (d.b.batch_count > 1 ? d.batch : 1)),
                      "B");
   if (rc) return rc;
 

@@ -87,17 +87,17 @@ class SoftmaxAttention(torch.nn.Module):
             q, k, v = self.project_qkv(x)
             return self.project_out(attention(q, k, v))
         b, n = x.shape[:2]
-        position_ids = kwargs.get("position_ids")
-        if position_ids is None:
-            position_ids = torch.arange(n, device=x.device)
+        given = kwargs.get("position_ids")
+        position_ids = given if given is not None else torch.arange(n, device=x.device)
         q, k, v = self.project_qkv(x)
         if self.rope is not None:
             k = self.rope(k, position_ids=position_ids, rope_freqs=kwargs.get("rope"))
             q = self.rope(q, position_ids=position_ids, rope_freqs=kwargs.get("rope"))
         h, i = q.shape[2], q.shape[3]
         qr = q.reshape(b, n, h * i, self.kq_d)
-        qpos = kwargs.get("query_positions", position_ids)
-        kpos = kwargs.get("kv_positions", position_ids)
+        # positions 0..n-1 unless given (None lets the kernels use them implicitly)
+        qpos = kwargs.get("query_positions", given)
+        kpos = kwargs.get("kv_positions", given)
         qseg = kwargs.get("query_segment_ids")
         kseg = kwargs.get("kv_segment_ids", qseg)
         out = softmax_attention(qr, k, v, qpos, qseg, kpos, kseg, kwargs.get("attention_mask"), self.scale())
