@@ -77,6 +77,14 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_EPI_XENT 4    /* D = logits (bf16, optionally soft-capped) + per-row softmax partials  */
 #define UFP8_EPI_AXPBY 5   /* D = alpha * acc * sa * sb + beta * C (bf16 operands only)            */
 
+/* tile masks of a bf16 GEMM (ufp8_gemm_desc.tile_mask; tiles are 256 x 256): causal attention's
+ * products skip what its mask zeroes */
+#define UFP8_TILES_ALL 0
+#define UFP8_TILES_LOWER 1       /* only tiles whose N tile index <= M tile index; D elsewhere not written */
+#define UFP8_TILES_K_TO_DIAG 2   /* M tile m contracts K in [0, 256 (m + 1)) of each K slice           */
+#define UFP8_TILES_K_FROM_DIAG 3 /* M tile m contracts K in [256 m, K) of each K slice                  */
+/* (tile masks: an M tile whose K range is empty is not written either)                              */
+
 const char* ufp8_last_error(void);
 int ufp8_abi_version(void);
 
@@ -216,6 +224,8 @@ typedef struct ufp8_gemm_desc {
   int64_t c_batch_stride;
   float alpha;
   float beta;
+  int32_t tile_mask; /* UFP8_TILES_* (bf16 operands only) */
+  int32_t reserved2;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);

@@ -20,6 +20,7 @@ BF16 = 2  # bf16 GEMM operands; unquantised output of ufp8_xent_backward
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH, EPI_XENT, EPI_AXPBY = 0, 1, 2, 3, 4, 5
+TILES_ALL, TILES_LOWER, TILES_K_TO_DIAG, TILES_K_FROM_DIAG = 0, 1, 2, 3
 GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE, GEMM_CTA_PAIR_N512 = (
     0, 1, 2, 3, 4, 5)
 
@@ -113,6 +114,8 @@ class GemmDesc(ctypes.Structure):
         ("c_batch_stride", ctypes.c_int64),
         ("alpha", ctypes.c_float),
         ("beta", ctypes.c_float),
+        ("tile_mask", ctypes.c_int32),
+        ("reserved2", ctypes.c_int32),
     ]
 
 

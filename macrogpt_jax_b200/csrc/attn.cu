@@ -16,6 +16,9 @@
 //   forward:  S_g = Q_g K_h^T            softmax rows -> P_g (bf16), lse     O_g = P_g V_h
 //   backward: dP_g = dO_g V_h^T          dS_g = scale * P_g (dP_g - rowsum(dO_g O_g))
 //             dQ_g = dS_g K_h            dK_h = sum_i dS_g^T Q_g             dV_h = sum_i P_g^T dO_g
+// With the default positions the masked upper triangle is skipped: the score products compute only
+// the 256 x 256 tiles on or below the diagonal, P V and dS K contract each query tile only up to its
+// diagonal, dS^T Q and P^T dO each key tile only from its diagonal (UFP8_TILES_*).
 // No transposed copy is made (MN-major operands).  RoPE: one kernel builds the bf16 sin/cos table
 // from positions (f32 angle = position * inv_freq, sinf/cosf, then bf16, as the reference's
 // compute_rope_embedding), one applies the rotation (bf16 rounding after each product and sum, as
@@ -258,8 +261,10 @@ ufp8_operand bop(const void* p, int major, int64_t ld, int64_t bstride, int32_t 
 }
 
 int gemm_bf16(const ufp8_operand& A, const ufp8_operand& B, int64_t M, int64_t N, int64_t K, int32_t batch,
-              int32_t kb, void* D, int d_f32, int64_t ldd, int64_t dbs, cudaStream_t s, const DeviceInfo& dev) {
+              int32_t kb, void* D, int d_f32, int64_t ldd, int64_t dbs, cudaStream_t s, const DeviceInfo& dev,
+              int tile_mask = UFP8_TILES_ALL) {
   ufp8_gemm_desc d{};
+  d.tile_mask = tile_mask;
   d.M = M;
   d.N = N;
   d.K = K;
@@ -375,6 +380,9 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const AttnLayout L = attn_layout(*d);
   const int64_t n = d->seq, H = d->kv_heads, I = d->group, Dh = d->head_dim, hi = H * I, nn = n * n;
+  // Default positions (0..n-1 for queries and keys): a key tile past the query tile is fully
+  // masked, so the products skip it (the softmax kernels write the zeros of P / dS there).
+  const bool causal = d->q_positions == nullptr && d->kv_positions == nullptr;
   const auto* qb = static_cast<const __nv_bfloat16*>(q);
   const auto* kb = static_cast<const __nv_bfloat16*>(k);
   const auto* vb = static_cast<const __nv_bfloat16*>(v);
@@ -390,7 +398,7 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
     for (int64_t h = 0; h < H; ++h) {  // S_g = Q_g K_h^T over the group's query heads
       int rc = gemm_bf16(bop(qB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
                          bop(kB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
-                         S + h * I * nn, 1, n, nn, s, *dev);
+                         S + h * I * nn, 1, n, nn, s, *dev, causal ? UFP8_TILES_LOWER : UFP8_TILES_ALL);
       if (rc) return rc;
     }
     SoftArgs a{};
@@ -410,7 +418,8 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
     for (int64_t h = 0; h < H; ++h) {  // O_g = P_g V_h
       int rc = gemm_bf16(bop(P + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
                          bop(vB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
-                         ob + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev);
+                         ob + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev,
+                         causal ? UFP8_TILES_K_TO_DIAG : UFP8_TILES_ALL);
       if (rc) return rc;
     }
   }
@@ -432,6 +441,9 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const AttnLayout L = attn_layout(*d);
   const int64_t n = d->seq, H = d->kv_heads, I = d->group, Dh = d->head_dim, hi = H * I, nn = n * n;
+  // Default positions (0..n-1 for queries and keys): a key tile past the query tile is fully
+  // masked, so the products skip it (the softmax kernels write the zeros of P / dS there).
+  const bool causal = d->q_positions == nullptr && d->kv_positions == nullptr;
   const auto* qb = static_cast<const __nv_bfloat16*>(q);
   const auto* kb = static_cast<const __nv_bfloat16*>(k);
   const auto* vb = static_cast<const __nv_bfloat16*>(v);
@@ -453,7 +465,7 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
     for (int64_t h = 0; h < H; ++h) {  // dP_g = dO_g V_h^T
       int rc = gemm_bf16(bop(goB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
                          bop(vB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
-                         dP + h * I * nn, 1, n, nn, s, *dev);
+                         dP + h * I * nn, 1, n, nn, s, *dev, causal ? UFP8_TILES_LOWER : UFP8_TILES_ALL);
       if (rc) return rc;
     }
     SoftArgs a{};
@@ -478,18 +490,21 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
       // dQ_g = dS_g K_h
       int rc = gemm_bf16(bop(dS + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
                          bop(kB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
-                         dqb + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev);
+                         dqb + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev,
+                         causal ? UFP8_TILES_K_TO_DIAG : UFP8_TILES_ALL);
       if (rc) return rc;
     }
     // dK_h = sum_i dS_g^T Q_g, dV_h = sum_i P_g^T dO_g: one launch over the kv heads (batch H), the
     // contraction running over the group's query rows (k_batches I, slice h * I + i = g).
     int rc = gemm_bf16(bop(dS, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
                        bop(qB, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)), n, Dh, n,
-                       static_cast<int32_t>(H), static_cast<int32_t>(I), dkb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev);
+                       static_cast<int32_t>(H), static_cast<int32_t>(I), dkb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev,
+                       causal ? UFP8_TILES_K_FROM_DIAG : UFP8_TILES_ALL);
     if (rc) return rc;
     rc = gemm_bf16(bop(P, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
                    bop(goB, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)), n, Dh, n,
-                   static_cast<int32_t>(H), static_cast<int32_t>(I), dvb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev);
+                   static_cast<int32_t>(H), static_cast<int32_t>(I), dvb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev,
+                   causal ? UFP8_TILES_K_FROM_DIAG : UFP8_TILES_ALL);
     if (rc) return rc;
   }
   return UFP8_OK;

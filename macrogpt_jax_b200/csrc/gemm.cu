@@ -85,7 +85,23 @@ struct GemmArgs {
   long long ldc, c_bstride;
   float alpha_mul, beta;
   int c_vec;  // AXPBY: C rows 16-byte aligned
+  int tile_mask;  // UFP8_TILES_* (bf16 operands only)
 };
+
+// The tiles of a masked bf16 GEMM (UFP8_TILES_*): whether M tile mb / N tile nb runs, and its k-step
+// range [lo, hi) within each K slice (k-steps of `step` elements; tiles are 256 x 256).
+__device__ __forceinline__ bool masked_tile(const GemmArgs& a, int mb, int nb, int step, int& lo, int& hi) {
+  lo = 0;
+  hi = a.ksteps;
+  if (a.tile_mask == UFP8_TILES_LOWER) return nb <= mb;
+  if (a.tile_mask == UFP8_TILES_K_TO_DIAG) {
+    const int e = (mb + 1) * 2 * kBM;
+    hi = min(hi, (e + step - 1) / step);
+  } else if (a.tile_mask == UFP8_TILES_K_FROM_DIAG) {
+    lo = (mb * 2 * kBM) / step;
+  }
+  return hi > lo;
+}
 
 // Waits until the all-gather block of rank s has arrived (flag == epoch), bounded like the
 // pipeline waits; on expiry raises abort_flag and the peer-timeout status bit.  After the
@@ -712,6 +728,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters) {
         int g, mb, nb;
         map_tile(tile, args, g, mb, nb);
+        constexpr int kKc = kBf16 ? kBK / 2 : kBK;  // K elements per 128-byte chunk
+        int lo = 0, hi = args.ksteps;
+        if constexpr (kBf16) {
+          if (!masked_tile(args, mb, nb, KCH * kKc, lo, hi)) continue;
+        }
+        const int span = hi - lo;
         const int row0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
         if (args.ag_flags != nullptr && row0 < args.M) {
           const int src = static_cast<int>(row0 / args.ag_rows);
@@ -720,11 +742,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             arrived |= 1u << src;
           }
         }
-        for (int ks = 0; ks < total_k; ++ks) {
+        for (int ks = 0; ks < args.k_batches * span; ++ks) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
-          const int kb = ks / args.ksteps;
-          constexpr int kKc = kBf16 ? kBK / 2 : kBK;  // K elements per 128-byte chunk
-          const int k0 = (ks - kb * args.ksteps) * (KCH * kKc);
+          const int kb = ks / span;
+          const int k0 = (lo + ks - kb * span) * (KCH * kKc);
           uint8_t* sa = smem + stage * kStageBytes;
           uint8_t* sb = sa + KCH * kPHalfBytes;
           if (leader) {
@@ -793,13 +814,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       for (int tile = cluster_id; tile < num_tiles && !*abort_flag; tile += num_clusters, ++local) {
+        int tile_k = total_k;
+        if constexpr (kBf16) {
+          int g, mb, nb, lo, hi;
+          map_tile(tile, args, g, mb, nb);
+          if (!masked_tile(args, mb, nb, KCH * (kBK / 2), lo, hi)) {
+            --local;  // a skipped tile takes no TMEM buffer
+            continue;
+          }
+          tile_k = args.k_batches * (hi - lo);
+        }
         const int buf = local & 1;
         const uint32_t tphase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tphase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
         bool ok = true;
-        for (int ks = 0; ks < total_k; ++ks) {
+        for (int ks = 0; ks < tile_k; ++ks) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -880,6 +911,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     }
     int local = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
+      if constexpr (kBf16) {
+        int g_, mb_, nb_, lo_, hi_;
+        map_tile(tile, args, g_, mb_, nb_);
+        if (!masked_tile(args, mb_, nb_, KCH * (kBK / 2), lo_, hi_)) {
+          --local;
+          continue;
+        }
+      }
       const int buf = local & 1;
       const uint32_t tphase = (local >> 1) & 1;
       bool ok = mbar_wait(&tfull[buf], tphase, abort_flag);
@@ -1660,6 +1699,10 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
     if (reinterpret_cast<uintptr_t>(d.c) & 1u) return set_error(UFP8_ERR_ALIGN, "AXPBY: c not 2-byte aligned");
     if (d.K == 0 && d.M > 0 && d.N > 0) return set_error(UFP8_ERR_UNSUPPORTED, "AXPBY with K == 0");
   }
+  if (d.tile_mask < UFP8_TILES_ALL || d.tile_mask > UFP8_TILES_K_FROM_DIAG)
+    return set_error(UFP8_ERR_INVALID, "unknown tile_mask %d", d.tile_mask);
+  if (d.tile_mask != UFP8_TILES_ALL && !bf16)
+    return set_error(UFP8_ERR_UNSUPPORTED, "tile masks take bf16 operands");
   if (bf16 && (variant == UFP8_GEMM_SINGLE_CTA || d.ag_flags != nullptr))
     return set_error(UFP8_ERR_UNSUPPORTED, "bf16 operands run on the CTA-pair kernel without all-gather");
   if (d.epilogue == UFP8_EPI_XENT) {
@@ -1747,6 +1790,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.alpha_mul = d.epilogue == UFP8_EPI_AXPBY ? d.alpha : 1.0f;
   a.beta = d.beta;
   a.c_vec = a.c != nullptr && aligned16(d.c) && (d.ldc * 2) % 16 == 0 && (d.c_batch_stride * 2) % 16 == 0;
+  a.tile_mask = d.tile_mask;
 
   if (d.K == 0) {
     if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");

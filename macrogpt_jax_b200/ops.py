@@ -130,7 +130,7 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
          h: torch.Tensor | None = None, ldh: int = 0, ug: torch.Tensor | None = None, ldug: int = 0,
          ug_batch_stride: int = 0, amax_out: torch.Tensor | None = None, rs_slots: int | None = None,
          rs_rank: int = 0, rs_rows_per_rank: int = 0, ag: tuple | None = None,
-         xent: tuple | None = None, axpby: tuple | None = None) -> None:
+         xent: tuple | None = None, axpby: tuple | None = None, tile_mask: int = 0) -> None:
     desc = C.GemmDesc()
     desc.M, desc.N, desc.K = M, N, K
     desc.batch, desc.k_batches = batch, k_batches
@@ -150,6 +150,7 @@ def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ld
         desc.ag_flags, desc.ag_epoch, desc.ag_rank, desc.ag_rows_per_rank = ag
     if xent is not None:  # (stats tensor, pitch in pairs, soft cap): the XENT epilogue's partials
         desc.xent_stats, desc.xent_ld_stats, desc.xent_cap = xent[0].data_ptr(), xent[1], xent[2]
+    desc.tile_mask = tile_mask
     if axpby is not None:  # (C tensor, ldc, c batch stride, alpha, beta): D = alpha acc + beta C
         desc.c, desc.ldc, desc.c_batch_stride = axpby[0].data_ptr(), axpby[1], axpby[2]
         desc.alpha, desc.beta = axpby[3], axpby[4]

@@ -76,6 +76,28 @@ def test_attention_against_oracle(cuda, b, n, h, grp, dh):
         compare(bf16_bits_to_f32(torch_bf16_to_bits(t)), ref)
 
 
+@pytest.mark.parametrize("b,n,h,grp,dh", [(2, 520, 2, 2, 64), (1, 768, 1, 4, 128)])
+def test_attention_default_positions_against_oracle(cuda, b, n, h, grp, dh):
+    """Without positions (0..n-1) the products skip the masked tiles (UFP8_TILES_*): same results."""
+    import torch
+    from macrogpt_jax_b200.attention import softmax_attention
+    rng = np.random.default_rng(n + grp)
+    qb = bf16_normal(rng, (b, n, h * grp, dh))
+    kb, vb = bf16_normal(rng, (b, n, h, dh)), bf16_normal(rng, (b, n, h, dh))
+    seg = _segments(b, n, rng)
+    q, k, v = (bits_to_torch_bf16(t, cuda).requires_grad_(True) for t in (qb, kb, vb))
+    segt = torch.from_numpy(seg).to(cuda)
+    out = softmax_attention(q, k, v, None, segt, None, segt, scale=dh ** -0.5)
+    gob = bf16_normal(rng, (b, n, h * grp, dh))
+    out.backward(bits_to_torch_bf16(gob, cuda))
+    torch.cuda.synchronize()
+    ro, P = oa.attention_forward(qb, kb, vb, seg, seg, None, None, dh ** -0.5)
+    compare(bf16_bits_to_f32(torch_bf16_to_bits(out)), bf16_bits_to_f32(ro))
+    dq, dk, dv = oa.attention_backward(gob, torch_bf16_to_bits(out), P, qb, kb, vb, dh ** -0.5)
+    for t, ref in ((q.grad, dq), (k.grad, dk), (v.grad, dv)):
+        compare(bf16_bits_to_f32(torch_bf16_to_bits(t)), ref)
+
+
 def test_attention_segments_isolate(cuda):
     """Changing the keys of one document leaves the other documents' outputs bit-identical."""
     import torch

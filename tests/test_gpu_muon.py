@@ -128,3 +128,36 @@ def test_orthogonalize_shapes_determinism_and_errors(cuda):
         muon.orthogonalize(torch.zeros(8, device=cuda))
     with pytest.raises(C.UFP8Error, match="multiples of 8"):
         muon.orthogonalize(torch.zeros((12, 64), device=cuda))
+
+
+@pytest.mark.parametrize("mask", [1, 2, 3])
+def test_bf16_gemm_tile_masks(cuda, mask):
+    """UFP8_TILES_LOWER computes exactly the 256 x 256 tiles on or below the diagonal (D elsewhere
+    untouched); K_TO_DIAG / K_FROM_DIAG contract M tile m over K < 256 (m + 1) / K >= 256 m of each
+    K slice (k_batches 2 here)."""
+    import torch
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200 import ops
+    M, N, K, kb = 640, 768 if mask == 1 else 128, 640, 1 if mask == 1 else 2
+    rng = np.random.default_rng(40 + mask)
+    a_bits = op.bf16_normal(rng, (kb, M, K))
+    b_bits = op.bf16_normal(rng, (kb, N, K))
+    at, bt = bits_to_torch_bf16(a_bits, cuda), bits_to_torch_bf16(b_bits, cuda)
+    d = torch.full((M, N), -7.0, dtype=torch.float32, device=cuda)
+    desc_kw = dict(k_batches=kb) if kb > 1 else {}
+    ops.gemm(ops.bf16_operand(at, C.K_MAJOR, K, M * K, kb), ops.bf16_operand(bt, C.K_MAJOR, K, N * K, kb),
+             M, N, K, d, N, tile_mask=mask, **desc_kw)
+    torch.cuda.synchronize()
+    a64, b64 = bf16_bits_to_f64(a_bits), bf16_bits_to_f64(b_bits)
+    ref = np.full((M, N), -7.0)
+    for mt in range((M + 255) // 256):
+        rows = slice(256 * mt, min(256 * mt + 256, M))
+        if mask == 1:
+            cols = slice(0, min(256 * mt + 256, N))
+            ref[rows, cols] = np.einsum("mk,nk->mn", a64[0, rows], b64[0, cols])
+        else:
+            ks = slice(0, 256 * (mt + 1)) if mask == 2 else slice(256 * mt, K)
+            ref[rows] = sum(a64[s, rows, ks] @ b64[s, :, ks].T for s in range(kb))
+    got = d.double().cpu().numpy()
+    np.testing.assert_array_equal(got == -7.0, ref == -7.0)
+    _cmp(got, ref, True)
