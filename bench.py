@@ -253,8 +253,11 @@ def gpu_arm_config(args, cfg, world):
     """The `config` dict both arms print for this workload and GPU count."""
     d, h, T = cfg["d"], cfg["h"], cfg["B"] * cfg["S"]
     if world > 1:
-        parallelism = (f"tp{world} (all-gather + reduce-scatter: NVLink P2P fused with the GEMMs, all-gather by "
-                       f"{'SM push kernel' if args.tp_ag == 'sm' else 'copy engines'})" if args.tp_rs == "p2p"
+        rs = {"auto": "y pushed from the GEMM epilogue, dx by copy engines beside dWf",
+              "epilogue": "pushed from the GEMM epilogues", "copy": "by copy engines"}[args.tp_rs_engine]
+        parallelism = (f"tp{world} (NVLink P2P; all-gather consumed block by block by the GEMMs, by "
+                       f"{'SM push kernel' if args.tp_ag == 'sm' else f'copy engines on {args.tp_lanes} lanes'}; "
+                       f"reduce-scatter {rs})" if args.tp_rs == "p2p"
                        else f"tp{world} (NCCL all-gather / reduce-scatter / all-reduce)")
     else:
         parallelism = "tp1"
@@ -460,6 +463,8 @@ def run_ours(args, cfg, rank, world, local_rank):
         from macrogpt_jax_b200 import tp as tp_mod
         from macrogpt_jax_b200.tp import TPGMLP
         tp_mod.AG_ENGINE = _capi.AG_SM if args.tp_ag == "sm" else _capi.AG_COPY_ENGINE
+        tp_mod.COPY_LANES = args.tp_lanes
+        tp_mod.RS_ENGINE = args.tp_rs_engine
         mlp = TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
                      fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5),
                      fused_reduce_scatter=args.tp_rs == "p2p")
@@ -1060,7 +1065,13 @@ def main():
     ap.add_argument("--tp-ag", choices=["sm", "ce"], default="ce",
                     help="P2P all-gather engine: an SM push kernel beside the GEMM, or copy engines")
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p",
-                    help="tensor-parallel reduce-scatter: fused into the GEMM epilogue over NVLink, or NCCL")
+                    help="tensor-parallel collectives: NVLink P2P (all-gather and reduce-scatter with the GEMMs), "
+                         "or NCCL")
+    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="auto",
+                    help="P2P reduce-scatter push: GEMM epilogue, copy engines beside independent work, or auto "
+                         "(epilogue for y, copy engines for dx)")
+    ap.add_argument("--tp-lanes", type=int, default=2, choices=range(1, 9),
+                    help="streams the copy-engine pushes spread their per-peer copies over")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

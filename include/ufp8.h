@@ -363,6 +363,21 @@ int ufp8_tp_local(ufp8_tp_ctx* ctx, uint64_t epoch, void** data, uint32_t** flag
 #define UFP8_AG_SM 1
 int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine, ufp8_stream_t stream);
 
+/* Copy lanes of a context (1..8, default 1): the copy-engine pushes (UFP8_AG_COPY_ENGINE and
+ * ufp8_tp_rs_push_copy) spread their per-peer copies round-robin over this many streams,
+ * forked from the caller's stream and joined back into it, so that several copy engines move
+ * blocks at once; the flag of each all-gather block still follows its own copy. */
+int ufp8_tp_set_copy_lanes(ufp8_tp_ctx* ctx, int lanes);
+
+/* Reduce-scatter push by copy engines (the alternative to the UFP8_EPI_RS_PUSH epilogue when
+ * independent work can run while the blocks travel): src holds this rank's partial sums,
+ * k * rows rows of `cols` bf16 at pitch ld_src; block p (rows p*rows .. ) goes into slot
+ * [rank] of rank p's buffer of `epoch` (from ufp8_tp_begin) at pitch cols, this rank's own
+ * block included.  The copies are ordered before later work on `stream`; ufp8_tp_finish on
+ * that stream (ld_slot = cols) then signals the peers and sums as after the epilogue push. */
+int ufp8_tp_rs_push_copy(ufp8_tp_ctx* ctx, uint64_t epoch, const void* src, int64_t ld_src, int64_t rows,
+                         int64_t cols, ufp8_stream_t stream);
+
 /* MAX all-reduce of n (1..8) non-negative f32 values (per-tensor amax values) over the group
  * of a connected context: every rank's `out` receives the elementwise maximum of all ranks'
  * `in` (NaN propagates).  One single-warp kernel: P2P stores with a system-scope release into

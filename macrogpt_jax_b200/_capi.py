@@ -47,6 +47,8 @@ EXPORTED_SYMBOLS = (
     "ufp8_tp_allreduce_max",
     "ufp8_tp_local",
     "ufp8_tp_ag_push",
+    "ufp8_tp_set_copy_lanes",
+    "ufp8_tp_rs_push_copy",
     "ufp8_amax_quant_noalloc",
     "ufp8_rmsnorm_quant",
     "ufp8_rmsnorm_backward_workspace",
@@ -180,6 +182,8 @@ def load() -> ctypes.CDLL:
     lib.ufp8_tp_allreduce_max.argtypes = [vp, vp, vp, i32, vp]
     lib.ufp8_tp_local.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp), ctypes.POINTER(vp)]
     lib.ufp8_tp_ag_push.argtypes = [vp, ctypes.c_uint64, i64, i32, vp]
+    lib.ufp8_tp_set_copy_lanes.argtypes = [vp, i32]
+    lib.ufp8_tp_rs_push_copy.argtypes = [vp, ctypes.c_uint64, vp, i64, i64, i64, vp]
     f32 = ctypes.c_float
     lib.ufp8_rmsnorm_quant.argtypes = [vp, i64, i64, i64, vp, i64, i32, f32, i32, vp, vp, vp, vp, vp, i64, vp]
     lib.ufp8_rmsnorm_backward_workspace.argtypes = [i64, i64, ctypes.POINTER(i64)]
@@ -199,7 +203,8 @@ def load() -> ctypes.CDLL:
                  "ufp8_set_gemm_ctas", "ufp8_set_gemm_variant", "ufp8_set_gemm_raster", "ufp8_tp_create",
                  "ufp8_tp_connect", "ufp8_tp_connect_local", "ufp8_tp_destroy", "ufp8_tp_set_timeout_ms", "ufp8_tp_slot_bytes", "ufp8_tp_begin",
                  "ufp8_tp_finish", "ufp8_tp_allreduce_max", "ufp8_amax_quant_noalloc",
-                 "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
+                 "ufp8_tp_local", "ufp8_tp_ag_push", "ufp8_tp_set_copy_lanes", "ufp8_tp_rs_push_copy",
+                 "ufp8_rmsnorm_quant", "ufp8_rmsnorm_backward_workspace",
                  "ufp8_rmsnorm_backward", "ufp8_xent_forward", "ufp8_xent_combine", "ufp8_xent_backward",
                  "ufp8_newton_schulz_workspace", "ufp8_newton_schulz", "ufp8_rope_table", "ufp8_rope",
                  "ufp8_attention_workspace", "ufp8_attention_forward", "ufp8_attention_backward"):
@@ -400,6 +405,15 @@ class TPReduceScatter:
         AG_COPY_ENGINE: copy engines), each followed by the arrival flag."""
         check(load().ufp8_tp_ag_push(self.ctx, epoch, nbytes, engine, stream))
         _count(1 if engine == AG_SM and self.world > 1 else 0)
+
+    def set_copy_lanes(self, lanes: int) -> None:
+        """Streams (1..8) over which the copy-engine pushes spread their per-peer copies."""
+        check(load().ufp8_tp_set_copy_lanes(self.ctx, lanes))
+
+    def rs_push_copy(self, epoch: int, src_ptr: int, ld_src: int, rows: int, cols: int, stream: int) -> None:
+        """Copy-engine reduce-scatter push: block p of the k * rows partial rows (bf16, pitch
+        ld_src) into slot [rank] of rank p's buffer of `epoch`; finish with ld_slot = cols."""
+        check(load().ufp8_tp_rs_push_copy(self.ctx, epoch, src_ptr, ld_src, rows, cols, stream))
 
     def allreduce_max(self, in_ptr: int, out_ptr: int, n: int, stream: int) -> None:
         """Elementwise MAX over the group of n (1..8) non-negative device f32 values."""

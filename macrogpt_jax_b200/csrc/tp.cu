@@ -18,6 +18,7 @@
 // each copy; the consuming GEMM waits per row block (ufp8_gemm_desc.ag_*).
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -47,6 +48,12 @@ struct TPContext {
   uint64_t epoch = 0;
   uint64_t ex_epoch = 0;          // small-value exchanges issued
   int timeout_ms = 5000;
+  // Copy lanes: the copy-engine pushes spread their per-peer copies over `lanes` streams
+  // (forked from and joined back into the caller's stream), created on first use.
+  int lanes = 1;
+  cudaStream_t lane_stream[kMaxRanks] = {};
+  cudaEvent_t fork_event = nullptr;
+  cudaEvent_t lane_event[kMaxRanks] = {};
   char* ex_region(int p) const { return peer_base[p] + 2 * buffer_bytes; }
 };
 
@@ -65,6 +72,48 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Forks the copy lanes from `s`: every lane stream waits for the work issued on `s` so far.
+// With one lane the caller's stream is the lane.  Returns 0 or a UFP8 error code.
+int lanes_fork(TPContext* c, cudaStream_t s, int n) {
+  if (n <= 1) {
+    c->lane_stream[0] = nullptr;
+    return UFP8_OK;
+  }
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "copy lanes: cudaGetDevice");
+  if (dev != c->device) return set_error(UFP8_ERR_INVALID, "copy lanes: current device %d, context on %d", dev, c->device);
+  if (!c->fork_event && (e = cudaEventCreateWithFlags(&c->fork_event, cudaEventDisableTiming)) != cudaSuccess)
+    return cuda_error(e, "copy lanes: event");
+  for (int l = 0; l < n; ++l) {
+    if (!c->lane_stream[l] && (e = cudaStreamCreateWithFlags(&c->lane_stream[l], cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_error(e, "copy lanes: stream");
+    if (!c->lane_event[l] && (e = cudaEventCreateWithFlags(&c->lane_event[l], cudaEventDisableTiming)) != cudaSuccess)
+      return cuda_error(e, "copy lanes: event");
+  }
+  if ((e = cudaEventRecord(c->fork_event, s)) != cudaSuccess) return cuda_error(e, "copy lanes: fork record");
+  for (int l = 0; l < n; ++l)
+    if ((e = cudaStreamWaitEvent(c->lane_stream[l], c->fork_event, 0)) != cudaSuccess)
+      return cuda_error(e, "copy lanes: fork wait");
+  return UFP8_OK;
+}
+
+cudaStream_t lane_of(const TPContext* c, cudaStream_t s, int n, int i) {
+  return n <= 1 ? s : c->lane_stream[i % n];
+}
+
+// Joins the lanes back into `s`: work issued on `s` afterwards waits for every lane's copies.
+int lanes_join(TPContext* c, cudaStream_t s, int n) {
+  if (n <= 1) return UFP8_OK;
+  cudaError_t e;
+  for (int l = 0; l < n; ++l) {
+    if ((e = cudaEventRecord(c->lane_event[l], c->lane_stream[l])) != cudaSuccess)
+      return cuda_error(e, "copy lanes: join record");
+    if ((e = cudaStreamWaitEvent(s, c->lane_event[l], 0)) != cudaSuccess) return cuda_error(e, "copy lanes: join wait");
+  }
+  return UFP8_OK;
 }
 
 struct FinishArgs {
@@ -344,6 +393,11 @@ int ufp8_tp_connect_local(ufp8_tp_ctx* ctx, ufp8_tp_ctx* const* peers) {
 int ufp8_tp_destroy(ufp8_tp_ctx* ctx) {
   TPContext* c = reinterpret_cast<TPContext*>(ctx);
   if (!c) return UFP8_OK;
+  for (int l = 0; l < kMaxRanks; ++l) {
+    if (c->lane_stream[l]) cudaStreamDestroy(c->lane_stream[l]);
+    if (c->lane_event[l]) cudaEventDestroy(c->lane_event[l]);
+  }
+  if (c->fork_event) cudaEventDestroy(c->fork_event);
   for (int p = 0; p < kMaxRanks; ++p)
     if (c->peer_opened[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
   if (c->d_slot_ptrs) cudaFree(c->d_slot_ptrs);
@@ -501,9 +555,12 @@ int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine,
   if (!write_value) return set_error(UFP8_ERR_CUDA, "cuStreamWriteValue32 is unavailable from the driver");
   const size_t off = (epoch & 1) * c->buffer_bytes;
   const char* src = c->base + off + kFlagBytes + c->rank * c->slot_bytes;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaStream_t s0 = reinterpret_cast<cudaStream_t>(stream);
+  const int nl = c->world > 1 ? std::min(c->lanes, c->world - 1) : 1;
+  if (int rc = lanes_fork(c, s0, nl)) return rc;
   for (int i = 1; i < c->world; ++i) {
     const int p = (c->rank - i + c->world) % c->world;
+    cudaStream_t s = lane_of(c, s0, nl, i - 1);
     char* dst = c->peer_base[p] + off + kFlagBytes + c->rank * c->slot_bytes;
     if (bytes > 0) {
       cudaError_t e = cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToDevice, s);
@@ -514,7 +571,48 @@ int ufp8_tp_ag_push(ufp8_tp_ctx* ctx, uint64_t epoch, int64_t bytes, int engine,
                              CU_STREAM_WRITE_VALUE_DEFAULT);
     if (r != CUDA_SUCCESS) return set_error(UFP8_ERR_CUDA, "ufp8_tp_ag_push: cuStreamWriteValue32 (CUresult %d)", r);
   }
+  return lanes_join(c, s0, nl);
+}
+
+int ufp8_tp_set_copy_lanes(ufp8_tp_ctx* ctx, int lanes) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || lanes < 1 || lanes > kMaxRanks) return set_error(UFP8_ERR_INVALID, "ufp8_tp_set_copy_lanes: bad argument");
+  c->lanes = lanes;
   return UFP8_OK;
+}
+
+int ufp8_tp_rs_push_copy(ufp8_tp_ctx* ctx, uint64_t epoch, const void* src, int64_t ld_src, int64_t rows,
+                         int64_t cols, ufp8_stream_t stream) {
+  TPContext* c = reinterpret_cast<TPContext*>(ctx);
+  if (!c || (!src && rows > 0)) return set_error(UFP8_ERR_INVALID, "ufp8_tp_rs_push_copy: null pointer");
+  if (epoch == 0 || epoch > c->epoch) return set_error(UFP8_ERR_INVALID, "ufp8_tp_rs_push_copy: epoch not begun");
+  if (rows < 0 || cols <= 0 || ld_src < cols)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_rs_push_copy: bad extents");
+  if (static_cast<size_t>(rows * cols * 2) > c->slot_bytes)
+    return set_error(UFP8_ERR_INVALID, "ufp8_tp_rs_push_copy: %lld x %lld rows exceed the staging slot",
+                     static_cast<long long>(rows), static_cast<long long>(cols));
+  if (reinterpret_cast<uintptr_t>(src) & 1u) return set_error(UFP8_ERR_ALIGN, "ufp8_tp_rs_push_copy: src not 2-byte aligned");
+  for (int p = 0; p < c->world; ++p)
+    if (!c->peer_base[p]) return set_error(UFP8_ERR_INVALID, "ufp8_tp_rs_push_copy: rank %d is not connected", p);
+  if (rows == 0) return UFP8_OK;
+  const size_t off = (epoch & 1) * c->buffer_bytes;
+  cudaStream_t s0 = reinterpret_cast<cudaStream_t>(stream);
+  const int nl = std::min(c->lanes, c->world);
+  if (int rc = lanes_fork(c, s0, nl)) return rc;
+  const size_t row_bytes = static_cast<size_t>(cols) * 2, pitch = static_cast<size_t>(ld_src) * 2;
+  for (int i = 0; i < c->world; ++i) {  // own block first, then rank+1, rank+2, ... (mod k)
+    const int p = (c->rank + i) % c->world;
+    cudaStream_t s = lane_of(c, s0, nl, i);
+    char* dst = c->peer_base[p] + off + kFlagBytes + c->rank * c->slot_bytes;
+    const char* blk = static_cast<const char*>(src) + static_cast<size_t>(p) * rows * pitch;
+    const cudaError_t e =
+        pitch == row_bytes
+            ? cudaMemcpyAsync(dst, blk, row_bytes * rows, cudaMemcpyDeviceToDevice, s)
+            : cudaMemcpy2DAsync(dst, row_bytes, blk, pitch, row_bytes, static_cast<size_t>(rows),
+                                cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_error(e, "ufp8_tp_rs_push_copy: peer copy");
+  }
+  return lanes_join(c, s0, nl);
 }
 
 int ufp8_tp_slot_bytes(const ufp8_tp_ctx* ctx, int64_t* out) {

@@ -43,6 +43,17 @@ from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 # ~225 KiB of shared memory each) needs, so the GEMM starts only when the push ends.
 AG_ENGINE = C.AG_COPY_ENGINE
 
+# Streams over which the copy-engine pushes spread their per-peer copies (ufp8_tp_set_copy_lanes):
+# one copy engine moves a block at well under the link rate, so several run at once.
+COPY_LANES = 2
+
+# How each reduce-scatter's partial rows reach their owners: "epilogue" (the GEMM epilogue
+# stores them into the peers' slots, UFP8_EPI_RS_PUSH), "copy" (the GEMM stores locally and
+# copy engines push the blocks, ufp8_tp_rs_push_copy, while independent work runs), or "auto":
+# the epilogue push for y (nothing in the forward can run beside it) and copy engines for dx
+# (dWf = x^T dUG runs while the blocks travel).
+RS_ENGINE = "auto"
+
 
 def tensor_group(mesh):
     """The process group of the 'tensor' axis of `mesh` (ueaj/model/mlp.py:85,96 and
@@ -141,6 +152,38 @@ class TPContext:
             self._rs = self._connect(slot_bytes)
         return self._rs
 
+    def _side_stream(self, device) -> torch.cuda.Stream:
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=device)
+        return self._side
+
+    def copy_reduce_scatter(self, partial: torch.Tensor, between=None):
+        """partial [T, d] bf16 (this rank's partial sums): copy engines push block p to rank p on
+        the side stream while `between()` (independent work) runs on the current stream, then the
+        finish sums; returns (this rank's summed block [T / k, d], between's result)."""
+        T, d = partial.shape
+        rl = T // self.world
+        rs = self._rs_ctx(((rl * d * 2 + 255) // 256) * 256)
+        _, epoch = rs.begin()
+        main = torch.cuda.current_stream()
+        side = self._side_stream(partial.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        side.wait_event(ready)
+        rs.rs_push_copy(epoch, partial.data_ptr(), partial.stride(0), rl, d, side.cuda_stream)
+        partial.record_stream(side)
+        done = torch.cuda.Event()
+        done.record(side)
+        mid = between() if between is not None else None
+        main.wait_event(done)
+        out = torch.empty((rl, d), dtype=partial.dtype, device=partial.device)
+        rs.finish(epoch, rl, d, d, out.data_ptr(), d, main.cuda_stream)
+        return out, mid
+
+    def rs_by_copy(self, role: str) -> bool:
+        """Whether the reduce-scatter of `role` ("y" or "dx") goes by copy engines (RS_ENGINE)."""
+        return RS_ENGINE == "copy" or (RS_ENGINE == "auto" and role == "dx")
+
     def push_reduce_scatter(self, push, rows: int, cols: int, dtype, device, between=None):
         """Runs `push(slot_table, rank, rows_per_rank)` (a GEMM with the RS_PUSH epilogue over
         all `rows`), then `between()` if given (independent work that runs while the peers'
@@ -168,6 +211,7 @@ class TPContext:
         handles = [None] * self.world
         dist.all_gather_object(handles, ctx.handle, group=self.group)
         ctx.connect(handles)
+        ctx.set_copy_lanes(COPY_LANES)
         return ctx
 
     def gather_tokens_p2p(self, role: str, x: torch.Tensor, fmt: int, amax_t: torch.Tensor):
@@ -191,8 +235,7 @@ class TPContext:
         full = _device_bytes(data, (rl * self.world, d), x.device).view(cuda_ops.FP8_DTYPE[fmt])
         q = self.be.quantize(x, fmt, amax_t, out=full[self.rank * rl:(self.rank + 1) * rl])
         main = torch.cuda.current_stream()
-        if self._side is None:
-            self._side = torch.cuda.Stream(device=x.device)
+        self._side_stream(x.device)
         ready = torch.cuda.Event()
         ready.record(main)
         self._side.wait_event(ready)
@@ -273,7 +316,9 @@ class _TPGMLPFn(torch.autograd.Function):
             ug, hid, amax_h = be.gmlp_f1(qx, qwf)
         amax_h = tp.allreduce_max_(amax_h)
         qh = be.quantize(hid, C.E4M3, amax_h)
-        if tp.fused_rs:
+        if tp.fused_rs and tp.rs_by_copy("y"):
+            y, _ = tp.copy_reduce_scatter(be.gmlp_f2(qh, qwd))
+        elif tp.fused_rs:
             T, d = qh.q.shape[0], qwd.q.shape[1]
             y, _ = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_f2_push(qh, qwd, tab, r, rl), T, d,
                                           torch.bfloat16, qh.q.device)
@@ -307,7 +352,9 @@ class _TPGMLPFn(torch.autograd.Function):
         amax_dug = tp.allreduce_max_(amax_dug)
         dwd = be.gmlp_b1(qh, qdy)
         qdug = be.quantize(dug, C.E5M2, amax_dug)
-        if tp.fused_rs:
+        if tp.fused_rs and tp.rs_by_copy("dx"):
+            dx, dwf = tp.copy_reduce_scatter(be.gmlp_b4(qdug, qwf), between=lambda: be.gmlp_b3(qx, qdug))
+        elif tp.fused_rs:
             T, d = qdug.q.shape[1], qwf.q.shape[1]
             dx, dwf = tp.push_reduce_scatter(lambda tab, r, rl: be.gmlp_b4_push(qdug, qwf, tab, r, rl), T, d,
                                              torch.bfloat16, qdug.q.device, between=lambda: be.gmlp_b3(qx, qdug))

@@ -1,7 +1,8 @@
 """Kernel timeline of one tensor-parallel GMLP step on every GPU of a node (torch.profiler).
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \\
-        -m macrogpt_jax_b200.tp_timeline [--tp-rs p2p|nccl] [--tp-ag ce|sm] [--out DIR]
+        -m macrogpt_jax_b200.tp_timeline [--tp-rs p2p|nccl] [--tp-ag ce|sm] [--tp-lanes N]
+        [--tp-rs-engine auto|epilogue|copy] [--out DIR]
 
 Builds the TPGMLP of the tensor-parallel bench workload (16384 tokens, d_model 4096, hidden
 14336), runs 5 untimed steps, then records 3 steps with torch.profiler (CUDA activity only) and
@@ -23,6 +24,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--tp-ag", choices=["ce", "sm"], default="ce")
+    ap.add_argument("--tp-lanes", type=int, default=2)
+    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="auto")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--hidden", type=int, default=14336)
@@ -41,6 +44,8 @@ def main() -> None:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     try:
         tp_mod.AG_ENGINE = C.AG_COPY_ENGINE if args.tp_ag == "ce" else C.AG_SM
+        tp_mod.COPY_LANES = args.tp_lanes
+        tp_mod.RS_ENGINE = args.tp_rs_engine
         d, h, T = args.d, args.hidden, args.tokens
         mlp = tp_mod.TPGMLP(model_d=d, hidden_d=h, rngs=Rngs(0), device=dev,
                             fused_init=scaled_normal_init(d ** -0.5), down_init=scaled_normal_init(h ** -0.5),
@@ -71,7 +76,7 @@ def main() -> None:
                          key=lambda e: e.time_range.start)
             t0 = evs[0].time_range.start if evs else 0.0
             os.makedirs(args.out, exist_ok=True)
-            path = os.path.join(args.out, f"timeline_tp{world}_{args.tp_rs}_{args.tp_ag}_rank{rank}.txt")
+            path = os.path.join(args.out, f"timeline_tp{world}_{args.tp_rs}_{args.tp_ag}{args.tp_lanes}_{args.tp_rs_engine}_rank{rank}.txt")
             with open(path, "w") as f:
                 for e in evs:
                     f.write(f"{e.time_range.start - t0:10.1f} {e.time_range.elapsed_us():8.1f} "

@@ -21,7 +21,7 @@ def _port() -> int:
     return p
 
 
-def _worker(rank, world, port, outdir, fused=True, ag_engine=1):
+def _worker(rank, world, port, outdir, fused=True, ag_engine=1, rs_engine="auto", lanes=2):
     import sys
     import torch.distributed as dist
     sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
@@ -34,6 +34,8 @@ def _worker(rank, world, port, outdir, fused=True, ag_engine=1):
         from macrogpt_jax_b200.einsum import Rngs, scaled_normal_init
         from macrogpt_jax_b200.tp import TPGMLP
         tp_mod.AG_ENGINE = ag_engine
+        tp_mod.RS_ENGINE = rs_engine
+        tp_mod.COPY_LANES = lanes
         from oracle import path as op
         dev = torch.device("cuda", rank)
         m = TPGMLP(D, H, rngs=Rngs(7), device=dev, fused_init=scaled_normal_init(D ** -0.5),
@@ -66,9 +68,13 @@ def _worker(rank, world, port, outdir, fused=True, ag_engine=1):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("fused,ag_engine", [(True, 1), (True, 0), (False, 1)],
-                         ids=["p2p_sm_push", "p2p_copy_engine", "nccl"])
-def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused, ag_engine):
+@pytest.mark.parametrize("fused,ag_engine,rs_engine,lanes",
+                         [(True, 1, "epilogue", 1), (True, 0, "epilogue", 1), (True, 0, "auto", 2),
+                          (True, 0, "copy", 3), (False, 1, "auto", 2)],
+                         ids=["p2p_sm_push", "p2p_copy_engine", "p2p_auto_2lanes", "p2p_copy_rs_3lanes", "nccl"])
+def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused, ag_engine, rs_engine, lanes):
+    """All-gather by SM push kernel or copy engines (1..3 lanes), reduce-scatter pushed from the
+    GEMM epilogue, by copy engines, or auto (epilogue for y, copy engines beside dWf for dx)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -77,7 +83,7 @@ def test_tp2_gpu_matches_oracle(cuda, tmp_path, fused, ag_engine):
     from macrogpt_jax_b200.mlp import GMLP
     from oracle import path as op
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.spawn(_worker, args=(2, _port(), str(tmp_path), fused, ag_engine), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _port(), str(tmp_path), fused, ag_engine, rs_engine, lanes), nprocs=2, join=True)
     r = [np.load(tmp_path / f"rank{i}.npz") for i in range(2)]
     cpu = torch.device("cpu")
     full = GMLP.override(fused_proj=Einsum.override(initializer=scaled_normal_init(D ** -0.5), device=cpu),
