@@ -163,9 +163,11 @@ def gemm_plan(input_expr: str, weight_expr: str, output_expr: str, batch_dims: s
 
 class _FP8EinsumFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, plan, fwd_fmt, bwd_fmt, static_scale):
-        out, saved = ops.einsum_forward(plan, x, w, fwd_fmt, static_scale)
+    def forward(ctx, x, w, plan, fwd_fmt, bwd_fmt, static_scale, global_amax=None):
+        fn, operands = global_amax if global_amax is not None else (None, ())
+        out, saved = ops.einsum_forward(plan, x, w, fwd_fmt, static_scale, fn, operands)
         ctx.plan, ctx.bwd_fmt, ctx.static_scale, ctx.saved = plan, bwd_fmt, static_scale, saved
+        ctx.global_amax = (fn, operands)
         ctx.x_shape, ctx.w_shape = x.shape, w.shape
         return out
 
@@ -173,10 +175,10 @@ class _FP8EinsumFn(torch.autograd.Function):
     def backward(ctx, dout):
         need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
         dx, dw = ops.einsum_backward(ctx.plan, dout.to(torch.bfloat16).contiguous(), ctx.saved, ctx.bwd_fmt,
-                                     need_dx, need_dw, ctx.static_scale)
+                                     need_dx, need_dw, ctx.static_scale, *ctx.global_amax)
         ctx.saved = None
         return (dx.reshape(ctx.x_shape) if dx is not None else None,
-                dw.reshape(ctx.w_shape) if dw is not None else None, None, None, None, None)
+                dw.reshape(ctx.w_shape) if dw is not None else None, None, None, None, None, None)
 
 
 @config
@@ -209,6 +211,10 @@ class Einsum(torch.nn.Module):
         self.sharding = sharding
         self.mesh = mesh
         self.shard = None  # (canonical dim, rank, ranks) once reshard() has sliced the weight
+        # (amax_fn, operands): operands ("x", "w", "dout") quantised with amax_fn(t) instead of
+        # their local amax; a tensor-parallel block sets it so that shards take the whole
+        # logical tensor's scale (a MAX over the group).
+        self.global_amax = None
         if fwd_dtype not in ops.FMT_OF_DTYPE or bwd_dtype not in ops.FMT_OF_DTYPE:
             raise ValueError("fwd_dtype / bwd_dtype must be float8_e4m3fn or float8_e5m2")
         self.fwd_dtype, self.bwd_dtype = fwd_dtype, bwd_dtype
@@ -236,7 +242,7 @@ class Einsum(torch.nn.Module):
         if x.dtype != torch.bfloat16:
             x = x.to(torch.bfloat16)
         return _FP8EinsumFn.apply(x, w, self.plan(x.shape), ops.FMT_OF_DTYPE[self.fwd_dtype],
-                                  ops.FMT_OF_DTYPE[self.bwd_dtype], self.static_scale)
+                                  ops.FMT_OF_DTYPE[self.bwd_dtype], self.static_scale, self.global_amax)
 
     def get_einsum_metadata(self) -> Dict[str, EinsumMetadata]:
         return {"w": self.metadata}

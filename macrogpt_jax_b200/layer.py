@@ -51,7 +51,7 @@ class _NormGMLPFn(torch.autograd.Function):
 
 def norm_fusable(norm, mlp) -> bool:
     """True when mlp(norm(x)) can run as the fused RMSNorm -> FP8 GMLP node."""
-    return isinstance(norm, RMSNorm) and isinstance(mlp, GMLP) and mlp.fused() and \
+    return isinstance(norm, RMSNorm) and isinstance(mlp, GMLP) and mlp._tp is None and mlp.fused() and \
         (norm.scale is None or norm.scale.dtype == torch.bfloat16)
 
 

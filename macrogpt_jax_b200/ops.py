@@ -171,14 +171,18 @@ class EinsumPlan:
 
 
 def einsum_forward(plan: EinsumPlan, x: torch.Tensor, w: torch.Tensor, fwd_fmt: int,
-                   alpha: float | None = None):
-    """Forward of ueaj.model.Einsum (ueaj/model/einsum.py:233-251) in FP8."""
+                   alpha: float | None = None, amax_fn=None, amax_operands=()):
+    """Forward of ueaj.model.Einsum (ueaj/model/einsum.py:233-251) in FP8.  `amax_fn(t)` gives
+    the amax of the operands named in `amax_operands` ("x", "w"): under tensor parallelism the
+    MAX over the group, so that a shard is quantised with the whole logical tensor's scale."""
     G, K, N = plan.G, plan.K, plan.N
     M = 1
     for s in plan.M_shape:
         M *= s
-    qx = quantize(x.reshape(M, K), fwd_fmt)
-    qw = quantize(w.reshape(G, K, N), fwd_fmt)
+    x2 = x.reshape(M, K)
+    w3 = w.reshape(G, K, N)
+    qx = quantize(x2, fwd_fmt, amax_fn(x2) if "x" in amax_operands else None)
+    qw = quantize(w3, fwd_fmt, amax_fn(w3) if "w" in amax_operands else None)
     out = torch.empty((G, M, N), dtype=torch.bfloat16, device=x.device)
     inv_b = qw.inv_scale if alpha is None else qw.inv_scale * alpha
     gemm(operand(qx, C.K_MAJOR, K), operand(qw, C.MN_MAJOR, N, K * N, G, inv_scale=inv_b),
@@ -187,12 +191,14 @@ def einsum_forward(plan: EinsumPlan, x: torch.Tensor, w: torch.Tensor, fwd_fmt: 
 
 
 def einsum_backward(plan: EinsumPlan, dout: torch.Tensor, saved, bwd_fmt: int, need_dx: bool, need_dw: bool,
-                    alpha: float | None = None):
-    """dX = dOut W^T (summed over weight batch slices) and dW = X^T dOut."""
+                    alpha: float | None = None, amax_fn=None, amax_operands=()):
+    """dX = dOut W^T (summed over weight batch slices) and dW = X^T dOut; `amax_fn` as in
+    einsum_forward, for "dout"."""
     qx, qw = saved
     G, K, N = plan.G, plan.K, plan.N
     M = qx.q.shape[0]
-    qd = quantize(dout.reshape(G * M, N), bwd_fmt)
+    d2 = dout.reshape(G * M, N)
+    qd = quantize(d2, bwd_fmt, amax_fn(d2) if "dout" in amax_operands else None)
     dx = dw = None
     if need_dx:
         dx = torch.empty((M, K), dtype=torch.bfloat16, device=dout.device)

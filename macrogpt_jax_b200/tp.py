@@ -289,6 +289,62 @@ class TPContext:
         return out
 
 
+    def all_gather_rows(self, x: torch.Tensor) -> torch.Tensor:
+        """[rows, ...] on every rank -> [k * rows, ...] in rank order (NCCL / gloo all-gather)."""
+        x = x.contiguous()
+        full = torch.empty((x.shape[0] * self.world,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(full, x, group=self.group)
+        return full
+
+    def reduce_scatter_rows(self, partial: torch.Tensor) -> torch.Tensor:
+        """[k * rows, ...] partial sums on every rank -> this rank's summed block [rows, ...]:
+        with the NVLink path bf16 blocks go by copy engines into the peers' staging slots and the
+        finish kernel sums them in fp32 in rank order; otherwise NCCL / gloo."""
+        if self.fused_rs and partial.dtype == torch.bfloat16 and partial.is_cuda:
+            lead, rest = partial.shape[0], tuple(partial.shape[1:])
+            flat = partial.reshape(lead, -1).contiguous()
+            if flat.shape[1] % 2 == 0:
+                out, _ = self.copy_reduce_scatter(flat)
+                return out.reshape((lead // self.world,) + rest)
+        return self.reduce_scatter_tokens(partial)
+
+
+class _GatherRowsFn(torch.autograd.Function):
+    """All-gather over the group along dim 0; its gradient is the reduce-scatter."""
+
+    @staticmethod
+    def forward(ctx, x, tp):
+        ctx.tp = tp
+        return tp.all_gather_rows(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.reduce_scatter_rows(g.contiguous()), None
+
+
+class _ScatterRowsFn(torch.autograd.Function):
+    """Reduce-scatter over the group along dim 0; its gradient is the all-gather."""
+
+    @staticmethod
+    def forward(ctx, partial, tp):
+        ctx.tp = tp
+        return tp.reduce_scatter_rows(partial)
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.tp.all_gather_rows(g.contiguous()), None
+
+
+def gather_rows(x: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """Differentiable all-gather of the ranks' dim-0 blocks (token shards) in rank order."""
+    return _GatherRowsFn.apply(x, tp)
+
+
+def scatter_rows(partial: torch.Tensor, tp: TPContext) -> torch.Tensor:
+    """Differentiable reduce-scatter: sums the ranks' partials and keeps this rank's dim-0 block."""
+    return _ScatterRowsFn.apply(partial, tp)
+
+
 class _TPGMLPFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, wf, wd, tp: TPContext):

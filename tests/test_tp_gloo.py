@@ -173,3 +173,38 @@ def test_gmlp_with_mesh_is_tensor_parallel(tmp_path):
     # reshard: each rank holds its contiguous column block of the same full weight
     assert (r[0]["e_full"] == r[1]["e_full"]).all()
     assert (np.concatenate([r[0]["e_local"], r[1]["e_local"]], axis=1) == r[0]["e_full"]).all()
+
+
+def _rows_worker(rank, world, port, outdir):
+    """gather_rows / scatter_rows (the token all-gather and reduce-scatter the tensor-parallel
+    attention wraps around its local heads) and their gradients, on CPU ranks."""
+    import sys
+    sys.path.insert(0, os.path.dirname(__file__))
+    sys.path.insert(0, os.path.dirname(os.path.dirname(__file__)))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    from cpu_backend import CpuBackend
+    from macrogpt_jax_b200.tp import TPContext, gather_rows, scatter_rows
+    tp = TPContext(backend=CpuBackend())
+    assert not tp.fused_rs
+    gen = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn((3, 2, 5), generator=gen, dtype=torch.float64).requires_grad_(True)
+    c = float(rank + 2)
+    full = gather_rows(x, tp)
+    y = scatter_rows(full * c, tp)
+    g = torch.randn(y.shape, generator=gen, dtype=torch.float64)
+    y.backward(g)
+    np.savez(os.path.join(outdir, f"rows{rank}.npz"), x=x.detach().numpy(), full=full.detach().numpy(),
+             y=y.detach().numpy(), g=g.numpy(), dx=x.grad.numpy())
+    dist.destroy_process_group()
+
+
+def test_gather_scatter_rows_autograd(tmp_path):
+    """y_r = block r of sum_s c_s * cat(x) = (c_0 + c_1) x_r, and dx_r = (c_0 + c_1) g_r."""
+    mp.spawn(_rows_worker, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+    r = [np.load(tmp_path / f"rows{i}.npz") for i in range(2)]
+    cat = np.concatenate([r[0]["x"], r[1]["x"]])
+    for i in range(2):
+        np.testing.assert_array_equal(r[i]["full"], cat)
+        np.testing.assert_allclose(r[i]["y"], 5.0 * r[i]["x"], rtol=1e-12)
+        np.testing.assert_allclose(r[i]["dx"], 5.0 * r[i]["g"], rtol=1e-12)
