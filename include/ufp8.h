@@ -41,7 +41,7 @@ extern "C" {
 
 typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 
-#define UFP8_ABI_VERSION 4
+#define UFP8_ABI_VERSION 5
 
 /* return codes */
 #define UFP8_OK 0
@@ -76,6 +76,10 @@ typedef struct CUstream_st* ufp8_stream_t; /* same handle as cudaStream_t */
 #define UFP8_EPI_RS_PUSH 3 /* D rows stored into their owner rank's reduce-scatter staging slot */
 #define UFP8_EPI_XENT 4    /* D = logits (bf16, optionally soft-capped) + per-row softmax partials  */
 #define UFP8_EPI_AXPBY 5   /* D = alpha * acc * sa * sb + beta * C (bf16 operands only)            */
+/* Attention products with the default positions (bf16 operands; see the attn_* fields): */
+#define UFP8_EPI_ATTN_STATS 6 /* scores: per-row softmax partials of scale * acc, nothing stored  */
+#define UFP8_EPI_ATTN_P 7     /* scores: D = bf16(exp(scale * acc - lse[row])), masked -> 0       */
+#define UFP8_EPI_ATTN_DS 8    /* dP: D = bf16(scale * P (acc - attn_row[row])), P read from `c`  */
 
 /* tile masks of a bf16 GEMM (ufp8_gemm_desc.tile_mask; tiles are 256 x 256): causal attention's
  * products skip what its mask zeroes */
@@ -160,7 +164,9 @@ typedef struct ufp8_operand {
   int64_t ld;
   int64_t batch_stride;
   int32_t batch_count;    /* slices present in memory (1 = broadcast over the GEMM batch) */
-  int32_t reserved;
+  int32_t batch_group;    /* > 1: GEMM batch g reads slice g / batch_group (a slice shared by
+                             batch_group consecutive products, e.g. one key head for its group of
+                             query heads); 0 or 1: slice g.  Needs k_batches == 1, not SWIGLU. */
   const float* inv_scale; /* device f32: 1/s of this operand */
 } ufp8_operand;
 
@@ -226,6 +232,23 @@ typedef struct ufp8_gemm_desc {
   float beta;
   int32_t tile_mask; /* UFP8_TILES_* (bf16 operands only) */
   int32_t reserved2;
+  /* UFP8_EPI_ATTN_*: batch entry g, row r (query), column c (key) of the score matrix
+   * scale * (A_g B_g^T)[r, c] is visible iff c <= r and both carry the same non-negative segment
+   * id (attn_q_segment_ids[r], attn_kv_segment_ids[c]; NULL: all 0).
+   *   STATS: (m, s) = (max, sum exp(x - m)) of the visible x of each group j of 128 columns as two
+   *          f32 at attn_stats + 2 * ((g * M + r) * attn_ld_stats + j) (m = -inf, s = 0 when none
+   *          is visible); D is not written (may be NULL).
+   *   P:     D = bf16(exp(x - attn_row[g * M + r])) where visible, else 0 (attn_row = lse).
+   *   DS:    D = bf16(scale * (P * (acc - attn_row[g * M + r]))), each step rounded in f32, with
+   *          P the bf16 matrix `c` (pitch ldc, slice pitch c_batch_stride; attn_row = rowsum(dO O)).
+   * With UFP8_TILES_LOWER the tiles past the diagonal are not computed (not written). */
+  const int32_t* attn_q_segment_ids;
+  const int32_t* attn_kv_segment_ids;
+  float* attn_stats;
+  int64_t attn_ld_stats;
+  const float* attn_row;
+  float attn_scale;
+  int32_t attn_reserved;
 } ufp8_gemm_desc;
 
 int ufp8_gemm(const ufp8_gemm_desc* desc, ufp8_stream_t stream);

@@ -20,6 +20,7 @@ BF16 = 2  # bf16 GEMM operands; unquantised output of ufp8_xent_backward
 K_MAJOR, MN_MAJOR = 0, 1
 OUT_BF16, OUT_F32 = 0, 1
 EPI_STORE, EPI_SWIGLU, EPI_DSWIGLU, EPI_RS_PUSH, EPI_XENT, EPI_AXPBY = 0, 1, 2, 3, 4, 5
+EPI_ATTN_STATS, EPI_ATTN_P, EPI_ATTN_DS = 6, 7, 8
 TILES_ALL, TILES_LOWER, TILES_K_TO_DIAG, TILES_K_FROM_DIAG = 0, 1, 2, 3
 GEMM_AUTO, GEMM_SINGLE_CTA, GEMM_CTA_PAIR, GEMM_CTA_PAIR_DIRECT, GEMM_CTA_PAIR_WIDE, GEMM_CTA_PAIR_N512 = (
     0, 1, 2, 3, 4, 5)
@@ -74,7 +75,7 @@ class Operand(ctypes.Structure):
         ("ld", ctypes.c_int64),
         ("batch_stride", ctypes.c_int64),
         ("batch_count", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("batch_group", ctypes.c_int32),
         ("inv_scale", ctypes.c_void_p),
     ]
 
@@ -118,6 +119,13 @@ class GemmDesc(ctypes.Structure):
         ("beta", ctypes.c_float),
         ("tile_mask", ctypes.c_int32),
         ("reserved2", ctypes.c_int32),
+        ("attn_q_segment_ids", ctypes.c_void_p),
+        ("attn_kv_segment_ids", ctypes.c_void_p),
+        ("attn_stats", ctypes.c_void_p),
+        ("attn_ld_stats", ctypes.c_int64),
+        ("attn_row", ctypes.c_void_p),
+        ("attn_scale", ctypes.c_float),
+        ("attn_reserved", ctypes.c_int32),
     ]
 
 

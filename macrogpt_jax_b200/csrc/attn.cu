@@ -8,17 +8,21 @@
 // query attention: query head (h, i) uses key/value head h.
 //
 // B200 layout of the computation: the products are the bf16 CTA-pair GEMM (tcgen05 kind::f16, fp32
-// accumulation) launched per (batch element, kv head) over the group's query heads; the key/value
-// head is a broadcast operand (batch_count 1), and dK, dV concatenate the contraction over the
-// group (k_batches).  The scores S (f32) and probabilities P (bf16) of one batch element are
+// accumulation), one launch per batch element and product over all query heads g = h * I + i; the
+// key/value operand repeats each head for its group (batch_group I: product g reads head g / I),
+// and dK, dV concatenate the contraction over the group (k_batches).  The scores S (f32) and probabilities P (bf16) of one batch element are
 // materialised in HBM (HI x n x n per batch element; P is kept for the backward), and the masked
 // softmax and its backward are row kernels between the GEMMs:
 //   forward:  S_g = Q_g K_h^T            softmax rows -> P_g (bf16), lse     O_g = P_g V_h
 //   backward: dP_g = dO_g V_h^T          dS_g = scale * P_g (dP_g - rowsum(dO_g O_g))
 //             dQ_g = dS_g K_h            dK_h = sum_i dS_g^T Q_g             dV_h = sum_i P_g^T dO_g
-// With the default positions the masked upper triangle is skipped: the score products compute only
-// the 256 x 256 tiles on or below the diagonal, P V and dS K contract each query tile only up to its
-// diagonal, dS^T Q and P^T dO each key tile only from its diagonal (UFP8_TILES_*).
+// With the default positions (0..n-1) the masked upper triangle is skipped: the score products
+// compute only the 256 x 256 tiles on or below the diagonal, P V and dS K contract each query tile
+// only up to its diagonal, dS^T Q and P^T dO each key tile only from its diagonal (UFP8_TILES_*);
+// and S and dP never reach memory: the score product runs once for per-row softmax partials
+// (UFP8_EPI_ATTN_STATS, combined into the lse by a row kernel) and once more writing P from its
+// accumulators (UFP8_EPI_ATTN_P), and the dP product writes dS = scale P (dP - rowsum(dO O))
+// (UFP8_EPI_ATTN_DS).  Explicit positions take the materialised path above.
 // No transposed copy is made (MN-major operands).  RoPE: one kernel builds the bf16 sin/cos table
 // from positions (f32 angle = position * inv_freq, sinf/cosf, then bf16, as the reference's
 // compute_rope_embedding), one applies the rotation (bf16 rounding after each product and sum, as
@@ -249,8 +253,53 @@ __global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftA
   }
 }
 
-ufp8_operand bop(const void* p, int major, int64_t ld, int64_t bstride, int32_t count) {
+// Default positions: the lse of each score row from the UFP8_EPI_ATTN_STATS partials (one
+// (max, sum exp) per 128 columns), over the groups up to the end of the row's 256-wide diagonal
+// tile (the products skip the tiles past it).  One thread per row (row = g * n + q).
+__global__ void __launch_bounds__(kAThreads) attn_lse_kernel(const float2* __restrict__ stats, int64_t rows,
+                                                             int64_t n, int64_t ld, float* __restrict__ lse) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x;
+  if (row >= rows) return;
+  const int64_t q = row % n;
+  const int64_t diag = (q / 256 + 1) * 2;
+  const int64_t groups = diag < ld ? diag : ld;
+  const float2* st = stats + row * ld;
+  float M = -INFINITY;
+  for (int64_t j = 0; j < groups; ++j) M = fmaxf(M, st[j].x);
+  if (M == -INFINITY) {
+    lse[row] = -INFINITY;
+    return;
+  }
+  float S = 0.0f;
+  for (int64_t j = 0; j < groups; ++j) {
+    const float2 v = st[j];
+    if (v.y > 0.0f) S += v.y * __expf(v.x - M);
+  }
+  lse[row] = __fadd_rn(M, logf(S));
+}
+
+// rowsum(dO * O) of every (query head g, query q) row of one batch element (O, dO [n][hi][d]):
+// one warp per row, f32 products summed lane-strided then by a fixed shuffle tree.
+__global__ void __launch_bounds__(kAThreads) attn_rowdot_kernel(const __nv_bfloat16* __restrict__ O,
+                                                                const __nv_bfloat16* __restrict__ dO, int64_t n,
+                                                                int64_t hi, int64_t d, float* __restrict__ out) {
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (w >= hi * n) return;
+  const int64_t g = w / n, q = w - g * n;
+  const __nv_bfloat16* o = O + (q * hi + g) * d;
+  const __nv_bfloat16* go = dO + (q * hi + g) * d;
+  float part = 0.0f;
+  for (int64_t j = lane; j < d; j += 32)
+    part = __fadd_rn(part, __fmul_rn(__bfloat162float(o[j]), __bfloat162float(go[j])));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, off));
+  if (lane == 0) out[w] = part;
+}
+
+ufp8_operand bop(const void* p, int major, int64_t ld, int64_t bstride, int32_t count, int32_t group = 0) {
   ufp8_operand o{};
+  o.batch_group = group;
   o.ptr = p;
   o.fmt = UFP8_BF16;
   o.major = major;
@@ -280,6 +329,36 @@ int gemm_bf16(const ufp8_operand& A, const ufp8_operand& B, int64_t M, int64_t N
   return launch_gemm(d, s, dev, 0, UFP8_GEMM_AUTO, 0);
 }
 
+// One score-shaped product (M = N = n, batch = query heads) with an attention epilogue.
+int gemm_attn(int mode, const ufp8_operand& A, const ufp8_operand& B, int64_t n, int64_t K, int32_t batch, void* D,
+              const int32_t* qseg, const int32_t* kseg, float* stats, int64_t ld_stats, const float* row,
+              const void* P, float scale, cudaStream_t s, const DeviceInfo& dev) {
+  ufp8_gemm_desc d{};
+  d.M = n;
+  d.N = n;
+  d.K = K;
+  d.batch = batch;
+  d.k_batches = 1;
+  d.a = A;
+  d.b = B;
+  d.d = D;
+  d.d_dtype = UFP8_OUT_BF16;
+  d.epilogue = mode;
+  d.ldd = n;
+  d.d_batch_stride = n * n;
+  d.tile_mask = UFP8_TILES_LOWER;
+  d.attn_q_segment_ids = qseg;
+  d.attn_kv_segment_ids = kseg;
+  d.attn_stats = stats;
+  d.attn_ld_stats = ld_stats;
+  d.attn_row = row;
+  d.c = P;
+  d.ldc = n;
+  d.c_batch_stride = n * n;
+  d.attn_scale = scale;
+  return launch_gemm(d, s, dev, 0, UFP8_GEMM_AUTO, 0);
+}
+
 int attn_check(const ufp8_attn_desc* d, const char* who) {
   if (!d) return set_error(UFP8_ERR_INVALID, "%s: null descriptor", who);
   if (d->batch < 0 || d->seq < 1 || d->kv_heads < 1 || d->group < 1 || d->head_dim < 2 || d->head_dim % 8)
@@ -292,24 +371,32 @@ int attn_check(const ufp8_attn_desc* d, const char* who) {
   return UFP8_OK;
 }
 
+// Workspaces per batch element.  Default positions (fused): forward = ATTN_STATS partials
+// [HI * n][ceil(n / 128)] float2, backward = rowsum(dO O) [HI * n] f32 + dS.  Explicit positions:
+// forward = S f32, backward = dP f32 + dS.
 struct AttnLayout {
-  int64_t S, total_fwd;       // forward workspace: S f32 of one batch element
+  int64_t S, total_fwd;       // forward workspace: S f32 or the partials, at offset 0
   int64_t P, lse, saved;      // saved: P bf16 and lse of every batch element
-  int64_t dP, dS, total_bwd;  // backward workspace: dP f32 and dS bf16 of one batch element
+  int64_t dP, dS, total_bwd;  // backward workspace: dP f32 or rowsum(dO O) at offset 0, dS bf16
+  int64_t ld_stats;           // float2 partials per row (fused path)
 };
 
 int64_t al256(int64_t b) { return (b + 255) / 256 * 256; }
 
+bool attn_fused(const ufp8_attn_desc& d) { return d.q_positions == nullptr && d.kv_positions == nullptr; }
+
 AttnLayout attn_layout(const ufp8_attn_desc& d) {
   const int64_t hi = d.kv_heads * d.group, nn = d.seq * d.seq;
+  const bool fused = attn_fused(d);
   AttnLayout L{};
+  L.ld_stats = (d.seq + 127) / 128;
   L.S = 0;
-  L.total_fwd = al256(hi * nn * 4);
+  L.total_fwd = fused ? al256(hi * d.seq * L.ld_stats * 8) : al256(hi * nn * 4);
   L.P = 0;
   L.lse = al256(d.batch * hi * nn * 2);
   L.saved = L.lse + al256(d.batch * hi * d.seq * 4);
   L.dP = 0;
-  L.dS = al256(hi * nn * 4);
+  L.dS = fused ? al256(hi * d.seq * 4) : al256(hi * nn * 4);
   L.total_bwd = L.dS + al256(hi * nn * 2);
   return L;
 }
@@ -395,12 +482,38 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
     const __nv_bfloat16* kB = kb + b * n * H * Dh;
     const __nv_bfloat16* vB = vb + b * n * H * Dh;
     __nv_bfloat16* P = P0 + b * hi * nn;
-    for (int64_t h = 0; h < H; ++h) {  // S_g = Q_g K_h^T over the group's query heads
-      int rc = gemm_bf16(bop(qB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
-                         bop(kB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
-                         S + h * I * nn, 1, n, nn, s, *dev, causal ? UFP8_TILES_LOWER : UFP8_TILES_ALL);
+    const int32_t* qsegB = d->q_segment_ids ? d->q_segment_ids + b * n : nullptr;
+    const int32_t* ksegB = d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr;
+    const ufp8_operand qop = bop(qB, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi));
+    const ufp8_operand kop = bop(kB, UFP8_K_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I));
+    if (causal) {
+      // Fused: the score product runs twice without storing S, first for the per-row softmax
+      // partials (-> lse), then writing P = exp(scale s - lse) straight from the accumulators.
+      auto* stats = reinterpret_cast<float*>(S);
+      int rc = gemm_attn(UFP8_EPI_ATTN_STATS, qop, kop, n, Dh, static_cast<int32_t>(hi), nullptr, qsegB, ksegB, stats,
+                         L.ld_stats, nullptr, nullptr, d->scale, s, *dev);
       if (rc) return rc;
+      const int64_t rows = hi * n;
+      attn_lse_kernel<<<static_cast<unsigned>((rows + kAThreads - 1) / kAThreads), kAThreads, 0, s>>>(
+          reinterpret_cast<const float2*>(stats), rows, n, L.ld_stats, lse0 + b * hi * n);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_error(e, "attention lse launch");
+      rc = gemm_attn(UFP8_EPI_ATTN_P, qop, kop, n, Dh, static_cast<int32_t>(hi), P, qsegB, ksegB, nullptr, 0,
+                     lse0 + b * hi * n, nullptr, d->scale, s, *dev);
+      if (rc) return rc;
+      rc = gemm_bf16(bop(P, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(hi)),
+                     bop(vB, UFP8_MN_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, Dh, n,
+                     static_cast<int32_t>(hi), 1, ob + b * n * hi * Dh, 0, hi * Dh, Dh, s, *dev,
+                     UFP8_TILES_K_TO_DIAG);
+      if (rc) return rc;
+      continue;
     }
+    // S_g = Q_g K_h^T for every query head g = h * I + i in one launch (key head g / I).
+    int rc = gemm_bf16(bop(qB, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)),
+                       bop(kB, UFP8_K_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, n,
+                       Dh, static_cast<int32_t>(hi), 1, S, 1, n, nn, s, *dev,
+                       UFP8_TILES_ALL);
+    if (rc) return rc;
     SoftArgs a{};
     a.S = S;
     a.rows = hi * n;
@@ -415,13 +528,12 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
     attn_softmax_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "attention softmax launch");
-    for (int64_t h = 0; h < H; ++h) {  // O_g = P_g V_h
-      int rc = gemm_bf16(bop(P + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
-                         bop(vB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
-                         ob + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev,
-                         causal ? UFP8_TILES_K_TO_DIAG : UFP8_TILES_ALL);
-      if (rc) return rc;
-    }
+    // O_g = P_g V_{g / I}
+    rc = gemm_bf16(bop(P, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(hi)),
+                   bop(vB, UFP8_MN_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, Dh, n,
+                   static_cast<int32_t>(hi), 1, ob + b * n * hi * Dh, 0, hi * Dh, Dh, s, *dev,
+                   UFP8_TILES_ALL);
+    if (rc) return rc;
   }
   return UFP8_OK;
 }
@@ -462,41 +574,56 @@ extern "C" int ufp8_attention_backward(const ufp8_attn_desc* d, const void* q, c
     const __nv_bfloat16* oB = ob + b * n * hi * Dh;
     const __nv_bfloat16* goB = gob + b * n * hi * Dh;
     const __nv_bfloat16* P = P0 + b * hi * nn;
-    for (int64_t h = 0; h < H; ++h) {  // dP_g = dO_g V_h^T
-      int rc = gemm_bf16(bop(goB + h * I * Dh, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(I)),
-                         bop(vB + h * Dh, UFP8_K_MAJOR, H * Dh, 0, 1), n, n, Dh, static_cast<int32_t>(I), 1,
-                         dP + h * I * nn, 1, n, nn, s, *dev, causal ? UFP8_TILES_LOWER : UFP8_TILES_ALL);
+    int rc;
+    if (causal) {
+      // Fused: D = rowsum(dO O), then the dP product writes dS = scale P (dP - D) from its
+      // accumulators and the saved P (no dP in memory).
+      float* Drow = dP;
+      const int64_t warps = hi * n;
+      attn_rowdot_kernel<<<static_cast<unsigned>((warps * 32 + kAThreads - 1) / kAThreads), kAThreads, 0, s>>>(
+          oB, goB, n, hi, Dh, Drow);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_error(e, "attention rowdot launch");
+      rc = gemm_attn(UFP8_EPI_ATTN_DS, bop(goB, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)),
+                         bop(vB, UFP8_K_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, Dh,
+                         static_cast<int32_t>(hi), dS, d->q_segment_ids ? d->q_segment_ids + b * n : nullptr,
+                         d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr, nullptr, 0, Drow, P, d->scale, s,
+                         *dev);
       if (rc) return rc;
-    }
-    SoftArgs a{};
-    a.rows = hi * n;
-    a.n = n;
-    a.scale = d->scale;
-    a.P = const_cast<__nv_bfloat16*>(P);
-    a.dP = dP;
-    a.O = oB;
-    a.dO = goB;
-    a.hi = hi;
-    a.d = Dh;
-    a.dS = dS;
-    a.qseg = d->q_segment_ids ? d->q_segment_ids + b * n : nullptr;
-    a.kseg = d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr;
-    a.qpos = d->q_positions ? d->q_positions + b * n : nullptr;
-    a.kpos = d->kv_positions ? d->kv_positions + b * n : nullptr;
-    attn_softmax_bwd_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_error(e, "attention softmax backward launch");
-    for (int64_t h = 0; h < H; ++h) {
-      // dQ_g = dS_g K_h
-      int rc = gemm_bf16(bop(dS + h * I * nn, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(I)),
-                         bop(kB + h * Dh, UFP8_MN_MAJOR, H * Dh, 0, 1), n, Dh, n, static_cast<int32_t>(I), 1,
-                         dqb + b * n * hi * Dh + h * I * Dh, 0, hi * Dh, Dh, s, *dev,
-                         causal ? UFP8_TILES_K_TO_DIAG : UFP8_TILES_ALL);
+    } else {
+      // dP_g = dO_g V_{g / I}^T, then the softmax backward rows
+      rc = gemm_bf16(bop(goB, UFP8_K_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)),
+                     bop(vB, UFP8_K_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, n, Dh,
+                     static_cast<int32_t>(hi), 1, dP, 1, n, nn, s, *dev, UFP8_TILES_ALL);
       if (rc) return rc;
+      SoftArgs a{};
+      a.rows = hi * n;
+      a.n = n;
+      a.scale = d->scale;
+      a.P = const_cast<__nv_bfloat16*>(P);
+      a.dP = dP;
+      a.O = oB;
+      a.dO = goB;
+      a.hi = hi;
+      a.d = Dh;
+      a.dS = dS;
+      a.qseg = d->q_segment_ids ? d->q_segment_ids + b * n : nullptr;
+      a.kseg = d->kv_segment_ids ? d->kv_segment_ids + b * n : nullptr;
+      a.qpos = d->q_positions ? d->q_positions + b * n : nullptr;
+      a.kpos = d->kv_positions ? d->kv_positions + b * n : nullptr;
+      attn_softmax_bwd_kernel<<<static_cast<unsigned>(hi * n), kAThreads, 0, s>>>(a);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return cuda_error(e, "attention softmax backward launch");
     }
+    // dQ_g = dS_g K_{g / I}
+    rc = gemm_bf16(bop(dS, UFP8_K_MAJOR, n, nn, static_cast<int32_t>(hi)),
+                   bop(kB, UFP8_MN_MAJOR, H * Dh, Dh, static_cast<int32_t>(H), static_cast<int32_t>(I)), n, Dh, n,
+                   static_cast<int32_t>(hi), 1, dqb + b * n * hi * Dh, 0, hi * Dh, Dh, s, *dev,
+                   causal ? UFP8_TILES_K_TO_DIAG : UFP8_TILES_ALL);
+    if (rc) return rc;
     // dK_h = sum_i dS_g^T Q_g, dV_h = sum_i P_g^T dO_g: one launch over the kv heads (batch H), the
     // contraction running over the group's query rows (k_batches I, slice h * I + i = g).
-    int rc = gemm_bf16(bop(dS, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
+    rc = gemm_bf16(bop(dS, UFP8_MN_MAJOR, n, nn, static_cast<int32_t>(hi)),
                        bop(qB, UFP8_MN_MAJOR, hi * Dh, Dh, static_cast<int32_t>(hi)), n, Dh, n,
                        static_cast<int32_t>(H), static_cast<int32_t>(I), dkb + b * n * H * Dh, 0, H * Dh, Dh, s, *dev,
                        causal ? UFP8_TILES_K_FROM_DIAG : UFP8_TILES_ALL);

@@ -55,6 +55,7 @@ struct GemmArgs {
   int M, N, K;
   int batch, k_batches, mode;
   int a_major, b_major, a_bcast, b_bcast;
+  int a_group, b_group;  // GEMM batch g reads operand slice g / group (k_batches == 1)
   int tiles_m, tiles_n, ksteps;
   uint32_t idesc;
   const float* inv_a;
@@ -86,6 +87,16 @@ struct GemmArgs {
   float alpha_mul, beta;
   int c_vec;  // AXPBY: C rows 16-byte aligned
   int tile_mask;  // UFP8_TILES_* (bf16 operands only)
+  // UFP8_EPI_ATTN_* (bf16 operands): segment ids of rows / columns, STATS partials, the per-row
+  // value (lse for P, rowsum(dO O) for DS), P for DS (pitch ldc, slice pitch c_bstride), scale.
+  const int32_t* attn_qseg;
+  const int32_t* attn_kseg;
+  float* attn_stats;
+  long long attn_ld;
+  const float* attn_row;
+  const __nv_bfloat16* attn_p;
+  float attn_scale;
+  int attn_kseg_vec;  // column ids readable as int4
 };
 
 // The tiles of a masked bf16 GEMM (UFP8_TILES_*): whether M tile mb / N tile nb runs, and its k-step
@@ -257,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           armed |= 1u << stage;
           armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.a_group);
           if (args.a_major == UFP8_K_MAJOR)
             tma_load_3d(sa, &tmA, &full[stage], k0, mb * kBM, az);
           else
@@ -270,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               bz = half;
             } else {
               n0 = nb * kBN + half * 128;
-              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.b_group);
             }
             if (args.b_major == UFP8_K_MAJOR)
               tma_load_3d(sb + half * kHalfBytesB, &tmB, &full[stage], k0, n0, bz);
@@ -649,14 +660,108 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 }
 
 
+// One 32-column chunk of an attention epilogue (UFP8_EPI_ATTN_*): accumulators r of row `row`
+// (query), columns col0 .. col0 + 31 (keys; `valid` of them below N), batch entry g; sq = the
+// row's segment id, rv = its attn_row value.  Column c is visible iff c <= row and its segment id
+// equals sq >= 0.  STATS folds the visible x = scale * acc into the running (m, s) of this
+// thread's 128 columns; P and DS store 32 bf16 values at d.
+__device__ __forceinline__ void attn_chunk(const GemmArgs& a, const uint32_t (&r)[32], int row, int col0, int valid,
+                                           int g, int sq, float rv, float& m, float& s, __nv_bfloat16* d, int vec,
+                                           uint64_t pol, bool uni, uint32_t segmask) {
+  uint32_t vis = 0;
+  const int lim = min(min(valid, 32), row - col0 + 1);  // causal: columns <= row
+  if (sq >= 0 && lim > 0) {
+    const uint32_t upto = lim >= 32 ? 0xFFFFFFFFu : ((1u << lim) - 1u);
+    if (uni) {  // the warp's rows share sq: segmask = the columns carrying it (one ballot)
+      vis = segmask & upto;
+    } else if (a.attn_kseg == nullptr) {
+      vis = sq == 0 ? upto : 0u;
+    } else if (a.attn_kseg_vec && valid >= 32) {
+      const int4* kp = reinterpret_cast<const int4*>(a.attn_kseg + col0);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int4 k4 = kp[i];
+        vis |= (static_cast<uint32_t>(k4.x == sq) | (static_cast<uint32_t>(k4.y == sq) << 1) |
+                (static_cast<uint32_t>(k4.z == sq) << 2) | (static_cast<uint32_t>(k4.w == sq) << 3))
+               << (4 * i);
+      }
+      vis &= upto;
+    } else {
+#pragma unroll 4
+      for (int j = 0; j < 32; ++j)
+        if (j < lim && a.attn_kseg[col0 + j] == sq) vis |= 1u << j;
+    }
+  }
+  if (a.mode == UFP8_EPI_ATTN_STATS) {
+    if (vis == 0u) return;
+    float x[32];
+    // four independent partial maxima / sums (short dependency chains)
+    float cm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (vis == 0xFFFFFFFFu) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] = __fmul_rn(__uint_as_float(r[j]), a.attn_scale);
+        cm4[j & 3] = fmaxf(cm4[j & 3], x[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        x[j] = ((vis >> j) & 1u) ? __fmul_rn(__uint_as_float(r[j]), a.attn_scale) : -INFINITY;
+        cm4[j & 3] = fmaxf(cm4[j & 3], x[j]);
+      }
+    }
+    const float cm = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3]));
+    if (cm > m) {
+      s = s * __expf(m - cm);  // m = -inf on the first visible chunk: s = 0 * 0
+      m = cm;
+    }
+    float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc4[j & 3] += __expf(__fsub_rn(x[j], m));  // masked: exp(-inf) = 0
+    s += (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+    return;
+  }
+  uint32_t o[16];
+  if (a.mode == UFP8_EPI_ATTN_P) {
+    if (vis == 0xFFFFFFFFu) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        o[j] = pack_bf16x2(__expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j]), a.attn_scale), rv)),
+                           __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j + 1]), a.attn_scale), rv)));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float p0 = ((vis >> (2 * j)) & 1u)
+                             ? __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j]), a.attn_scale), rv)) : 0.0f;
+        const float p1 = ((vis >> (2 * j + 1)) & 1u)
+                             ? __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j + 1]), a.attn_scale), rv)) : 0.0f;
+        o[j] = pack_bf16x2(p0, p1);
+      }
+    }
+  } else {  // DS
+    const __nv_bfloat16* pp = a.attn_p + g * a.c_bstride + static_cast<long long>(row) * a.ldc + col0;
+    uint32_t pw[2][8];
+    load_bf16x16_packed(pp, pw[0], valid, a.c_vec);
+    load_bf16x16_packed(pp + 16, pw[1], valid - 16, a.c_vec);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t w2 = pw[j >> 3][j & 7];
+      const float d0 = __fmul_rn(__fmul_rn(lo_f(w2), __fsub_rn(__uint_as_float(r[2 * j]), rv)), a.attn_scale);
+      const float d1 = __fmul_rn(__fmul_rn(hi_f(w2), __fsub_rn(__uint_as_float(r[2 * j + 1]), rv)), a.attn_scale);
+      o[j] = pack_bf16x2(d0, d1);
+    }
+  }
+  store_bf16x32_packed_h(d, o, valid, vec, pol);
+}
+
 // KCH = 128-byte K chunks per ring stage (1 or 2): a stage holds KCH A sub-tiles followed by KCH
 // B sub-tiles of 16 KiB each, and the MMA thread issues 4 * KCH MMAs per stage, so the per-stage
 // barrier hand-offs (full -> MMA issue -> commit -> empty -> next load) occur half as often.
 // kBf16: bf16 operands (tcgen05.mma kind::f16).  The ring stages hold the same bytes: a 128-byte K
 // chunk is 64 elements, a K-major sub-tile 128 rows x 128 B as for fp8, and an MN-major sub-tile
 // two 64-element (128-byte) MN atoms of 64 K rows each, 8 KiB apart (the descriptor's leading
-// byte offset).  Each MMA consumes K = 16 (32 bytes), four per chunk as with fp8.  Only the STORE
-// and AXPBY epilogues are compiled in.
+// byte offset).  Each MMA consumes K = 16 (32 bytes), four per chunk as with fp8.  Only the STORE,
+// AXPBY and ATTN epilogues are compiled in.
 template <int NSTAGES, int kVar, int KCH = 1, bool kBf16 = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -754,14 +859,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.a_group);
           int n0, bz;
           if (swiglu) {
             n0 = nb * 128;
             bz = static_cast<int>(rank);
           } else {
             n0 = nb * kBN + static_cast<int>(rank) * 128;
-            bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+            bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.b_group);
           }
 #pragma unroll
           for (int j = 0; j < KCH; ++j) {
@@ -1043,7 +1148,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           }
         }
       } else if (args.mode == UFP8_EPI_STORE || args.mode == UFP8_EPI_RS_PUSH || args.mode == UFP8_EPI_XENT ||
-                 args.mode == UFP8_EPI_AXPBY) {
+                 args.mode == UFP8_EPI_AXPBY || args.mode >= UFP8_EPI_ATTN_STATS) {
         // RS_PUSH: this row goes to its owner's staging slot for this rank (peer memory).
         // XENT: bf16 logits (soft-capped if asked) and the softmax partials of this warp's 128 columns.
         const bool xent = args.mode == UFP8_EPI_XENT;
@@ -1054,16 +1159,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
           rs_row = static_cast<__nv_bfloat16*>(args.rs_slots[owner]) +
                    (args.rs_rank * args.rs_rows + (row - owner * args.rs_rows)) * args.ldd;
         }
+        const bool attn = kBf16 && args.mode >= UFP8_EPI_ATTN_STATS;
+        int attn_sq = 0;
+        float attn_rv = 0.0f;
+        if (attn && row_ok) {
+          attn_sq = args.attn_qseg ? args.attn_qseg[row] : 0;
+          if (args.attn_row) attn_rv = args.attn_row[static_cast<long long>(g) * args.M + row];
+        }
+        // All rows of this warp in range and of one segment: one ballot per chunk gives the
+        // columns of that segment (row_ok differs only in a partial last tile).
+        const int attn_sq0 = __shfl_sync(0xFFFFFFFFu, attn_sq, 0);
+        const bool attn_uni = attn && __all_sync(0xFFFFFFFFu, row_ok && attn_sq == attn_sq0);
 #pragma unroll 1
         for (int c = chalf * 128; c < chalf * 128 + 128; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
           const int col0 = nb * kBN + c;
+          uint32_t segmask = 0xFFFFFFFFu;
+          if (attn_uni && col0 < args.N) {  // warp-uniform condition: every lane takes part
+            if (args.attn_kseg != nullptr) {
+              const int kc = col0 + lane;
+              const int kv = kc < args.N ? args.attn_kseg[kc] : -1;
+              segmask = __ballot_sync(0xFFFFFFFFu, kv == attn_sq0);
+            } else {
+              segmask = attn_sq0 == 0 ? 0xFFFFFFFFu : 0u;
+            }
+          }
           if (row_ok && col0 < args.N) {
             const int valid = args.N - col0;
             float am = alpha;  // the accumulator multiplier of the stores below
             if constexpr (kBf16) {
+              if (attn) {
+                attn_chunk(args, r, row, col0, valid, g, attn_sq, attn_rv, xm, xs,
+                           static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride +
+                               static_cast<long long>(row) * args.ldd + col0,
+                           vec, stream, attn_uni, segmask);
+                continue;
+              }
               if (args.c != nullptr) {
                 // AXPBY: v = acc * alpha + beta * C, each product and the sum rounded once.
                 const __nv_bfloat16* cp = args.c + g * args.c_bstride + static_cast<long long>(row) * args.ldc + col0;
@@ -1106,6 +1239,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         }
         if (xent && row_ok && nb * kBN + chalf * 128 < args.N)
           *reinterpret_cast<float2*>(args.xent_stats + 2 * (static_cast<long long>(row) * args.xent_ld + nb * 2 + chalf)) =
+              make_float2(xm, xs);
+        if (attn && args.mode == UFP8_EPI_ATTN_STATS && row_ok && nb * kBN + chalf * 128 < args.N)
+          *reinterpret_cast<float2*>(args.attn_stats +
+                                     2 * ((static_cast<long long>(g) * args.M + row) * args.attn_ld + nb * 2 + chalf)) =
               make_float2(xm, xs);
       } else if (args.mode == UFP8_EPI_SWIGLU) {
         // TMEM columns [0,128) hold up, [128,256) hold gate for hidden units nb*128 + c.
@@ -1336,7 +1473,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
           }
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+          const int az = args.a_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.a_group);
           if (args.a_major == UFP8_K_MAJOR)
             tma_load_3d_pair(sa, &tmA, bar, k0, row0, az);
           else
@@ -1349,7 +1486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
               bz = static_cast<int>(rank);
             } else {
               n0 = nb * 2 * kBN + j * kBN + static_cast<int>(rank) * 128;
-              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g);
+              bz = args.b_bcast ? 0 : (args.k_batches > 1 ? g * args.k_batches + kb : g / args.b_group);
             }
             uint8_t* sb = sa + (1 + j) * kPHalfBytes;
             if (args.b_major == UFP8_K_MAJOR)
@@ -1685,14 +1822,35 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
                 int variant, int group_m) {
   if (d.M < 0 || d.N < 0 || d.K < 0) return set_error(UFP8_ERR_INVALID, "negative GEMM extent");
   if (d.batch < 1 || d.k_batches < 1) return set_error(UFP8_ERR_INVALID, "batch and k_batches must be >= 1");
-  if (d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_SWIGLU && d.epilogue != UFP8_EPI_DSWIGLU &&
-      d.epilogue != UFP8_EPI_RS_PUSH && d.epilogue != UFP8_EPI_XENT && d.epilogue != UFP8_EPI_AXPBY)
+  if (d.epilogue < UFP8_EPI_STORE || d.epilogue > UFP8_EPI_ATTN_DS)
     return set_error(UFP8_ERR_INVALID, "unknown epilogue %d", d.epilogue);
+  const bool attn = d.epilogue >= UFP8_EPI_ATTN_STATS;
   const bool bf16 = d.a.fmt == UFP8_BF16;
   if (bf16 != (d.b.fmt == UFP8_BF16))
     return set_error(UFP8_ERR_INVALID, "A and B must both be fp8 or both be bf16 (one MMA kind)");
-  if (bf16 && d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_AXPBY)
-    return set_error(UFP8_ERR_UNSUPPORTED, "bf16 operands take the STORE and AXPBY epilogues only");
+  if (bf16 && d.epilogue != UFP8_EPI_STORE && d.epilogue != UFP8_EPI_AXPBY && !attn)
+    return set_error(UFP8_ERR_UNSUPPORTED, "bf16 operands take the STORE, AXPBY and ATTN epilogues only");
+  if (attn) {
+    if (!bf16) return set_error(UFP8_ERR_UNSUPPORTED, "the ATTN epilogues take bf16 operands");
+    if (d.K == 0) return set_error(UFP8_ERR_UNSUPPORTED, "ATTN epilogues with K == 0");
+    if (d.epilogue != UFP8_EPI_ATTN_STATS && d.d_dtype != UFP8_OUT_BF16)
+      return set_error(UFP8_ERR_INVALID, "ATTN_P / ATTN_DS write bf16");
+    const uintptr_t ids = reinterpret_cast<uintptr_t>(d.attn_q_segment_ids) |
+                          reinterpret_cast<uintptr_t>(d.attn_kv_segment_ids);
+    if (ids & 3u) return set_error(UFP8_ERR_ALIGN, "ATTN: segment ids not 4-byte aligned");
+    if (d.epilogue == UFP8_EPI_ATTN_STATS) {
+      if (!d.attn_stats || d.attn_ld_stats < (d.N + 127) / 128)
+        return set_error(UFP8_ERR_INVALID, "ATTN_STATS needs attn_stats with attn_ld_stats >= ceil(N / 128)");
+      if (reinterpret_cast<uintptr_t>(d.attn_stats) & 7u)
+        return set_error(UFP8_ERR_ALIGN, "ATTN_STATS: attn_stats not 8-byte aligned");
+    } else if (!d.attn_row) {
+      return set_error(UFP8_ERR_INVALID, "ATTN_P / ATTN_DS need attn_row");
+    }
+    if (d.epilogue == UFP8_EPI_ATTN_DS) {
+      if (!d.c || d.ldc < d.N) return set_error(UFP8_ERR_INVALID, "ATTN_DS needs P in c with ldc >= N");
+      if (reinterpret_cast<uintptr_t>(d.c) & 1u) return set_error(UFP8_ERR_ALIGN, "ATTN_DS: c not 2-byte aligned");
+    }
+  }
   if (d.epilogue == UFP8_EPI_AXPBY) {
     if (!bf16) return set_error(UFP8_ERR_UNSUPPORTED, "AXPBY takes bf16 operands");
     if (!d.c || d.ldc < d.N) return set_error(UFP8_ERR_INVALID, "AXPBY needs c with ldc >= N");
@@ -1737,7 +1895,7 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   if ((d.epilogue == UFP8_EPI_SWIGLU || d.epilogue == UFP8_EPI_DSWIGLU) &&
       (d.d_dtype != UFP8_OUT_BF16 || d.batch != 1 || d.k_batches != 1))
     return set_error(UFP8_ERR_INVALID, "SWIGLU/DSWIGLU epilogues need bf16 output, batch 1, k_batches 1");
-  if (!d.d && !rs) return set_error(UFP8_ERR_INVALID, "null output pointer");
+  if (!d.d && !rs && d.epilogue != UFP8_EPI_ATTN_STATS) return set_error(UFP8_ERR_INVALID, "null output pointer");
   if (d.ldd < d.N) return set_error(UFP8_ERR_INVALID, "ldd < N");
   if (d.epilogue == UFP8_EPI_SWIGLU && (!d.h || d.ldh < d.N))
     return set_error(UFP8_ERR_INVALID, "SWIGLU needs h with ldh >= N");
@@ -1791,6 +1949,19 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   a.beta = d.beta;
   a.c_vec = a.c != nullptr && aligned16(d.c) && (d.ldc * 2) % 16 == 0 && (d.c_batch_stride * 2) % 16 == 0;
   a.tile_mask = d.tile_mask;
+  a.attn_qseg = attn ? d.attn_q_segment_ids : nullptr;
+  a.attn_kseg = attn ? d.attn_kv_segment_ids : nullptr;
+  a.attn_stats = d.epilogue == UFP8_EPI_ATTN_STATS ? d.attn_stats : nullptr;
+  a.attn_ld = d.attn_ld_stats;
+  a.attn_row = attn ? d.attn_row : nullptr;
+  a.attn_p = d.epilogue == UFP8_EPI_ATTN_DS ? static_cast<const __nv_bfloat16*>(d.c) : nullptr;
+  a.attn_scale = d.attn_scale;
+  a.attn_kseg_vec = (reinterpret_cast<uintptr_t>(d.attn_kv_segment_ids) & 15u) == 0;
+  if (d.epilogue == UFP8_EPI_ATTN_DS) {
+    a.ldc = d.ldc;
+    a.c_bstride = d.c_batch_stride;
+    a.c_vec = aligned16(d.c) && (d.ldc * 2) % 16 == 0 && (d.c_batch_stride * 2) % 16 == 0;
+  }
 
   if (d.K == 0) {
     if (rs) return set_error(UFP8_ERR_UNSUPPORTED, "RS_PUSH with K == 0");
@@ -1803,11 +1974,19 @@ int launch_gemm(const ufp8_gemm_desc& d, cudaStream_t stream, const DeviceInfo& 
   // k_batches > 1: operand slice g * k_batches + kb holds batch g's K block kb.
   const int64_t kslices = static_cast<int64_t>(d.batch) * d.k_batches;
   if (kslices >= (int64_t(1) << 31)) return set_error(UFP8_ERR_INVALID, "batch * k_batches exceeds 2^31");
-  int rc = check_operand(d.a, d.M, d.K, d.k_batches > 1 ? static_cast<int>(kslices) : (d.a.batch_count > 1 ? d.batch : 1), "A");
+  const int a_group = d.a.batch_group > 1 ? d.a.batch_group : 1;
+  const int b_group = d.b.batch_group > 1 ? d.b.batch_group : 1;
+  if (d.a.batch_group < 0 || d.b.batch_group < 0) return set_error(UFP8_ERR_INVALID, "negative batch_group");
+  if ((a_group > 1 || b_group > 1) && (d.k_batches > 1 || swiglu))
+    return set_error(UFP8_ERR_UNSUPPORTED, "batch_group > 1 with k_batches > 1 or SWIGLU");
+  const int a_need = (d.batch + a_group - 1) / a_group, b_need = (d.batch + b_group - 1) / b_group;
+  int rc = check_operand(d.a, d.M, d.K, d.k_batches > 1 ? static_cast<int>(kslices) : (d.a.batch_count > 1 ? a_need : 1), "A");
   if (rc) return rc;
-  rc = check_operand(d.b, d.N, d.K, swiglu ? 2 : (d.k_batches > 1 ? static_cast<int>(kslices) : (d.b.batch_count > 1 ? d.batch : 1)),
+  rc = check_operand(d.b, d.N, d.K, swiglu ? 2 : (d.k_batches > 1 ? static_cast<int>(kslices) : (d.b.batch_count > 1 ? b_need : 1)),
                      "B");
   if (rc) return rc;
+  a.a_group = a_group;
+  a.b_group = b_group;
 
   a.a_major = d.a.major;
   a.b_major = d.b.major;

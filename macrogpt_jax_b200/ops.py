@@ -118,11 +118,13 @@ def operand(t: Fp8Tensor, major: int, ld: int, batch_stride: int = 0, batch_coun
     return C.Operand(t.q.data_ptr(), t.fmt, major, ld, batch_stride, batch_count, 0, inv.data_ptr())
 
 
-def bf16_operand(t: torch.Tensor, major: int, ld: int, batch_stride: int = 0, batch_count: int = 1) -> C.Operand:
-    """A bf16 GEMM operand (tcgen05 kind::f16), no scale factor."""
+def bf16_operand(t: torch.Tensor, major: int, ld: int, batch_stride: int = 0, batch_count: int = 1,
+                 batch_group: int = 0) -> C.Operand:
+    """A bf16 GEMM operand (tcgen05 kind::f16), no scale factor; `batch_group` > 1: GEMM batch g
+    reads slice g / batch_group."""
     if t.dtype != torch.bfloat16 or not t.is_cuda:
         raise ValueError("bf16_operand: expected a CUDA bfloat16 tensor")
-    return C.Operand(t.data_ptr(), C.BF16, major, ld, batch_stride, batch_count, 0, None)
+    return C.Operand(t.data_ptr(), C.BF16, major, ld, batch_stride, batch_count, batch_group, None)
 
 
 def gemm(a: C.Operand, b: C.Operand, M: int, N: int, K: int, d: torch.Tensor, ldd: int,

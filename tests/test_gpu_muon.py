@@ -82,7 +82,7 @@ def test_bf16_gemm_rejects_mixed_and_fp8_epilogues(cuda):
     d = torch.empty((64, 64), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(C.UFP8Error, match="both be fp8 or both be bf16"):
         ops.gemm(ops.bf16_operand(a, C.K_MAJOR, 64), ops.operand(q, C.K_MAJOR, 64), 64, 64, 64, d, 64)
-    with pytest.raises(C.UFP8Error, match="STORE and AXPBY"):
+    with pytest.raises(C.UFP8Error, match="STORE, AXPBY and ATTN"):
         ops.gemm(ops.bf16_operand(a, C.K_MAJOR, 64), ops.bf16_operand(a, C.K_MAJOR, 64), 64, 64, 64, d, 64,
                  epilogue=C.EPI_SWIGLU, h=d, ldh=64, amax_out=torch.empty(1, device=cuda))
 
@@ -161,3 +161,33 @@ def test_bf16_gemm_tile_masks(cuda, mask):
     got = d.double().cpu().numpy()
     np.testing.assert_array_equal(got == -7.0, ref == -7.0)
     _cmp(got, ref, True)
+
+
+@pytest.mark.parametrize("b_major", [0, 1])
+def test_bf16_gemm_batch_group(cuda, b_major):
+    """batch_group 3: product g (of 6) reads B slice g / 3 (the key / value head shared by a group
+    of query heads), slices laid out with a pitch smaller than the row pitch as the attention's
+    [token, head, d] tensors are."""
+    from macrogpt_jax_b200 import _capi as C
+    from macrogpt_jax_b200 import ops
+    import torch
+    G, grp, M, N, K = 6, 3, 320, 128, 192
+    rng = np.random.default_rng(50 + b_major)
+    a_bits = op.bf16_normal(rng, (G, M, K))
+    if b_major == C.K_MAJOR:
+        b_bits = op.bf16_normal(rng, (N, G // grp, K))  # [n, head, k]: slice pitch K, row pitch heads * K
+        bt = bits_to_torch_bf16(b_bits, cuda)
+        bop = ops.bf16_operand(bt, C.K_MAJOR, (G // grp) * K, K, G // grp, grp)
+        bmat = lambda s: b_bits[:, s, :]  # noqa: E731  [N, K]
+    else:
+        b_bits = op.bf16_normal(rng, (K, G // grp, N))  # [k, head, n]: MN-major
+        bt = bits_to_torch_bf16(b_bits, cuda)
+        bop = ops.bf16_operand(bt, C.MN_MAJOR, (G // grp) * N, N, G // grp, grp)
+        bmat = lambda s: b_bits[:, s, :].T  # noqa: E731
+    at = bits_to_torch_bf16(a_bits, cuda)
+    d = torch.empty((G, M, N), dtype=torch.float32, device=cuda)
+    ops.gemm(ops.bf16_operand(at, C.K_MAJOR, K, M * K, G), bop, M, N, K, d, N, M * N, batch=G)
+    torch.cuda.synchronize()
+    a64 = bf16_bits_to_f64(a_bits)
+    ref = np.stack([a64[g] @ bf16_bits_to_f64(np.ascontiguousarray(bmat(g // grp))).T for g in range(G)])
+    _cmp(d.double().cpu().numpy(), ref, True)
