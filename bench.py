@@ -256,7 +256,8 @@ def gpu_arm_config(args, cfg, world):
         rs = {"auto": "y pushed from the GEMM epilogue, dx by copy engines beside dWf",
               "epilogue": "pushed from the GEMM epilogues", "copy": "by copy engines"}[args.tp_rs_engine]
         parallelism = (f"tp{world} (NVLink P2P; all-gather consumed block by block by the GEMMs, by "
-                       f"{'SM push kernel' if args.tp_ag == 'sm' else f'copy engines on {args.tp_lanes} lanes'}; "
+                       f"{'SM push kernel' if args.tp_ag == 'sm' else 'copy engines'}"
+                       f"{'' if args.tp_lanes == 1 or args.tp_ag == 'sm' else f' on {args.tp_lanes} lanes'}; "
                        f"reduce-scatter {rs})" if args.tp_rs == "p2p"
                        else f"tp{world} (NCCL all-gather / reduce-scatter / all-reduce)")
     else:
@@ -1067,10 +1068,10 @@ def main():
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p",
                     help="tensor-parallel collectives: NVLink P2P (all-gather and reduce-scatter with the GEMMs), "
                          "or NCCL")
-    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="auto",
+    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="epilogue",
                     help="P2P reduce-scatter push: GEMM epilogue, copy engines beside independent work, or auto "
                          "(epilogue for y, copy engines for dx)")
-    ap.add_argument("--tp-lanes", type=int, default=2, choices=range(1, 9),
+    ap.add_argument("--tp-lanes", type=int, default=1, choices=range(1, 9),
                     help="streams the copy-engine pushes spread their per-peer copies over")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -665,9 +665,8 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 // row's segment id, rv = its attn_row value.  Column c is visible iff c <= row and its segment id
 // equals sq >= 0.  STATS folds the visible x = scale * acc into the running (m, s) of this
 // thread's 128 columns; P and DS store 32 bf16 values at d.
-__device__ __forceinline__ void attn_chunk(const GemmArgs& a, const uint32_t (&r)[32], int row, int col0, int valid,
-                                           int g, int sq, float rv, float& m, float& s, __nv_bfloat16* d, int vec,
-                                           uint64_t pol, bool uni, uint32_t segmask) {
+__device__ __forceinline__ uint32_t attn_vis(const GemmArgs& a, int row, int col0, int valid, int sq, bool uni,
+                                             uint32_t segmask) {
   uint32_t vis = 0;
   const int lim = min(min(valid, 32), row - col0 + 1);  // causal: columns <= row
   if (sq >= 0 && lim > 0) {
@@ -692,35 +691,43 @@ __device__ __forceinline__ void attn_chunk(const GemmArgs& a, const uint32_t (&r
         if (j < lim && a.attn_kseg[col0 + j] == sq) vis |= 1u << j;
     }
   }
-  if (a.mode == UFP8_EPI_ATTN_STATS) {
-    if (vis == 0u) return;
-    float x[32];
-    // four independent partial maxima / sums (short dependency chains)
-    float cm4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    if (vis == 0xFFFFFFFFu) {
+  return vis;
+}
+
+// STATS over 64 columns (two 32-column chunks r0, r1 from col0): the visible x = scale * acc
+// fold into the running (m, s) of this thread's 128 columns with one rescale.
+__device__ __forceinline__ void attn_stats64(const GemmArgs& a, uint32_t (&r0)[32], uint32_t (&r1)[32], int row,
+                                             int col0, int valid, int sq, bool uni, uint32_t sm0, uint32_t sm1,
+                                             float& m, float& s) {
+  const uint32_t v0 = attn_vis(a, row, col0, valid, sq, uni, sm0);
+  const uint32_t v1 = valid > 32 ? attn_vis(a, row, col0 + 32, valid - 32, sq, uni, sm1) : 0u;
+  if ((v0 | v1) == 0u) return;
+  float cm2[2] = {-INFINITY, -INFINITY};  // independent partial maxima / sums (short chains)
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        x[j] = __fmul_rn(__uint_as_float(r[j]), a.attn_scale);
-        cm4[j & 3] = fmaxf(cm4[j & 3], x[j]);
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        x[j] = ((vis >> j) & 1u) ? __fmul_rn(__uint_as_float(r[j]), a.attn_scale) : -INFINITY;
-        cm4[j & 3] = fmaxf(cm4[j & 3], x[j]);
-      }
-    }
-    const float cm = fmaxf(fmaxf(cm4[0], cm4[1]), fmaxf(cm4[2], cm4[3]));
-    if (cm > m) {
-      s = s * __expf(m - cm);  // m = -inf on the first visible chunk: s = 0 * 0
-      m = cm;
-    }
-    float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int j = 0; j < 32; ++j) acc4[j & 3] += __expf(__fsub_rn(x[j], m));  // masked: exp(-inf) = 0
-    s += (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
-    return;
+  for (int j = 0; j < 32; ++j) {
+    const float x0 = ((v0 >> j) & 1u) ? __fmul_rn(__uint_as_float(r0[j]), a.attn_scale) : -INFINITY;
+    const float x1 = ((v1 >> j) & 1u) ? __fmul_rn(__uint_as_float(r1[j]), a.attn_scale) : -INFINITY;
+    r0[j] = __float_as_uint(x0);
+    r1[j] = __float_as_uint(x1);
+    cm2[j & 1] = fmaxf(cm2[j & 1], fmaxf(x0, x1));
   }
+  const float cm = fmaxf(cm2[0], cm2[1]);
+  if (cm > m) {
+    s = s * __expf(m - cm);  // m = -inf on the first visible chunk: s = 0 * 0
+    m = cm;
+  }
+  float acc2[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int j = 0; j < 32; ++j)  // masked: exp(-inf) = 0
+    acc2[j & 1] += __expf(__fsub_rn(__uint_as_float(r0[j]), m)) + __expf(__fsub_rn(__uint_as_float(r1[j]), m));
+  s += acc2[0] + acc2[1];
+}
+
+// P / DS for one 32-column chunk (see attn_vis for the mask), stored as 32 bf16 at d.
+__device__ __forceinline__ void attn_chunk(const GemmArgs& a, const uint32_t (&r)[32], int row, int col0, int valid,
+                                           int g, int sq, float rv, __nv_bfloat16* d, int vec, uint64_t pol,
+                                           bool uni, uint32_t segmask) {
+  const uint32_t vis = a.mode == UFP8_EPI_ATTN_P ? attn_vis(a, row, col0, valid, sq, uni, segmask) : 0u;
   uint32_t o[16];
   if (a.mode == UFP8_EPI_ATTN_P) {
     if (vis == 0xFFFFFFFFu) {
@@ -1016,12 +1023,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
     }
     int local = 0;
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
+      int pf_sq = 0;      // ATTN: this row's segment id and attn_row value, loaded before the wait
+      float pf_rv = 0.0f;
       if constexpr (kBf16) {
         int g_, mb_, nb_, lo_, hi_;
         map_tile(tile, args, g_, mb_, nb_);
         if (!masked_tile(args, mb_, nb_, KCH * (kBK / 2), lo_, hi_)) {
           --local;
           continue;
+        }
+        const int row_ = mb_ * 2 * kBM + row_in_tile;
+        if (args.mode >= UFP8_EPI_ATTN_STATS && row_ < args.M) {
+          pf_sq = args.attn_qseg ? args.attn_qseg[row_] : 0;
+          if (args.attn_row) pf_rv = args.attn_row[static_cast<long long>(g_) * args.M + row_];
+          const int c0 = nb_ * kBN + chalf * 128;
+          if (args.attn_p != nullptr && c0 < args.N) {  // DS: this row's 128 P values into L2
+            const __nv_bfloat16* pp = args.attn_p + g_ * args.c_bstride + static_cast<long long>(row_) * args.ldc + c0;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(pp));
+            if (c0 + 64 < args.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(pp + 64));
+          }
         }
       }
       const int buf = local & 1;
@@ -1163,40 +1183,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         int attn_sq = 0;
         float attn_rv = 0.0f;
         if (attn && row_ok) {
-          attn_sq = args.attn_qseg ? args.attn_qseg[row] : 0;
-          if (args.attn_row) attn_rv = args.attn_row[static_cast<long long>(g) * args.M + row];
+          attn_sq = pf_sq;
+          attn_rv = pf_rv;
         }
         // All rows of this warp in range and of one segment: one ballot per chunk gives the
         // columns of that segment (row_ok differs only in a partial last tile).
         const int attn_sq0 = __shfl_sync(0xFFFFFFFFu, attn_sq, 0);
         const bool attn_uni = attn && __all_sync(0xFFFFFFFFu, row_ok && attn_sq == attn_sq0);
+        if (attn) {
+          // 64 columns per step: two TMEM loads under one wait, the key segment ballots issued
+          // before it (warp-uniform conditions: every lane takes part).
 #pragma unroll 1
-        for (int c = chalf * 128; c < chalf * 128 + 128; c += 32) {
+          for (int c = chalf * 128; c < chalf * 128 + 128; c += 64) {
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(tbase + c, r0);
+            tmem_ld_32x32b_x32(tbase + c + 32, r1);
+            const int col0 = nb * kBN + c;
+            uint32_t sm0 = 0xFFFFFFFFu, sm1 = 0xFFFFFFFFu;
+            if (attn_uni && col0 < args.N && args.mode != UFP8_EPI_ATTN_DS) {
+              if (args.attn_kseg != nullptr) {
+                const int k0 = col0 + lane, k1 = col0 + 32 + lane;
+                const int kv0 = k0 < args.N ? args.attn_kseg[k0] : -1;
+                const int kv1 = k1 < args.N ? args.attn_kseg[k1] : -1;
+                sm0 = __ballot_sync(0xFFFFFFFFu, kv0 == attn_sq0);
+                sm1 = __ballot_sync(0xFFFFFFFFu, kv1 == attn_sq0);
+              } else {
+                sm0 = sm1 = attn_sq0 == 0 ? 0xFFFFFFFFu : 0u;
+              }
+            }
+            tmem_ld_wait();
+            if (row_ok && col0 < args.N) {
+              const int valid = args.N - col0;
+              if (args.mode == UFP8_EPI_ATTN_STATS) {
+                attn_stats64(args, r0, r1, row, col0, valid, attn_sq, attn_uni, sm0, sm1, xm, xs);
+              } else {
+                __nv_bfloat16* dp = static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride +
+                                    static_cast<long long>(row) * args.ldd + col0;
+                attn_chunk(args, r0, row, col0, valid, g, attn_sq, attn_rv, dp, vec, stream, attn_uni, sm0);
+                if (valid > 32)
+                  attn_chunk(args, r1, row, col0 + 32, valid - 32, g, attn_sq, attn_rv, dp + 32, vec, stream, attn_uni,
+                             sm1);
+              }
+            }
+          }
+        }
+#pragma unroll 1
+        for (int c = chalf * 128; !attn && c < chalf * 128 + 128; c += 32) {  // the other modes
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c, r);
           tmem_ld_wait();
           const int col0 = nb * kBN + c;
-          uint32_t segmask = 0xFFFFFFFFu;
-          if (attn_uni && col0 < args.N) {  // warp-uniform condition: every lane takes part
-            if (args.attn_kseg != nullptr) {
-              const int kc = col0 + lane;
-              const int kv = kc < args.N ? args.attn_kseg[kc] : -1;
-              segmask = __ballot_sync(0xFFFFFFFFu, kv == attn_sq0);
-            } else {
-              segmask = attn_sq0 == 0 ? 0xFFFFFFFFu : 0u;
-            }
-          }
           if (row_ok && col0 < args.N) {
             const int valid = args.N - col0;
             float am = alpha;  // the accumulator multiplier of the stores below
             if constexpr (kBf16) {
-              if (attn) {
-                attn_chunk(args, r, row, col0, valid, g, attn_sq, attn_rv, xm, xs,
-                           static_cast<__nv_bfloat16*>(args.d) + g * args.d_bstride +
-                               static_cast<long long>(row) * args.ldd + col0,
-                           vec, stream, attn_uni, segmask);
-                continue;
-              }
               if (args.c != nullptr) {
                 // AXPBY: v = acc * alpha + beta * C, each product and the sum rounded once.
                 const __nv_bfloat16* cp = args.c + g * args.c_bstride + static_cast<long long>(row) * args.ldc + col0;

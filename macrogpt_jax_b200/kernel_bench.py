@@ -3,7 +3,8 @@
     python -m macrogpt_jax_b200.kernel_bench [--tokens T] [--d D] [--hidden H]
                                              [--gemms F1,F2,B2,B1,B4,B3] [--reps R] [--warmup W]
                                              [--variant V] [--seconds S] [--cublas]
-                                             [--quant | --norm | --rs-push]
+                                             [--quant | --norm | --rs-push | --xent | --ns |
+                                              --attn [--batch B --seq S --kv-heads H --group I]]
 
 Each named GEMM of the GMLP step runs R times after W warm-up launches on seeded fp8
 operands; the script prints one line per GEMM with its mean duration and TFLOP/s.  With
@@ -254,6 +255,39 @@ def ns_bench(args, dev):
           flush=True)
 
 
+def attn_bench(args, dev):
+    """Causal segment-masked GQA attention (softmax_attention) forward and backward on
+    [batch, seq, kv_heads * group, head_dim] bf16, default positions.  Algorithmic TF/s counts the
+    causal half of each product, 2 b hi n^2 d / 2 FLOP: two in the forward (Q K^T, P V; the fused
+    path runs the score product twice, counted once) and four in the backward (dP, dQ, dK, dV)."""
+    from .attention import softmax_attention
+    b, n, H, I, dh = args.batch, args.seq, args.kv_heads, args.group, args.head_dim
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(8)
+    mk = lambda shape: torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)  # noqa: E731
+    q = mk((b, n, H * I, dh)).requires_grad_(True)
+    k = mk((b, n, H, dh)).requires_grad_(True)
+    v = mk((b, n, H, dh)).requires_grad_(True)
+    do = mk((b, n, H * I, dh))
+    seg = torch.zeros((b, n), dtype=torch.int32, device=dev)
+    box = {}
+
+    def fwd():
+        box["o"] = softmax_attention(q, k, v, None, seg, None, seg, scale=dh ** -0.5)
+
+    def bwd():
+        q.grad = k.grad = v.grad = None
+        box["o"].backward(do, retain_graph=True)
+
+    fwd()
+    us_f = _time_us(fwd, args.reps, args.warmup)
+    us_b = _time_us(bwd, args.reps, args.warmup)
+    fl = 2.0 * b * H * I * n * n * dh / 2  # one causal product
+    print(json.dumps({"batch": b, "seq": n, "q_heads": H * I, "kv_heads": H, "head_dim": dh, "fwd_us": us_f,
+                      "bwd_us": us_b, "fwd_tflops": 2 * fl / us_f / 1e6, "bwd_tflops": 4 * fl / us_b / 1e6}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=16384)
@@ -272,6 +306,12 @@ def main():
     ap.add_argument("--vocab", type=int, default=128256)
     ap.add_argument("--ns", action="store_true", help="time Newton-Schulz on [batch, d, hidden] instead")
     ap.add_argument("--batch", type=int, default=2)
+    ap.add_argument("--attn", action="store_true",
+                    help="time the causal attention fwd / bwd on [batch, seq, kv_heads x group, head_dim] instead")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--kv-heads", type=int, default=8)
+    ap.add_argument("--group", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=128)
     ap.add_argument("--rs-push", action="store_true",
                     help="time the TP-2/4/8 F2 and B4 GEMMs storing locally vs pushing rows to a peer GPU")
     args = ap.parse_args()
@@ -288,6 +328,8 @@ def main():
         return xent_bench(args, dev)
     if args.ns:
         return ns_bench(args, dev)
+    if args.attn:
+        return attn_bench(args, dev)
     if args.rs_push:
         return rs_push_bench(args, dev)
     g = build(args.tokens, args.d, args.hidden, dev)

@@ -43,16 +43,18 @@ from .einsum import Einsum, Rngs, lecun_normal_init, zeros_init
 # ~225 KiB of shared memory each) needs, so the GEMM starts only when the push ends.
 AG_ENGINE = C.AG_COPY_ENGINE
 
-# Streams over which the copy-engine pushes spread their per-peer copies (ufp8_tp_set_copy_lanes):
-# one copy engine moves a block at well under the link rate, so several run at once.
-COPY_LANES = 2
+# Streams over which the copy-engine pushes spread their per-peer copies (ufp8_tp_set_copy_lanes).
+# Measured at TP 4 (GMLP, 16384 tokens, d 4096, h 14336): 2 lanes 2.27 ms/step and 3 lanes 3.14
+# against 2.21 with 1 (copy engines running at once slow each other down), so 1 is the default.
+COPY_LANES = 1
 
 # How each reduce-scatter's partial rows reach their owners: "epilogue" (the GEMM epilogue
 # stores them into the peers' slots, UFP8_EPI_RS_PUSH), "copy" (the GEMM stores locally and
 # copy engines push the blocks, ufp8_tp_rs_push_copy, while independent work runs), or "auto":
 # the epilogue push for y (nothing in the forward can run beside it) and copy engines for dx
-# (dWf = x^T dUG runs while the blocks travel).
-RS_ENGINE = "auto"
+# (dWf = x^T dUG runs while the blocks travel).  "auto" wins at TP 2 (4.00 vs 4.08 ms/step) and
+# loses badly at TP 4 (3.94 vs 2.21), so the epilogue push is the default.
+RS_ENGINE = "epilogue"
 
 
 def tensor_group(mesh):
@@ -298,9 +300,10 @@ class TPContext:
 
     def reduce_scatter_rows(self, partial: torch.Tensor) -> torch.Tensor:
         """[k * rows, ...] partial sums on every rank -> this rank's summed block [rows, ...]:
-        with the NVLink path bf16 blocks go by copy engines into the peers' staging slots and the
-        finish kernel sums them in fp32 in rank order; otherwise NCCL / gloo."""
-        if self.fused_rs and partial.dtype == torch.bfloat16 and partial.is_cuda:
+        with the NVLink path on 2 ranks the bf16 blocks go by copy engines into the peer's staging
+        slot and the finish kernel sums them in fp32 in rank order (copy-engine pushes to several
+        peers at once were measured slower than NCCL's); otherwise NCCL / gloo."""
+        if self.fused_rs and self.world == 2 and partial.dtype == torch.bfloat16 and partial.is_cuda:
             lead, rest = partial.shape[0], tuple(partial.shape[1:])
             flat = partial.reshape(lead, -1).contiguous()
             if flat.shape[1] % 2 == 0:

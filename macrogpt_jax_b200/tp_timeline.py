@@ -24,8 +24,8 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tp-rs", choices=["p2p", "nccl"], default="p2p")
     ap.add_argument("--tp-ag", choices=["ce", "sm"], default="ce")
-    ap.add_argument("--tp-lanes", type=int, default=2)
-    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="auto")
+    ap.add_argument("--tp-lanes", type=int, default=1)
+    ap.add_argument("--tp-rs-engine", choices=["auto", "epilogue", "copy"], default="epilogue")
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--d", type=int, default=4096)
     ap.add_argument("--hidden", type=int, default=14336)
