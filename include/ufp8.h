@@ -235,10 +235,11 @@ typedef struct ufp8_gemm_desc {
   /* UFP8_EPI_ATTN_*: batch entry g, row r (query), column c (key) of the score matrix
    * scale * (A_g B_g^T)[r, c] is visible iff c <= r and both carry the same non-negative segment
    * id (attn_q_segment_ids[r], attn_kv_segment_ids[c]; NULL: all 0).
-   *   STATS: (m, s) = (max, sum exp(x - m)) of the visible x of each group j of 128 columns as two
-   *          f32 at attn_stats + 2 * ((g * M + r) * attn_ld_stats + j) (m = -inf, s = 0 when none
-   *          is visible); D is not written (may be NULL).
-   *   P:     D = bf16(exp(x - attn_row[g * M + r])) where visible, else 0 (attn_row = lse).
+   *   STATS: in base 2, y = x * log2(e): (m, s) = (max y, sum 2^(y - m)) of the visible y of each
+   *          group j of 128 columns as two f32 at attn_stats + 2 * ((g * M + r) * attn_ld_stats + j)
+   *          (m = -inf, s = 0 when none is visible); D is not written (may be NULL).
+   *   P:     D = bf16(2^(x * log2(e) - attn_row[g * M + r] * log2(e))) where visible, else 0
+   *          (attn_row = lse, natural log).
    *   DS:    D = bf16(scale * (P * (acc - attn_row[g * M + r]))), each step rounded in f32, with
    *          P the bf16 matrix `c` (pitch ldc, slice pitch c_batch_stride; attn_row = rowsum(dO O)).
    * With UFP8_TILES_LOWER the tiles past the diagonal are not computed (not written). */

@@ -253,8 +253,8 @@ __global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftA
   }
 }
 
-// Default positions: the lse of each score row from the UFP8_EPI_ATTN_STATS partials (one
-// (max, sum exp) per 128 columns), over the groups up to the end of the row's 256-wide diagonal
+// Default positions: the lse of each score row (natural log) from the UFP8_EPI_ATTN_STATS partials
+// (one base-2 (max, sum 2^(y - max)) per 128 columns), over the groups up to the end of the row's 256-wide diagonal
 // tile (the products skip the tiles past it).  One thread per row (row = g * n + q).
 __global__ void __launch_bounds__(kAThreads) attn_lse_kernel(const float2* __restrict__ stats, int64_t rows,
                                                              int64_t n, int64_t ld, float* __restrict__ lse) {
@@ -273,9 +273,9 @@ __global__ void __launch_bounds__(kAThreads) attn_lse_kernel(const float2* __res
   float S = 0.0f;
   for (int64_t j = 0; j < groups; ++j) {
     const float2 v = st[j];
-    if (v.y > 0.0f) S += v.y * __expf(v.x - M);
+    if (v.y > 0.0f) S += v.y * exp2f(v.x - M);
   }
-  lse[row] = __fadd_rn(M, logf(S));
+  lse[row] = (M + log2f(S)) * 0.6931471805599453f;  // partials in base 2 -> natural log
 }
 
 // rowsum(dO * O) of every (query head g, query q) row of one batch element (O, dO [n][hi][d]):

@@ -665,6 +665,13 @@ __device__ __forceinline__ void load_bf16x16_packed(const __nv_bfloat16* p, uint
 // row's segment id, rv = its attn_row value.  Column c is visible iff c <= row and its segment id
 // equals sq >= 0.  STATS folds the visible x = scale * acc into the running (m, s) of this
 // thread's 128 columns; P and DS store 32 bf16 values at d.
+__device__ __forceinline__ float attn_ex2(float x) {  // 2^x, the MUFU instruction
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kAttnLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ uint32_t attn_vis(const GemmArgs& a, int row, int col0, int valid, int sq, bool uni,
                                              uint32_t segmask) {
   uint32_t vis = 0;
@@ -694,32 +701,44 @@ __device__ __forceinline__ uint32_t attn_vis(const GemmArgs& a, int row, int col
   return vis;
 }
 
-// STATS over 64 columns (two 32-column chunks r0, r1 from col0): the visible x = scale * acc
-// fold into the running (m, s) of this thread's 128 columns with one rescale.
+// STATS over 64 columns (two 32-column chunks r0, r1 from col0), base 2: the visible
+// y = acc * scale * log2(e) fold into the running (m, s) = (max y, sum 2^(y - m)) of this
+// thread's 128 columns with one rescale.
 __device__ __forceinline__ void attn_stats64(const GemmArgs& a, uint32_t (&r0)[32], uint32_t (&r1)[32], int row,
                                              int col0, int valid, int sq, bool uni, uint32_t sm0, uint32_t sm1,
                                              float& m, float& s) {
   const uint32_t v0 = attn_vis(a, row, col0, valid, sq, uni, sm0);
   const uint32_t v1 = valid > 32 ? attn_vis(a, row, col0 + 32, valid - 32, sq, uni, sm1) : 0u;
   if ((v0 | v1) == 0u) return;
+  const float c = a.attn_scale * kAttnLog2e;
   float cm2[2] = {-INFINITY, -INFINITY};  // independent partial maxima / sums (short chains)
+  if ((v0 & v1) == 0xFFFFFFFFu) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float x0 = ((v0 >> j) & 1u) ? __fmul_rn(__uint_as_float(r0[j]), a.attn_scale) : -INFINITY;
-    const float x1 = ((v1 >> j) & 1u) ? __fmul_rn(__uint_as_float(r1[j]), a.attn_scale) : -INFINITY;
-    r0[j] = __float_as_uint(x0);
-    r1[j] = __float_as_uint(x1);
-    cm2[j & 1] = fmaxf(cm2[j & 1], fmaxf(x0, x1));
+    for (int j = 0; j < 32; ++j) {
+      const float y0 = __uint_as_float(r0[j]) * c, y1 = __uint_as_float(r1[j]) * c;
+      r0[j] = __float_as_uint(y0);
+      r1[j] = __float_as_uint(y1);
+      cm2[j & 1] = fmaxf(cm2[j & 1], fmaxf(y0, y1));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float y0 = ((v0 >> j) & 1u) ? __uint_as_float(r0[j]) * c : -INFINITY;
+      const float y1 = ((v1 >> j) & 1u) ? __uint_as_float(r1[j]) * c : -INFINITY;
+      r0[j] = __float_as_uint(y0);
+      r1[j] = __float_as_uint(y1);
+      cm2[j & 1] = fmaxf(cm2[j & 1], fmaxf(y0, y1));
+    }
   }
   const float cm = fmaxf(cm2[0], cm2[1]);
   if (cm > m) {
-    s = s * __expf(m - cm);  // m = -inf on the first visible chunk: s = 0 * 0
+    s = s * attn_ex2(m - cm);  // m = -inf on the first visible chunk: s = 0 * 0
     m = cm;
   }
   float acc2[2] = {0.0f, 0.0f};
 #pragma unroll
-  for (int j = 0; j < 32; ++j)  // masked: exp(-inf) = 0
-    acc2[j & 1] += __expf(__fsub_rn(__uint_as_float(r0[j]), m)) + __expf(__fsub_rn(__uint_as_float(r1[j]), m));
+  for (int j = 0; j < 32; ++j)  // masked: 2^-inf = 0
+    acc2[j & 1] += attn_ex2(__uint_as_float(r0[j]) - m) + attn_ex2(__uint_as_float(r1[j]) - m);
   s += acc2[0] + acc2[1];
 }
 
@@ -729,19 +748,18 @@ __device__ __forceinline__ void attn_chunk(const GemmArgs& a, const uint32_t (&r
                                            bool uni, uint32_t segmask) {
   const uint32_t vis = a.mode == UFP8_EPI_ATTN_P ? attn_vis(a, row, col0, valid, sq, uni, segmask) : 0u;
   uint32_t o[16];
-  if (a.mode == UFP8_EPI_ATTN_P) {
+  if (a.mode == UFP8_EPI_ATTN_P) {  // P = 2^(acc * scale * log2(e) - lse * log2(e)); rv = -lse * log2(e)
+    const float c = a.attn_scale * kAttnLog2e;
     if (vis == 0xFFFFFFFFu) {
 #pragma unroll
       for (int j = 0; j < 16; ++j)
-        o[j] = pack_bf16x2(__expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j]), a.attn_scale), rv)),
-                           __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j + 1]), a.attn_scale), rv)));
+        o[j] = pack_bf16x2(attn_ex2(__fmaf_rn(__uint_as_float(r[2 * j]), c, rv)),
+                           attn_ex2(__fmaf_rn(__uint_as_float(r[2 * j + 1]), c, rv)));
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const float p0 = ((vis >> (2 * j)) & 1u)
-                             ? __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j]), a.attn_scale), rv)) : 0.0f;
-        const float p1 = ((vis >> (2 * j + 1)) & 1u)
-                             ? __expf(__fsub_rn(__fmul_rn(__uint_as_float(r[2 * j + 1]), a.attn_scale), rv)) : 0.0f;
+        const float p0 = ((vis >> (2 * j)) & 1u) ? attn_ex2(__fmaf_rn(__uint_as_float(r[2 * j]), c, rv)) : 0.0f;
+        const float p1 = ((vis >> (2 * j + 1)) & 1u) ? attn_ex2(__fmaf_rn(__uint_as_float(r[2 * j + 1]), c, rv)) : 0.0f;
         o[j] = pack_bf16x2(p0, p1);
       }
     }
@@ -1036,6 +1054,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPThreads, 1)
         if (args.mode >= UFP8_EPI_ATTN_STATS && row_ < args.M) {
           pf_sq = args.attn_qseg ? args.attn_qseg[row_] : 0;
           if (args.attn_row) pf_rv = args.attn_row[static_cast<long long>(g_) * args.M + row_];
+          if (args.mode == UFP8_EPI_ATTN_P) pf_rv = -pf_rv * kAttnLog2e;  // the exponent's offset, base 2
           const int c0 = nb_ * kBN + chalf * 128;
           if (args.attn_p != nullptr && c0 < args.N) {  // DS: this row's 128 P values into L2
             const __nv_bfloat16* pp = args.attn_p + g_ * args.c_bstride + static_cast<long long>(row_) * args.ldc + c0;
