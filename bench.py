@@ -936,7 +936,9 @@ def run_muon(args, cfg, rank, world, local_rank, dev):
 
 
 def run_layer(args, cfg, rank, world, local_rank, dev):
-    """TransformerLayer(x, query_segment_ids=...) forward and the backward of its summed output."""
+    """TransformerLayer(x, query_segment_ids=...) forward and the backward of its summed output; on
+    N > 1 GPUs TransformerLayer(..., mesh=group): kv heads and GMLP hidden split, each rank holding
+    B / N whole sequences."""
     import numpy as np
     import torch
     from macrogpt_jax_b200 import _capi, ops
@@ -944,19 +946,37 @@ def run_layer(args, cfg, rank, world, local_rank, dev):
     from macrogpt_jax_b200.layer import TransformerLayer
     from macrogpt_jax_b200.mlp import GMLP
     from macrogpt_jax_b200.soft_attn import SoftmaxAttention
-    if world > 1:
-        raise SystemExit("the transformer-layer workload runs on one GPU")
     d, h, H, I, Dh, B, S = (cfg[k] for k in ("d", "h", "kv_heads", "group", "head_d", "B", "S"))
+    if world > 1 and (B % world or H % world or h % world):
+        raise SystemExit(f"the tensor-parallel layer needs batch {B}, kv heads {H} and hidden {h} divisible by {world}")
     T = B * S
     init = Einsum.override(initializer=scaled_normal_init(d ** -0.5))
     attn = SoftmaxAttention.override(kq_d=Dh, kv_heads=H, kv_q_ratio=I, q=init, k=init, v=init, o=init)
     mlp = GMLP.override(hidden_d=h, fused_proj=init, down_proj=Einsum.override(initializer=scaled_normal_init(h ** -0.5)))
-    layer = TransformerLayer(d, attn=attn, mlp=mlp, rngs=Rngs(0))
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    layer = TransformerLayer(d, attn=attn, mlp=mlp, rngs=Rngs(0), mesh=group)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234)
     x = torch.randn((B, S, d), generator=gen, device=dev).to(torch.bfloat16)
     dy = (torch.randn((B, S, d), generator=gen, device=dev) * 1e-3).to(torch.bfloat16)
     seg = torch.zeros((B, S), dtype=torch.int32, device=dev)
+    if world > 1:  # this rank's whole sequences; segment ids stay full-batch
+        bl = B // world
+        x, dy = x[rank * bl:(rank + 1) * bl].contiguous(), dy[rank * bl:(rank + 1) * bl].contiguous()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
     params = list(layer.parameters())
 
     def fwd_bwd(xb, dyb):
@@ -972,10 +992,13 @@ def run_layer(args, cfg, rank, world, local_rank, dev):
     for _ in range(args.warmup):
         fwd_bwd(x, dy)
     torch.cuda.synchronize()
+    barrier()
     timer = ops.KernelTimer()
     clocks = ClockSampler(local_rank)
     clocks.start()
     launches0 = _capi.launches
+    torch.cuda.synchronize()
+    barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ops.set_timer(timer)
     ev0.record()
@@ -984,9 +1007,10 @@ def run_layer(args, cfg, rank, world, local_rank, dev):
     ev1.record()
     ops.set_timer(None)
     torch.cuda.synchronize()
+    barrier()
     launches = _capi.launches - launches0
     clk = clocks.stop()
-    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
     summ = timer.summary()
     peaks, peak_src = load_peaks()
     fl, proj_fl, attn_fl = layer_flops(cfg, T, S, B)
@@ -995,12 +1019,16 @@ def run_layer(args, cfg, rank, world, local_rank, dev):
     achieved = (g_fl / g_n) / (g_ms / g_n / 1000.0) / 1e12 if g_n else None
     out = {
         "metric": "FP8 Llama-3-8B transformer layer fwd+bwd tokens/s (TFLOP/s/GPU)",
-        "value": T * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "value": T * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp8", "data": "synthetic (seeded)",
         "config": {"workload": args.config_desc, "tokens": T, "d_model": d, "hidden": h, "q_heads": H * I,
-                   "kv_heads": H, "head_dim": Dh, "parallelism": "single GPU", "l2": "inputs larger than L2"},
-        "tflops_per_gpu": fl * args.steps / (ms / 1000.0) / 1e12,
+                   "kv_heads": H, "head_dim": Dh,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"tp{world} (kv heads of q/k/v/o and GMLP hidden split; token all-gather / reduce-scatter, "
+                   f"B/{world} sequences per rank)",
+                   "l2": "inputs larger than L2"},
+        "tflops_per_gpu": fl * args.steps / (ms / 1000.0) / 1e12 / world,
         "flops_per_step": {"total": fl, "projections": proj_fl, "attention_causal": attn_fl,
                            "gmlp": 18.0 * T * d * h},
         "roofline": {"kernel": "gemm_fp8_pair_kernel (FP8 projections and GMLP)", "bound": "tensor",
@@ -1013,12 +1041,15 @@ def run_layer(args, cfg, rank, world, local_rank, dev):
         "time_share": {k: round(v[1] / ms, 4) for k, v in summ.items()},
     }
     if not args.no_e2e:
-        ems = e2e_pipelined(fwd_bwd, x, dy, args.steps, lambda: None)
+        barrier()
+        ems = max_over_ranks(e2e_pipelined(fwd_bwd, x, dy, args.steps, barrier))
         out["e2e"] = {"value": T * args.steps / (ems / 1000.0), "unit": "tokens/s", "ms_per_step": ems / args.steps,
                       "h2d_bytes_per_step": 2 * x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
                       "path": "TransformerLayer forward + backward; x and dY in from pinned host memory each step "
                               "(side stream, double-buffered), y back (side stream, overlapping the backward)"}
-    if not args.no_cpu_baseline:
+    if rank != 0:
+        return None
+    if not args.no_cpu_baseline and world == 1:
         # The oracle's GMLP (hidden slice, full tokens) and attention (one kv-head group of one sequence)
         # timed and scaled by FLOPs; the projections at the GMLP port's FLOP rate.
         from oracle import attention as oa
