@@ -905,6 +905,8 @@ def run_muon(args, cfg, rank, world, local_rank, dev):
                    "parallelism": "single GPU", "l2": "inputs larger than L2"},
         "roofline": {"kernel": "ufp8_newton_schulz (bf16 gemm_fp8_pair_kernel + normalisation)", "bound": "tensor",
                      "achieved": achieved, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "flops": "executed: the symmetric X X^T and A A products run only their lower 256-tile "
+                              "triangle (the value above counts the algorithmic 4 s^2 l + 2 s^3 per step)",
                      "frac": (achieved / peaks["bf16_tflops_sustained"]) if achieved else None,
                      "peak_source": f"bf16_tflops_sustained (cuBLAS bf16 under the power cap), {peak_src}",
                      "launches": n_n, "time_share": n_ms / ms if ms else None, "traffic": None},

@@ -11,7 +11,11 @@
 //              MN-major operand);
 //     m >  n:  A = X^T X (both MN-major);          B as above;         X' = (X B) + a X (B taken
 //              as B^T: it is symmetric).
-// No transposed copy of X is made.  X, A and B are kept in bf16 between the GEMMs; the last step
+// A and B are symmetric, and bitwise so (element (i, j) sums the same products in the same order
+// as (j, i)): their GEMMs compute only the 256 x 256 tiles on or below the diagonal
+// (UFP8_TILES_LOWER) and a transpose-copy kernel fills the rest, a quarter fewer FLOPs per step
+// (3 s^2 l + s^3 instead of 4 s^2 l + 2 s^3 for the short side s and long side l) with the same
+// bits.  No transposed copy of X is made.  X, A and B are kept in bf16 between the GEMMs; the last step
 // writes the result straight in the output's type (f32 or bf16).  The normalisation is two
 // passes: per-slice partial sums of squares (fixed order), then x / (sqrt(sum) + eps) rounded to
 // bf16.
@@ -79,6 +83,26 @@ __global__ void __launch_bounds__(kNsThreads) ns_scale_kernel(const NsNormArgs a
 }
 
 int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+
+// Fills the tiles UFP8_TILES_LOWER skipped in each [s, s] slice: element (i, j) with
+// j / 256 > i / 256 becomes (j, i).  One CTA per 32 x 32 block of the upper part, through shared
+// memory (coalesced reads of the source rows, coalesced writes of the destination rows).
+__global__ void __launch_bounds__(kNsThreads) ns_mirror_kernel(__nv_bfloat16* m, int64_t s, int64_t ss) {
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
+  if ((c0 >> 8) <= (r0 >> 8)) return;  // computed by the GEMM (also the whole diagonal tile)
+  __shared__ __nv_bfloat16 t[32][33];
+  __nv_bfloat16* base = m + static_cast<int64_t>(blockIdx.z) * ss;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  for (int k = ty; k < 32; k += 8) {  // source rows c0 + k, columns r0 + tx
+    const int64_t i = c0 + k, j = r0 + tx;
+    if (i < s && j < s) t[k][tx] = base[i * s + j];
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {  // destination rows r0 + k, columns c0 + tx
+    const int64_t i = r0 + k, j = c0 + tx;
+    if (i < s && j < s) base[i * s + j] = t[tx][k];
+  }
+}
 
 struct NsLayout {
   int64_t x0, x1, A, B, parts, total;
@@ -172,6 +196,14 @@ extern "C" int ufp8_newton_schulz(const void* g, int g_dtype, int64_t batch, int
   const bool tr = m > n;            // work on X^T
   const int64_t sd = tr ? n : m;    // short side
   const int64_t mn = m * n, ss = sd * sd;
+  const dim3 mgrid(static_cast<unsigned>((sd + 31) / 32), static_cast<unsigned>((sd + 31) / 32),
+                   static_cast<unsigned>(batch));
+  auto mirror = [&](__nv_bfloat16* mat) -> int {
+    if (sd <= 256) return UFP8_OK;  // one diagonal tile: nothing skipped
+    ns_mirror_kernel<<<mgrid, kNsThreads, 0, s>>>(mat, sd, ss);
+    const cudaError_t me = cudaGetLastError();
+    return me == cudaSuccess ? UFP8_OK : cuda_error(me, "newton-schulz mirror launch");
+  };
   for (int it = 0; it < steps; ++it) {
     const float ca = coeffs[3 * it], cb = coeffs[3 * it + 1], cc = coeffs[3 * it + 2];
     const __nv_bfloat16* Xc = X[it & 1];
@@ -191,7 +223,9 @@ extern "C" int ufp8_newton_schulz(const void* g, int g_dtype, int64_t batch, int
     d.epilogue = UFP8_EPI_STORE;
     d.ldd = sd;
     d.d_batch_stride = ss;
+    d.tile_mask = UFP8_TILES_LOWER;
     if (int rc = launch_gemm(d, s, *dev, 0, UFP8_GEMM_AUTO, 0)) return rc;
+    if (int rc = mirror(A)) return rc;
     // B = c (A A) + b A   (A symmetric: its transpose is itself, a K-major B operand)
     d = ufp8_gemm_desc{};
     d.M = sd;
@@ -211,7 +245,9 @@ extern "C" int ufp8_newton_schulz(const void* g, int g_dtype, int64_t batch, int
     d.c_batch_stride = ss;
     d.alpha = cc;
     d.beta = cb;
+    d.tile_mask = UFP8_TILES_LOWER;
     if (int rc = launch_gemm(d, s, *dev, 0, UFP8_GEMM_AUTO, 0)) return rc;
+    if (int rc = mirror(B)) return rc;
     // X' = (B X) + a X  (m <= n)   or   X' = (X B) + a X  (m > n)
     d = ufp8_gemm_desc{};
     d.M = m;

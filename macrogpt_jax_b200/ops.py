@@ -528,7 +528,11 @@ def newton_schulz(g: torch.Tensor, coeffs, eps: float = 1e-8, out_dtype: torch.d
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=g.device)
     dt = {torch.float32: C.OUT_F32, torch.bfloat16: C.OUT_BF16}
     s, l = min(m, n), max(m, n)
-    flops = float(batch) * len(coeffs) * (4.0 * s * s * l + 2.0 * s ** 3)
+    # FLOPs executed: the symmetric X X^T and A A products compute only the tiles on or below
+    # the diagonal (a 256-tile triangle), the update B X all of its product
+    tiles = -(-s // 256)
+    tri = (tiles * (tiles + 1) / 2) / (tiles * tiles)
+    flops = float(batch) * len(coeffs) * (2.0 * s * s * l * (1.0 + tri) + 2.0 * s ** 3 * tri)
     _launch("newton_schulz", flops, lambda: C.newton_schulz(
         g.data_ptr(), dt[g.dtype], batch, m, n, coeffs, eps, out.data_ptr(), dt[out_dtype], ws.data_ptr(), nbytes,
         _stream()))

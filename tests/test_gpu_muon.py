@@ -87,7 +87,7 @@ def test_bf16_gemm_rejects_mixed_and_fp8_epilogues(cuda):
                  epilogue=C.EPI_SWIGLU, h=d, ldh=64, amax_out=torch.empty(1, device=cuda))
 
 
-@pytest.mark.parametrize("shape", [(1, 256, 512), (1, 512, 256), (3, 384, 384), (2, 128, 1024)])
+@pytest.mark.parametrize("shape", [(1, 256, 512), (1, 512, 256), (3, 384, 384), (2, 128, 1024), (1, 1200, 600)])
 @pytest.mark.parametrize("method", ["muon", "optimal"])
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_orthogonalize_against_oracle(cuda, shape, method, dtype):
