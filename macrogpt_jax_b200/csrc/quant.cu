@@ -165,11 +165,25 @@ __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __rest
   const uint32_t bound2 = bound < 0 ? 0u : (static_cast<uint32_t>(bound) * 0x00010001u);
   const int64_t n_vec32 = n_vec16 / 2;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n_vec32; i += stride) {
-    const uint4 a0 = ld_stream(x + 4 * i);
-    const uint4 b0 = ld_stream(x + 4 * i + 1);
-    const uint4 a1 = ld_stream(x + 4 * i + 2);
-    const uint4 b1 = ld_stream(x + 4 * i + 3);
+  // Software-pipelined: the next step's four 16-byte loads leave before this step's 32 values
+  // are converted and stored, so each thread keeps loads in flight through its compute.
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  uint4 a0, b0, a1, b1;
+  if (i < n_vec32) {
+    a0 = ld_stream(x + 4 * i);
+    b0 = ld_stream(x + 4 * i + 1);
+    a1 = ld_stream(x + 4 * i + 2);
+    b1 = ld_stream(x + 4 * i + 3);
+  }
+  for (; i < n_vec32; i += stride) {
+    const int64_t nx = i + stride;
+    uint4 c0 = make_uint4(0u, 0u, 0u, 0u), d0 = c0, c1 = c0, d1 = c0;
+    if (nx < n_vec32) {
+      c0 = ld_stream(x + 4 * nx);
+      d0 = ld_stream(x + 4 * nx + 1);
+      c1 = ld_stream(x + 4 * nx + 2);
+      d1 = ld_stream(x + 4 * nx + 3);
+    }
     const uint32_t m = absmax16(absmax16(absmax16(absmax16(0u, a0), b0), a1), b1);
     // both 16-bit lanes of m at or below the bound: no special product in these 32
     if (bound >= 0 && __vcmpleu2(m, bound2) == 0xFFFFFFFFu) {
@@ -179,6 +193,10 @@ __global__ void __launch_bounds__(kThreads) quant_vec_kernel(const uint4* __rest
       q[2 * i] = quant16(a0, b0, s, fmt);
       q[2 * i + 1] = quant16(a1, b1, s, fmt);
     }
+    a0 = c0;
+    b0 = d0;
+    a1 = c1;
+    b1 = d1;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0 && (n_vec16 & 1)) {
     const int64_t j = n_vec16 - 1;
