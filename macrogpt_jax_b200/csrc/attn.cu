@@ -254,28 +254,42 @@ __global__ void __launch_bounds__(kAThreads) attn_softmax_bwd_kernel(const SoftA
 }
 
 // Default positions: the lse of each score row (natural log) from the UFP8_EPI_ATTN_STATS partials
-// (one base-2 (max, sum 2^(y - max)) per 128 columns), over the groups up to the end of the row's 256-wide diagonal
-// tile (the products skip the tiles past it).  One thread per row (row = g * n + q).
+// (one base-2 (max, sum 2^(y - max)) per 128 columns), over the groups up to the end of the row's
+// 256-wide diagonal tile (the products skip the tiles past it).  One warp per row (row = g * n + q):
+// lane j merges groups j, j + 32, ... (coalesced reads) online, then a fixed xor butterfly merges
+// the lanes' (max, sum) pairs.
 __global__ void __launch_bounds__(kAThreads) attn_lse_kernel(const float2* __restrict__ stats, int64_t rows,
                                                              int64_t n, int64_t ld, float* __restrict__ lse) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x;
-  if (row >= rows) return;
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * kAThreads + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // whole warps
   const int64_t q = row % n;
   const int64_t diag = (q / 256 + 1) * 2;
   const int64_t groups = diag < ld ? diag : ld;
   const float2* st = stats + row * ld;
-  float M = -INFINITY;
-  for (int64_t j = 0; j < groups; ++j) M = fmaxf(M, st[j].x);
-  if (M == -INFINITY) {
-    lse[row] = -INFINITY;
+  float M = -INFINITY, S = 0.0f;  // this lane's (max, sum 2^(y - max)), merged online
+  for (int64_t j = lane; j < groups; j += 32) {
+    const float2 v = st[j];
+    if (v.y > 0.0f) {
+      if (v.x > M) {
+        S = S * exp2f(M - v.x);  // M = -inf at first: 0 * 0
+        M = v.x;
+      }
+      S += v.y * exp2f(v.x - M);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {  // fixed butterfly over (M, S) pairs
+    const float Mo = __shfl_xor_sync(0xFFFFFFFFu, M, o), So = __shfl_xor_sync(0xFFFFFFFFu, S, o);
+    const float Mn = fmaxf(M, Mo);
+    S = (S > 0.0f ? S * exp2f(M - Mn) : 0.0f) + (So > 0.0f ? So * exp2f(Mo - Mn) : 0.0f);
+    M = Mn;
+  }
+  if (!(S > 0.0f)) {
+    if (lane == 0) lse[row] = -INFINITY;
     return;
   }
-  float S = 0.0f;
-  for (int64_t j = 0; j < groups; ++j) {
-    const float2 v = st[j];
-    if (v.y > 0.0f) S += v.y * exp2f(v.x - M);
-  }
-  lse[row] = (M + log2f(S)) * 0.6931471805599453f;  // partials in base 2 -> natural log
+  if (lane == 0) lse[row] = (M + log2f(S)) * 0.6931471805599453f;  // partials in base 2 -> natural log
 }
 
 // rowsum(dO * O) of every (query head g, query q) row of one batch element (O, dO [n][hi][d]):
@@ -494,7 +508,7 @@ extern "C" int ufp8_attention_forward(const ufp8_attn_desc* d, const void* q, co
                          L.ld_stats, nullptr, nullptr, d->scale, s, *dev);
       if (rc) return rc;
       const int64_t rows = hi * n;
-      attn_lse_kernel<<<static_cast<unsigned>((rows + kAThreads - 1) / kAThreads), kAThreads, 0, s>>>(
+      attn_lse_kernel<<<static_cast<unsigned>((rows * 32 + kAThreads - 1) / kAThreads), kAThreads, 0, s>>>(
           reinterpret_cast<const float2*>(stats), rows, n, L.ld_stats, lse0 + b * hi * n);
       cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_error(e, "attention lse launch");
