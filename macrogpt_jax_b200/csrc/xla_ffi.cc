@@ -141,6 +141,47 @@ ffi::Error RmsnormQuantImpl(cudaStream_t s, ffi::AnyBuffer x, ffi::AnyBuffer sca
                                    nullptr, 0, st(s)));
 }
 
+// Causal segment-masked GQA softmax attention (the flash_attention call of
+// ueaj/model/soft_attn.py:186-196) with the default positions 0..n-1: q bf16 [b, n, h * i, d],
+// k / v bf16 [b, n, h, d], segment ids s32 [b, n] (queries and keys alike) -> out bf16 like q,
+// `saved` (P and lse, kept for the backward) and the scratch `workspace`; both byte sizes come from
+// ufp8_attention_workspace for the same shape.
+ufp8_attn_desc attn_desc(int64_t batch, int64_t seq, int64_t kv_heads, int64_t group, int64_t head_dim,
+                         const int32_t* seg, float scale) {
+  ufp8_attn_desc d = {};
+  d.batch = batch;
+  d.seq = seq;
+  d.kv_heads = kv_heads;
+  d.group = group;
+  d.head_dim = head_dim;
+  d.q_segment_ids = seg;
+  d.kv_segment_ids = seg;
+  d.scale = scale;
+  return d;
+}
+
+ffi::Error AttentionForwardImpl(cudaStream_t s, ffi::AnyBuffer q, ffi::AnyBuffer k, ffi::AnyBuffer v,
+                                ffi::Buffer<ffi::S32> seg, ffi::Result<ffi::AnyBuffer> out,
+                                ffi::Result<ffi::AnyBuffer> saved, ffi::Result<ffi::AnyBuffer> workspace,
+                                int64_t batch, int64_t seq, int64_t kv_heads, int64_t group, int64_t head_dim,
+                                float scale) {
+  const ufp8_attn_desc d = attn_desc(batch, seq, kv_heads, group, head_dim, seg.typed_data(), scale);
+  return status(ufp8_attention_forward(&d, q.untyped_data(), k.untyped_data(), v.untyped_data(), out->untyped_data(),
+                                       saved->untyped_data(), workspace->untyped_data(), st(s)));
+}
+
+// Its backward: dq, dk, dv (bf16, shaped like q, k, v) from dout at out and the forward's `saved`.
+ffi::Error AttentionBackwardImpl(cudaStream_t s, ffi::AnyBuffer q, ffi::AnyBuffer k, ffi::AnyBuffer v,
+                                 ffi::Buffer<ffi::S32> seg, ffi::AnyBuffer out, ffi::AnyBuffer dout,
+                                 ffi::AnyBuffer saved, ffi::Result<ffi::AnyBuffer> dq, ffi::Result<ffi::AnyBuffer> dk,
+                                 ffi::Result<ffi::AnyBuffer> dv, ffi::Result<ffi::AnyBuffer> workspace, int64_t batch,
+                                 int64_t seq, int64_t kv_heads, int64_t group, int64_t head_dim, float scale) {
+  const ufp8_attn_desc d = attn_desc(batch, seq, kv_heads, group, head_dim, seg.typed_data(), scale);
+  return status(ufp8_attention_backward(&d, q.untyped_data(), k.untyped_data(), v.untyped_data(), out.untyped_data(),
+                                        dout.untyped_data(), saved.untyped_data(), dq->untyped_data(),
+                                        dk->untyped_data(), dv->untyped_data(), workspace->untyped_data(), st(s)));
+}
+
 }  // namespace
 
 XLA_FFI_DEFINE_HANDLER_SYMBOL(Ufp8AmaxQuant, AmaxQuantImpl,
@@ -221,3 +262,41 @@ XLA_FFI_DEFINE_HANDLER_SYMBOL(Ufp8RmsnormQuant, RmsnormQuantImpl,
                                   .Attr<int64_t>("model_d")
                                   .Attr<int32_t>("centered")
                                   .Attr<float>("eps"));
+
+XLA_FFI_DEFINE_HANDLER_SYMBOL(Ufp8AttentionForward, AttentionForwardImpl,
+                              ffi::Ffi::Bind()
+                                  .Ctx<ffi::PlatformStream<cudaStream_t>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::S32>>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Attr<int64_t>("batch")
+                                  .Attr<int64_t>("seq")
+                                  .Attr<int64_t>("kv_heads")
+                                  .Attr<int64_t>("group")
+                                  .Attr<int64_t>("head_dim")
+                                  .Attr<float>("scale"));
+
+XLA_FFI_DEFINE_HANDLER_SYMBOL(Ufp8AttentionBackward, AttentionBackwardImpl,
+                              ffi::Ffi::Bind()
+                                  .Ctx<ffi::PlatformStream<cudaStream_t>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::Buffer<ffi::S32>>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Arg<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Ret<ffi::AnyBuffer>()
+                                  .Attr<int64_t>("batch")
+                                  .Attr<int64_t>("seq")
+                                  .Attr<int64_t>("kv_heads")
+                                  .Attr<int64_t>("group")
+                                  .Attr<int64_t>("head_dim")
+                                  .Attr<float>("scale"));

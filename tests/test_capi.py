@@ -144,8 +144,8 @@ def test_xla_ffi_shim_builds_when_jaxlib_is_present():
     from macrogpt_jax_b200 import build
     src = (build.CSRC / "xla_ffi.cc").read_text()
     handlers = sorted(re.findall(r"XLA_FFI_DEFINE_HANDLER_SYMBOL\((\w+),", src))
-    assert handlers == ["Ufp8AmaxQuant", "Ufp8AmaxQuantNoalloc", "Ufp8Gemm", "Ufp8GmlpB2", "Ufp8GmlpF1",
-                        "Ufp8RmsnormQuant"]
+    assert handlers == ["Ufp8AmaxQuant", "Ufp8AmaxQuantNoalloc", "Ufp8AttentionBackward", "Ufp8AttentionForward",
+                        "Ufp8Gemm", "Ufp8GmlpB2", "Ufp8GmlpF1", "Ufp8RmsnormQuant"]
     for entry in re.findall(r"\b(ufp8_[a-z0-9_]+)\(", src):
         assert hasattr(C.load(), entry), entry
     if build.jax_ffi_include_dir() is None:
