@@ -154,3 +154,24 @@ def test_xla_ffi_shim_builds_when_jaxlib_is_present():
     lib = ctypes.CDLL(str(build.build_xla_ffi(force=True)))
     for h in handlers:
         assert hasattr(lib, h), h
+
+
+def test_attention_workspace_sizes():
+    """With the default positions the attention keeps S and dP out of memory: the forward
+    workspace holds the per-row softmax partials (HI * n rows of ceil(n / 128) float2) and the
+    backward one rowsum(dO O) plus dS; explicit positions take the materialised S / dP (f32).
+    `saved` (P bf16 and lse of every batch element) is the same either way.  No device call."""
+    al = lambda b: (b + 255) // 256 * 256  # noqa: E731
+    b, n, H, I = 2, 520, 2, 4
+    hi, nn, ld = H * I, n * n, (n + 127) // 128
+    pos = (ctypes.c_int32 * 16)()  # any 16-byte aligned address stands for the position arrays
+    fused = C.AttnDesc(b, n, H, I, 64, None, None, None, None, 0.125, 0)
+    mat = C.AttnDesc(b, n, H, I, 64, None, None, ctypes.addressof(pos), ctypes.addressof(pos), 0.125, 0)
+    f_fwd, f_saved, f_bwd = C.attention_workspace(fused)
+    m_fwd, m_saved, m_bwd = C.attention_workspace(mat)
+    saved = al(b * hi * nn * 2) + al(b * hi * n * 4)
+    assert f_saved == m_saved == saved
+    assert f_fwd == al(hi * n * ld * 8) and m_fwd == al(hi * nn * 4)
+    assert f_bwd == al(hi * n * 4) + al(hi * nn * 2) and m_bwd == al(hi * nn * 4) + al(hi * nn * 2)
+    with pytest.raises(C.UFP8Error, match="multiple of 8"):
+        C.attention_workspace(C.AttnDesc(b, 522, H, I, 64, None, None, None, None, 0.125, 0))
