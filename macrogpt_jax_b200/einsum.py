@@ -163,9 +163,9 @@ def gemm_plan(input_expr: str, weight_expr: str, output_expr: str, batch_dims: s
 
 class _FP8EinsumFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, plan, fwd_fmt, bwd_fmt, static_scale, global_amax=None):
+    def forward(ctx, x, w, plan, fwd_fmt, bwd_fmt, static_scale, global_amax=None, qx=None):
         fn, operands = global_amax if global_amax is not None else (None, ())
-        out, saved = ops.einsum_forward(plan, x, w, fwd_fmt, static_scale, fn, operands)
+        out, saved = ops.einsum_forward(plan, x, w, fwd_fmt, static_scale, fn, operands, qx)
         ctx.plan, ctx.bwd_fmt, ctx.static_scale, ctx.saved = plan, bwd_fmt, static_scale, saved
         ctx.global_amax = (fn, operands)
         ctx.x_shape, ctx.w_shape = x.shape, w.shape
@@ -178,7 +178,7 @@ class _FP8EinsumFn(torch.autograd.Function):
                                      need_dx, need_dw, ctx.static_scale, *ctx.global_amax)
         ctx.saved = None
         return (dx.reshape(ctx.x_shape) if dx is not None else None,
-                dw.reshape(ctx.w_shape) if dw is not None else None, None, None, None, None, None)
+                dw.reshape(ctx.w_shape) if dw is not None else None, None, None, None, None, None, None)
 
 
 @config
@@ -237,12 +237,14 @@ class Einsum(torch.nn.Module):
         return gemm_plan(self.input_expr, self.weight_expr, self.output_expr, self.batch_dims, self.size_dict,
                          tuple(x_shape))
 
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, qx=None) -> torch.Tensor:
+        """`qx`: x already quantised to fwd_dtype as [tokens, reducing] (ops.quantize), shared by
+        Einsums that read the same input; gradients still flow to x."""
         w = self.w if self.w.dtype == torch.bfloat16 else self.w.to(torch.bfloat16)
         if x.dtype != torch.bfloat16:
             x = x.to(torch.bfloat16)
         return _FP8EinsumFn.apply(x, w, self.plan(x.shape), ops.FMT_OF_DTYPE[self.fwd_dtype],
-                                  ops.FMT_OF_DTYPE[self.bwd_dtype], self.static_scale, self.global_amax)
+                                  ops.FMT_OF_DTYPE[self.bwd_dtype], self.static_scale, self.global_amax, qx)
 
     def get_einsum_metadata(self) -> Dict[str, EinsumMetadata]:
         return {"w": self.metadata}

@@ -173,17 +173,22 @@ class EinsumPlan:
 
 
 def einsum_forward(plan: EinsumPlan, x: torch.Tensor, w: torch.Tensor, fwd_fmt: int,
-                   alpha: float | None = None, amax_fn=None, amax_operands=()):
+                   alpha: float | None = None, amax_fn=None, amax_operands=(), qx: Fp8Tensor | None = None):
     """Forward of ueaj.model.Einsum (ueaj/model/einsum.py:233-251) in FP8.  `amax_fn(t)` gives
     the amax of the operands named in `amax_operands` ("x", "w"): under tensor parallelism the
-    MAX over the group, so that a shard is quantised with the whole logical tensor's scale."""
+    MAX over the group, so that a shard is quantised with the whole logical tensor's scale.
+    `qx`: x already quantised ([M, K], fwd_fmt) by the caller, e.g. once for several Einsums that
+    share the input."""
     G, K, N = plan.G, plan.K, plan.N
     M = 1
     for s in plan.M_shape:
         M *= s
     x2 = x.reshape(M, K)
     w3 = w.reshape(G, K, N)
-    qx = quantize(x2, fwd_fmt, amax_fn(x2) if "x" in amax_operands else None)
+    if qx is None:
+        qx = quantize(x2, fwd_fmt, amax_fn(x2) if "x" in amax_operands else None)
+    elif qx.fmt != fwd_fmt or tuple(qx.q.shape) != (M, K):
+        raise ValueError("einsum_forward: the pre-quantised input does not match the expression")
     qw = quantize(w3, fwd_fmt, amax_fn(w3) if "w" in amax_operands else None)
     out = torch.empty((G, M, N), dtype=torch.bfloat16, device=x.device)
     inv_b = qw.inv_scale if alpha is None else qw.inv_scale * alpha

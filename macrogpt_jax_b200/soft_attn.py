@@ -37,6 +37,7 @@ import torch
 from .attention import RoPE, softmax_attention
 from .configurator import config
 from .einsum import Einsum, Rngs, zeros_init
+from .gradutils import LOW_PRECISION
 
 
 def _tensor_size(mesh, group) -> int:
@@ -117,7 +118,25 @@ class SoftmaxAttention(torch.nn.Module):
             b, n = x.shape[:2]
             q = qkv[0].reshape(b, n, self.kv_heads, 1, self.kq_d)
             return q, qkv[1], qkv[2]
+        qx = self._shared_input(x)
+        if qx is not None:  # q, k and v read one fp8 copy of x (the same bits each would make)
+            return self.q(x, qx), self.k(x, qx), self.v(x, qx)
         return self.q(x), self.k(x), self.v(x)
+
+    def _shared_input(self, x: torch.Tensor):
+        """x quantised once for the three projections when they are this package's FP8 Einsums
+        with one forward format and x's amax needs no exchange (else None: each quantises)."""
+        es = (self.q, self.k, self.v)
+        if not all(isinstance(e, Einsum) and type(e).forward is Einsum.forward for e in es) or \
+                len({e.fwd_dtype for e in es}) != 1:
+            return None
+        if any(e.global_amax is not None and "x" in e.global_amax[1] for e in es):
+            return None
+        if not x.is_cuda or x.numel() == 0 or x.dtype in LOW_PRECISION:
+            return None
+        from . import ops
+        x2 = x.to(torch.bfloat16).reshape(-1, self.model_d).contiguous()
+        return ops.quantize(x2, ops.FMT_OF_DTYPE[self.q.fwd_dtype])
 
     def project_out(self, attn: torch.Tensor) -> torch.Tensor:
         """attn [b, n, h, i, v] -> [b, n, d]."""
